@@ -1,0 +1,308 @@
+/*
+ * akili.h — C ABI of the B200 (sm_100a) backend for akili-bench's tensor-core
+ * fused-op benchmarks (the kbt_* family) and the flash-attention forward.
+ *
+ * Each benchmark keeps its reference argument block byte for byte: the
+ * structs below have the same field order, types, sizes and offsets as the
+ * `kernel_arg_t` of benchmarks/<bench>/common.h in akili-bench, so a harness
+ * that filled a `kernel_arg_t` for `vx_upload_bytes` can hand the very same
+ * bytes to `akili_<bench>()`.  The `*_addr` fields hold device addresses
+ * (CUDA device pointers cast to uint64_t) exactly as they held Vortex device
+ * addresses from `vx_mem_address`.
+ *
+ * Entry points replace the Vortex launch pair
+ *     vx_upload_bytes(arg) ; vx_start(device, kernel, args) ; vx_ready_wait(...)
+ * (e.g. benchmarks/kbt_gemm_add_relu/main.cpp:114-118) by one asynchronous
+ * call on a CUDA stream.  `grid_dim`/`block_dim` are Vortex launch hints and
+ * are ignored.
+ *
+ * Two forms per op:
+ *   akili_<bench>(arg, stream)          reference semantics: fp32 buffers,
+ *                                       operands rounded to fp16 on the
+ *                                       device (the kernels' f2h), fp32
+ *                                       accumulation, fp32 outputs.
+ *   akili_<bench>_ex(arg, ex, stream)   same struct plus an `akili_ex_t`:
+ *                                       fp16 inputs/outputs, flash
+ *                                       batch/heads/scale, caller workspace.
+ *
+ * Return value: 0 (AKILI_OK) or a negative AKILI_E_* code.  Nothing here
+ * calls exit().  Calls are asynchronous with respect to the host; device-side
+ * wait timeouts are reported by akili_device_status().
+ *
+ * Ownership: the caller owns every buffer and the stream.  Scratch fields of
+ * the reference structs (norm_addr, gate_addr, temp_addr) may be written.
+ */
+#ifndef AKILI_H_
+#define AKILI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t (cuda_runtime_api.h: typedef struct CUstream_st *cudaStream_t). */
+struct CUstream_st;
+typedef struct CUstream_st* akili_stream_t;
+
+#define AKILI_ABI_VERSION 1u
+
+/* ---- status codes -------------------------------------------------------- */
+#define AKILI_OK                  0
+#define AKILI_E_NULL_ARG         (-1)  /* arg block or a required buffer address is 0      */
+#define AKILI_E_SHAPE            (-2)  /* a size is 0 (other than M) or not a multiple of 8 */
+#define AKILI_E_ALIGN            (-3)  /* a buffer address is not 16-byte aligned           */
+#define AKILI_E_DTYPE            (-4)  /* unsupported in_dtype / out_dtype                  */
+#define AKILI_E_UNSUPPORTED      (-5)  /* e.g. causal=1, head_dim > 128                     */
+#define AKILI_E_NO_DEVICE        (-6)  /* current device is not an sm_100 part              */
+#define AKILI_E_ALLOC            (-7)  /* internal scratch pool could not grow              */
+#define AKILI_E_LAUNCH           (-8)  /* a CUDA launch or tensor-map encode failed         */
+#define AKILI_E_DEVICE_TIMEOUT   (-9)  /* a device-side wait ran out (see device status)    */
+#define AKILI_E_ABI             (-10)  /* ex->abi_version != AKILI_ABI_VERSION              */
+#define AKILI_E_WORKSPACE       (-11)  /* ex->workspace given but smaller than required     */
+
+#define AKILI_DTYPE_F32 0u
+#define AKILI_DTYPE_F16 1u
+
+/* ---- reference argument blocks (byte-identical to akili-bench) ---------- */
+
+/* benchmarks/kbt_sgemm/common.h:4-13 — C[MxN] = A[MxK] . B[KxN] */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  uint64_t a_addr, b_addr, c_addr;
+} kbt_sgemm_arg_t;
+
+/* benchmarks/kbt_gemm_add_relu/common.h:4-14 — ReLU(x.W + bias) */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kbt_gemm_add_relu_arg_t;
+
+/* benchmarks/kbt_gemm_mul_leakyrelu/common.h:4-16 — LeakyReLU((x.W + b) * multiplier) */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  float    multiplier;
+  float    negative_slope;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kbt_gemm_mul_leakyrelu_arg_t;
+
+/* benchmarks/kbt_gemm_div_sum_scale/common.h:4-14 — c[M] = scaling_factor * sum_j (x.W)[i,j] / 2 */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  float    scaling_factor;
+  uint64_t a_addr, w_addr, c_addr;
+} kbt_gemm_div_sum_scale_arg_t;
+
+/* benchmarks/kbt_gemm_layernorm/common.h:4-17 — LayerNorm(x.W + bias) * ln_w + ln_b */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  float    eps;
+  uint64_t a_addr, w_addr, bias_addr, ln_w_addr, ln_b_addr, c_addr;
+} kbt_gemm_layernorm_arg_t;
+
+/* benchmarks/kbt_attention_score/common.h:4-13 — softmax(Q.K^T / sqrt(D)), Q[MxD], K[NxD] */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, D;
+  uint64_t q_addr, k_addr, c_addr;
+} kbt_attention_score_arg_t;
+
+/* benchmarks/kbt_matmul_softmax/common.h:4-13 — softmax(A.B) */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  uint64_t a_addr, b_addr, c_addr;
+} kbt_matmul_softmax_arg_t;
+
+/* benchmarks/kbt_matmul_scale_residadd_clamp/common.h:4-17 —
+ * t = clamp(2*scale*(A.B)); lse = LSE_j t; c[i] = lse * mish(lse) */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  float    scale_factor;
+  float    clamp_min;
+  float    clamp_max;
+  uint64_t a_addr, b_addr, c_addr, temp_addr;
+} kbt_matmul_scale_residadd_clamp_arg_t;
+
+/* benchmarks/kbt_matmul_sum_max_avgpool/common.h:4-14 — c[i] = sum_j (x.W + bias)[i,j] */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kbt_matmul_sum_max_avgpool_arg_t;
+
+/* benchmarks/kbt_gemm_rmsnorm_swiglu/common.h:4-18 — SiLU(RMSNorm(x).Wg) * (RMSNorm(x).Wu) */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  float    eps;
+  uint64_t x_addr, rms_w_addr, wg_addr, wu_addr, norm_addr, gate_addr, c_addr;
+} kbt_gemm_rmsnorm_swiglu_arg_t;
+
+/* benchmarks/kbt_gemm_silu_mul/common.h:4-17 — SiLU(x.Wa + ba) * (x.Wb + bb) */
+typedef struct {
+  uint32_t grid_dim[3];
+  uint32_t block_dim[3];
+  uint32_t M, N, K;
+  uint64_t a_addr, wa_addr, ba_addr, wb_addr, bb_addr, gate_addr, c_addr;
+} kbt_gemm_silu_mul_arg_t;
+
+/* benchmarks/flash/common.h:8-20 — O = softmax(Q.K^T).V, one head, Q/K/V/O [seq_len x head_dim] */
+typedef struct {
+  uint32_t grid_dim[1];
+  uint32_t block_dim[1];
+  uint32_t kernel_type;   /* 0: SIMT, 1: tensor core — both run the same sm_100a kernel here */
+  uint32_t seq_len;
+  uint32_t head_dim;
+  uint32_t block_size_r;
+  uint32_t block_size_c;
+  uint64_t Q_addr, K_addr, V_addr, O_addr;
+} flash_arg_t;
+
+/* ---- extension block for the fp16 / batched forms ------------------------ */
+typedef struct {
+  uint32_t abi_version;     /* must be AKILI_ABI_VERSION                                  */
+  uint32_t in_dtype;        /* AKILI_DTYPE_F32 or AKILI_DTYPE_F16: activations + weights  */
+  uint32_t out_dtype;       /* AKILI_DTYPE_F32 or AKILI_DTYPE_F16                          */
+  uint32_t batch;           /* flash: batch size (0 means 1)                               */
+  uint32_t heads;           /* flash: heads per batch entry (0 means 1)                    */
+  float    softmax_scale;   /* flash: scale of Q.K^T (0 means 1, the unscaled reference)   */
+  uint32_t causal;          /* reserved; must be 0                                         */
+  uint32_t flags;           /* reserved; must be 0                                         */
+  uint64_t workspace;       /* optional device scratch; 0 means the internal pool          */
+  uint64_t workspace_bytes; /* size of `workspace`                                         */
+} akili_ex_t;
+/* Vectors (bias, ln_w, ln_b, rms_w, ba, bb) are fp32 in every form.
+ * Scratch fields in the fp16 form: norm_addr holds M*K fp16, gate_addr and
+ * temp_addr are not written. */
+
+/* ---- entry points ---------------------------------------------------------
+ * Each replaces the device launch of benchmarks/<bench>/kernel.cpp, i.e. the
+ * vx_upload_bytes + vx_start + vx_ready_wait sequence of
+ * benchmarks/<bench>/main.cpp (line ranges per op below).                   */
+
+/* kbt_sgemm/main.cpp:107-111, device kernel_body kbt_sgemm/kernel.cpp:20-84 */
+int akili_kbt_sgemm(const kbt_sgemm_arg_t* arg, akili_stream_t stream);
+int akili_kbt_sgemm_ex(const kbt_sgemm_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_gemm_add_relu/main.cpp:114-118, kernel.cpp:23-88 */
+int akili_kbt_gemm_add_relu(const kbt_gemm_add_relu_arg_t* arg, akili_stream_t stream);
+int akili_kbt_gemm_add_relu_ex(const kbt_gemm_add_relu_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_gemm_mul_leakyrelu/main.cpp:120-124, kernel.cpp:23-90 */
+int akili_kbt_gemm_mul_leakyrelu(const kbt_gemm_mul_leakyrelu_arg_t* arg, akili_stream_t stream);
+int akili_kbt_gemm_mul_leakyrelu_ex(const kbt_gemm_mul_leakyrelu_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_gemm_div_sum_scale/main.cpp:110-114, kernel.cpp:24-95 */
+int akili_kbt_gemm_div_sum_scale(const kbt_gemm_div_sum_scale_arg_t* arg, akili_stream_t stream);
+int akili_kbt_gemm_div_sum_scale_ex(const kbt_gemm_div_sum_scale_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_gemm_layernorm/main.cpp:136-140, kernel.cpp:24-113 */
+int akili_kbt_gemm_layernorm(const kbt_gemm_layernorm_arg_t* arg, akili_stream_t stream);
+int akili_kbt_gemm_layernorm_ex(const kbt_gemm_layernorm_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_attention_score/main.cpp:107-111, kernel.cpp:25-113 */
+int akili_kbt_attention_score(const kbt_attention_score_arg_t* arg, akili_stream_t stream);
+int akili_kbt_attention_score_ex(const kbt_attention_score_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_matmul_softmax/main.cpp:107-111, kernel.cpp:24-105 */
+int akili_kbt_matmul_softmax(const kbt_matmul_softmax_arg_t* arg, akili_stream_t stream);
+int akili_kbt_matmul_softmax_ex(const kbt_matmul_softmax_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_matmul_scale_residadd_clamp/main.cpp:119-123, kernel.cpp:24-117 */
+int akili_kbt_matmul_scale_residadd_clamp(const kbt_matmul_scale_residadd_clamp_arg_t* arg, akili_stream_t stream);
+int akili_kbt_matmul_scale_residadd_clamp_ex(const kbt_matmul_scale_residadd_clamp_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_matmul_sum_max_avgpool/main.cpp:114-118, kernel.cpp:25-96 */
+int akili_kbt_matmul_sum_max_avgpool(const kbt_matmul_sum_max_avgpool_arg_t* arg, akili_stream_t stream);
+int akili_kbt_matmul_sum_max_avgpool_ex(const kbt_matmul_sum_max_avgpool_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_gemm_rmsnorm_swiglu/main.cpp:137-141, kernel.cpp:70-124 */
+int akili_kbt_gemm_rmsnorm_swiglu(const kbt_gemm_rmsnorm_swiglu_arg_t* arg, akili_stream_t stream);
+int akili_kbt_gemm_rmsnorm_swiglu_ex(const kbt_gemm_rmsnorm_swiglu_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* kbt_gemm_silu_mul/main.cpp:136-140, kernel.cpp:25-146 */
+int akili_kbt_gemm_silu_mul(const kbt_gemm_silu_mul_arg_t* arg, akili_stream_t stream);
+int akili_kbt_gemm_silu_mul_ex(const kbt_gemm_silu_mul_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* flash/main.cpp:299-307, device entry flash_kernel_entry flash/kernel.cpp:344-417 */
+int akili_flash(const flash_arg_t* arg, akili_stream_t stream);
+int akili_flash_ex(const flash_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* ---- runtime helpers (no counterpart in the reference beyond RT_CHECK) --- */
+
+/* Human-readable text for an AKILI_E_* code (static storage). */
+const char* akili_strerror(int code);
+
+/* Bytes of scratch an `_ex` call with these arguments uses; `op` is the
+ * benchmark name without the akili_ prefix, e.g. "kbt_gemm_layernorm".  The
+ * `arg` pointer must point at that op's struct.  Returns AKILI_OK. */
+int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex, uint64_t* bytes);
+
+/* Device status word of the current device: 0 when no kernel has timed out
+ * on a device-side wait since the last clear, else the code of the first wait
+ * that gave up.  Synchronises the device. `clear` != 0 resets it. */
+int akili_device_status(uint32_t* status, int clear);
+
+/* Number of kernel launches this library has issued in this process
+ * (all devices).  For launch accounting in benchmarks. */
+uint64_t akili_launch_count(void);
+
+/* ABI version compiled into the library. */
+uint32_t akili_abi_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* Layout checks against the reference structs (offsets measured with g++ on
+ * x86-64 from benchmarks/<bench>/common.h; the same natural alignment holds
+ * on RV64). */
+#define AKILI_CHECK_LAYOUT(T, sz) static_assert(sizeof(T) == (sz), #T " size")
+AKILI_CHECK_LAYOUT(kbt_sgemm_arg_t, 64);
+AKILI_CHECK_LAYOUT(kbt_gemm_add_relu_arg_t, 72);
+AKILI_CHECK_LAYOUT(kbt_gemm_mul_leakyrelu_arg_t, 80);
+AKILI_CHECK_LAYOUT(kbt_gemm_div_sum_scale_arg_t, 64);
+AKILI_CHECK_LAYOUT(kbt_gemm_layernorm_arg_t, 88);
+AKILI_CHECK_LAYOUT(kbt_attention_score_arg_t, 64);
+AKILI_CHECK_LAYOUT(kbt_matmul_softmax_arg_t, 64);
+AKILI_CHECK_LAYOUT(kbt_matmul_scale_residadd_clamp_arg_t, 80);
+AKILI_CHECK_LAYOUT(kbt_matmul_sum_max_avgpool_arg_t, 72);
+AKILI_CHECK_LAYOUT(kbt_gemm_rmsnorm_swiglu_arg_t, 96);
+AKILI_CHECK_LAYOUT(kbt_gemm_silu_mul_arg_t, 96);
+AKILI_CHECK_LAYOUT(flash_arg_t, 64);
+AKILI_CHECK_LAYOUT(akili_ex_t, 48);
+static_assert(offsetof(kbt_sgemm_arg_t, M) == 24 && offsetof(kbt_sgemm_arg_t, a_addr) == 40 &&
+              offsetof(kbt_sgemm_arg_t, c_addr) == 56, "kbt_sgemm offsets");
+static_assert(offsetof(kbt_gemm_mul_leakyrelu_arg_t, multiplier) == 36 &&
+              offsetof(kbt_gemm_mul_leakyrelu_arg_t, a_addr) == 48, "mul_leakyrelu offsets");
+static_assert(offsetof(kbt_gemm_layernorm_arg_t, eps) == 36 &&
+              offsetof(kbt_gemm_layernorm_arg_t, c_addr) == 80, "layernorm offsets");
+static_assert(offsetof(kbt_matmul_scale_residadd_clamp_arg_t, clamp_max) == 44 &&
+              offsetof(kbt_matmul_scale_residadd_clamp_arg_t, temp_addr) == 72, "clamp offsets");
+static_assert(offsetof(kbt_gemm_rmsnorm_swiglu_arg_t, x_addr) == 40 &&
+              offsetof(kbt_gemm_rmsnorm_swiglu_arg_t, c_addr) == 88, "swiglu offsets");
+static_assert(offsetof(kbt_gemm_silu_mul_arg_t, bb_addr) == 72 &&
+              offsetof(kbt_gemm_silu_mul_arg_t, c_addr) == 88, "silu_mul offsets");
+static_assert(offsetof(flash_arg_t, kernel_type) == 8 && offsetof(flash_arg_t, block_size_c) == 24 &&
+              offsetof(flash_arg_t, Q_addr) == 32 && offsetof(flash_arg_t, O_addr) == 56, "flash offsets");
+#undef AKILI_CHECK_LAYOUT
+#endif
+
+#endif /* AKILI_H_ */

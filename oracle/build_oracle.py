@@ -1,0 +1,140 @@
+"""Build recipe for the CPU oracle and the reference-built pin binaries.
+
+TEST INFRASTRUCTURE.  Outputs:
+
+* ``oracle/liboracle.so`` — oracle/oracle.c (the plain-C restatement of the
+  reference gold loops), loaded by tests/ and by bench.py's CPU-baseline leg.
+* ``oracle/_ref/pin/<bench>`` — akili-bench's own, unchanged
+  ``benchmarks/<bench>/main.cpp`` compiled with the reference's host flags
+  (common/common.mk:63-71: ``-std=c++17 -O2 -DNDEBUG``) against
+  ``include/vortex.h`` + ``oracle/shim/vortex_host.cpp`` (a host-memory
+  device that runs the oracle) and force-including ``oracle/shim/probe.h``.
+  Run with ``AKILI_PROBE=exact`` the reference's verify loop passes only if
+  the oracle is bit-identical to the reference gold.
+* ``oracle/_ref/b200/<bench>`` — the same unchanged ``main.cpp`` linked
+  against the product's ``libakili_vortex.so`` (the Vortex runtime API on
+  top of the akili_* C ABI): the reference harness driving the B200 kernels
+  and judging them with its own gold check.
+
+The reference sources are read in place (``--ref``, default
+/root/reference); nothing is copied.  ``oracle/_ref/`` is git-ignored and
+travels with the working tree like the other built artefacts.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+REF_OUT = os.path.join(HERE, "_ref")
+
+BENCHES = [
+    "kbt_sgemm",
+    "kbt_gemm_add_relu",
+    "kbt_gemm_mul_leakyrelu",
+    "kbt_gemm_div_sum_scale",
+    "kbt_gemm_layernorm",
+    "kbt_attention_score",
+    "kbt_matmul_softmax",
+    "kbt_matmul_scale_residadd_clamp",
+    "kbt_matmul_sum_max_avgpool",
+    "kbt_gemm_rmsnorm_swiglu",
+    "kbt_gemm_silu_mul",
+    "flash",
+]
+
+# The reference's host compile flags (common/common.mk:63,69-71).
+REF_CXXFLAGS = ["-std=c++17", "-O2", "-DNDEBUG"]
+# The oracle is compiled with the same optimisation level and no FMA ISA so
+# its float arithmetic matches the reference's gold loops bit for bit.
+ORACLE_CFLAGS = ["-std=c11", "-O2", "-DNDEBUG", "-fPIC", "-ffp-contract=off"]
+
+
+def _run(cmd: list[str]) -> None:
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"command failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+
+
+def _newer(out: str, srcs: list[str]) -> bool:
+    if not os.path.exists(out):
+        return False
+    t = os.path.getmtime(out)
+    return all(os.path.getmtime(s) <= t for s in srcs if os.path.exists(s))
+
+
+def build_oracle_lib(force: bool = False) -> str:
+    """Compile oracle/oracle.c into oracle/liboracle.so."""
+    src = os.path.join(HERE, "oracle.c")
+    out = os.path.join(HERE, "liboracle.so")
+    if force or not _newer(out, [src, os.path.join(HERE, "oracle.h")]):
+        _run(["gcc", *ORACLE_CFLAGS, "-shared", src, "-o", out, "-lm"])
+    return out
+
+
+def build_pin_binaries(ref_root: str, force: bool = False) -> list[str]:
+    """Reference main.cpp + host-memory Vortex device running the oracle."""
+    os.makedirs(os.path.join(REF_OUT, "pin"), exist_ok=True)
+    obj = os.path.join(REF_OUT, "oracle_pin.o")
+    _run(["gcc", *ORACLE_CFLAGS, "-c", os.path.join(HERE, "oracle.c"), "-o", obj])
+    shim = os.path.join(HERE, "shim", "vortex_host.cpp")
+    probe = os.path.join(HERE, "shim", "probe.h")
+    # The shim is its own translation unit: the probe macros apply to main.cpp only.
+    shim_obj = os.path.join(REF_OUT, "vortex_host.o")
+    _run(["g++", *REF_CXXFLAGS, "-ffp-contract=off", "-I", os.path.join(ROOT, "include"),
+          "-c", shim, "-o", shim_obj])
+    built = []
+    for b in BENCHES:
+        main = os.path.join(ref_root, "benchmarks", b, "main.cpp")
+        out = os.path.join(REF_OUT, "pin", b)
+        if not force and _newer(out, [main, shim, probe, obj]):
+            built.append(out)
+            continue
+        _run(["g++", *REF_CXXFLAGS, "-ffp-contract=off", "-I", os.path.join(ROOT, "include"),
+              "-include", probe, main, shim_obj, obj, "-o", out, "-lm"])
+        built.append(out)
+    return built
+
+
+def build_b200_binaries(ref_root: str, libdir: str, force: bool = False) -> list[str]:
+    """Reference main.cpp linked against the product's Vortex-API library."""
+    lib = os.path.join(libdir, "libakili_vortex.so")
+    if not os.path.exists(lib):
+        raise FileNotFoundError(lib)
+    os.makedirs(os.path.join(REF_OUT, "b200"), exist_ok=True)
+    built = []
+    for b in BENCHES:
+        main = os.path.join(ref_root, "benchmarks", b, "main.cpp")
+        out = os.path.join(REF_OUT, "b200", b)
+        if not force and _newer(out, [main, lib]):
+            built.append(out)
+            continue
+        _run(["g++", *REF_CXXFLAGS, "-I", os.path.join(ROOT, "include"), main,
+              "-L", libdir, "-lakili_vortex", f"-Wl,-rpath,{libdir}", "-o", out])
+        built.append(out)
+    return built
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--libdir", default=os.path.join(ROOT, "akili_bench_b200"))
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args()
+    print(build_oracle_lib(a.force))
+    if os.path.isdir(a.ref):
+        for p in build_pin_binaries(a.ref, a.force):
+            print(p)
+        if os.path.exists(os.path.join(a.libdir, "libakili_vortex.so")):
+            for p in build_b200_binaries(a.ref, a.libdir, a.force):
+                print(p)
+    else:
+        print(f"reference tree {a.ref} absent: pin binaries not rebuilt", file=sys.stderr)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,315 @@
+/*
+ * oracle.c — CPU oracle (TEST INFRASTRUCTURE, never linked by the product).
+ *
+ * Plain-C restatement of akili-bench's host gold loops; each function cites
+ * the verify block it restates.  Loop order, accumulation order, the point
+ * where each scalar is applied and the libm calls (expf, logf, tanhf, sqrtf)
+ * follow the reference so that, compiled with the reference's host flags
+ * (-O2, no fast-math, no FMA ISA), the outputs are bit-identical to it.
+ * oracle/build_ref.sh proves that per op at several sizes.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* benchmarks/kbt_sgemm/main.cpp:117-131 */
+void oracle_kbt_sgemm(const float* a, const float* b, float* c, uint32_t M, uint32_t N,
+                      uint32_t K, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float expected = 0;
+      for (uint32_t k = 0; k < K; ++k) expected += a[(uint64_t)i * K + k] * b[(uint64_t)k * N + j];
+      c[(uint64_t)i * N + j] = expected;
+    }
+}
+
+/* benchmarks/kbt_gemm_add_relu/main.cpp:124-129 */
+void oracle_kbt_gemm_add_relu(const float* a, const float* w, const float* bias, float* c,
+                              uint32_t M, uint32_t N, uint32_t K, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum = bias[j];
+      for (uint32_t k = 0; k < K; ++k) sum += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      c[(uint64_t)i * N + j] = (sum > 0.0f) ? sum : 0.0f;
+    }
+}
+
+/* benchmarks/kbt_gemm_mul_leakyrelu/main.cpp:130-136 */
+void oracle_kbt_gemm_mul_leakyrelu(const float* a, const float* w, const float* bias, float* c,
+                                   uint32_t M, uint32_t N, uint32_t K, float multiplier,
+                                   float negative_slope, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum = bias[j];
+      for (uint32_t k = 0; k < K; ++k) sum += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      float val = sum * multiplier;
+      c[(uint64_t)i * N + j] = (val >= 0.0f) ? val : val * negative_slope;
+    }
+}
+
+/* benchmarks/kbt_gemm_div_sum_scale/main.cpp:120-128 */
+void oracle_kbt_gemm_div_sum_scale(const float* a, const float* w, float* c, uint32_t M,
+                                   uint32_t N, uint32_t K, float scaling_factor, uint32_t row0,
+                                   uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float row_sum = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      float gemm_val = 0.0f;
+      for (uint32_t k = 0; k < K; ++k)
+        gemm_val += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      row_sum += gemm_val * 0.5f;
+    }
+    c[i] = row_sum * scaling_factor;
+  }
+}
+
+/* benchmarks/kbt_gemm_layernorm/main.cpp:145-170 (GEMM+bias :146-152, LayerNorm :154-170) */
+void oracle_kbt_gemm_layernorm(const float* a, const float* w, const float* bias,
+                               const float* ln_w, const float* ln_b, float* c, uint32_t M,
+                               uint32_t N, uint32_t K, float eps, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float* ref = c + (uint64_t)i * N;
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum = 0;
+      for (uint32_t k = 0; k < K; ++k) sum += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      ref[j] = sum + bias[j];
+    }
+    float mean = 0;
+    for (uint32_t j = 0; j < N; ++j) mean += ref[j];
+    mean /= (float)N;
+    float var = 0;
+    for (uint32_t j = 0; j < N; ++j) {
+      float d = ref[j] - mean;
+      var += d * d;
+    }
+    var /= (float)N;
+    float inv_std = 1.0f / sqrtf(var + eps);
+    for (uint32_t j = 0; j < N; ++j) {
+      float norm = (ref[j] - mean) * inv_std;
+      ref[j] = norm * ln_w[j] + ln_b[j];
+    }
+  }
+}
+
+/* Row-wise softmax shared by attention_score and matmul_softmax:
+ * benchmarks/kbt_attention_score/main.cpp:132-142 and
+ * benchmarks/kbt_matmul_softmax/main.cpp:127-137. */
+static void softmax_row(float* ref, uint32_t N) {
+  float row_max = -INFINITY;
+  for (uint32_t j = 0; j < N; ++j)
+    if (ref[j] > row_max) row_max = ref[j];
+  float sum = 0;
+  for (uint32_t j = 0; j < N; ++j) {
+    ref[j] = expf(ref[j] - row_max);
+    sum += ref[j];
+  }
+  float inv = 1.0f / sum;
+  for (uint32_t j = 0; j < N; ++j) ref[j] *= inv;
+}
+
+/* benchmarks/kbt_attention_score/main.cpp:117-142: Q.K^T (accumulated in the
+ * output cell), a separate scaling pass by 1/sqrtf(D), then softmax. */
+void oracle_kbt_attention_score(const float* q, const float* k, float* c, uint32_t M,
+                                uint32_t N, uint32_t D, uint32_t row0, uint32_t row1) {
+  (void)M;
+  float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  for (uint32_t i = row0; i < row1; ++i) {
+    float* ref = c + (uint64_t)i * N;
+    for (uint32_t j = 0; j < N; ++j) {
+      ref[j] = 0;
+      for (uint32_t d = 0; d < D; ++d) ref[j] += q[(uint64_t)i * D + d] * k[(uint64_t)j * D + d];
+    }
+    for (uint32_t j = 0; j < N; ++j) ref[j] *= inv_sqrt_d;
+    softmax_row(ref, N);
+  }
+}
+
+/* benchmarks/kbt_matmul_softmax/main.cpp:117-137 */
+void oracle_kbt_matmul_softmax(const float* a, const float* b, float* c, uint32_t M, uint32_t N,
+                               uint32_t K, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float* ref = c + (uint64_t)i * N;
+    for (uint32_t j = 0; j < N; ++j) {
+      ref[j] = 0;
+      for (uint32_t k = 0; k < K; ++k) ref[j] += a[(uint64_t)i * K + k] * b[(uint64_t)k * N + j];
+    }
+    softmax_row(ref, N);
+  }
+}
+
+/* benchmarks/kbt_matmul_scale_residadd_clamp/main.cpp:129-153.  The output
+ * is one scalar per row; the row of clamped values (`row_vals`) is heap
+ * scratch because N can be large. */
+void oracle_kbt_matmul_scale_residadd_clamp(const float* a, const float* b, float* c, uint32_t M,
+                                            uint32_t N, uint32_t K, float scale_factor,
+                                            float clamp_min, float clamp_max, uint32_t row0,
+                                            uint32_t row1) {
+  (void)M;
+  float* row_vals = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = 0.0f;
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * b[(uint64_t)k * N + j];
+      float scaled = dot * scale_factor;
+      float res = scaled + scaled;
+      float clamped = res;
+      if (clamped < clamp_min) clamped = clamp_min;
+      if (clamped > clamp_max) clamped = clamp_max;
+      row_vals[j] = clamped;
+    }
+    float max_val = row_vals[0];
+    for (uint32_t j = 1; j < N; ++j)
+      if (row_vals[j] > max_val) max_val = row_vals[j];
+    float sum_exp = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) sum_exp += expf(row_vals[j] - max_val);
+    float lse = max_val + logf(sum_exp);
+    float mish_lse = lse * tanhf(logf(1.0f + expf(lse)));
+    c[i] = lse * mish_lse;
+  }
+  free(row_vals);
+}
+
+/* benchmarks/kbt_matmul_sum_max_avgpool/main.cpp:124-132 */
+void oracle_kbt_matmul_sum_max_avgpool(const float* a, const float* w, const float* bias,
+                                       float* c, uint32_t M, uint32_t N, uint32_t K,
+                                       uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float total = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = bias[j];
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      total += dot;
+    }
+    c[i] = total;
+  }
+}
+
+/* benchmarks/kbt_gemm_rmsnorm_swiglu/main.cpp:146-172: RMSNorm row (:147-156),
+ * dual GEMM from the fp32 normalised row (:158-168), SiLU(g)*u (:170-175). */
+void oracle_kbt_gemm_rmsnorm_swiglu(const float* x, const float* rms_w, const float* wg,
+                                    const float* wu, float* c, uint32_t M, uint32_t N,
+                                    uint32_t K, float eps, uint32_t row0, uint32_t row1) {
+  (void)M;
+  float* norm = (float*)malloc(sizeof(float) * (K ? K : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    const float* xr = x + (uint64_t)i * K;
+    float ss = 0;
+    for (uint32_t k = 0; k < K; ++k) {
+      float v = xr[k];
+      ss += v * v;
+    }
+    float inv_rms = 1.0f / sqrtf(ss / (float)K + eps);
+    for (uint32_t k = 0; k < K; ++k) norm[k] = xr[k] * inv_rms * rms_w[k];
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum_g = 0, sum_u = 0;
+      for (uint32_t k = 0; k < K; ++k) {
+        sum_g += norm[k] * wg[(uint64_t)k * N + j];
+        sum_u += norm[k] * wu[(uint64_t)k * N + j];
+      }
+      float silu_g = sum_g / (1.0f + expf(-sum_g));
+      c[(uint64_t)i * N + j] = silu_g * sum_u;
+    }
+  }
+  free(norm);
+}
+
+/* benchmarks/kbt_gemm_silu_mul/main.cpp:145-162 */
+void oracle_kbt_gemm_silu_mul(const float* a, const float* wa, const float* ba, const float* wb,
+                              const float* bb, float* c, uint32_t M, uint32_t N, uint32_t K,
+                              uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum_a = 0, sum_b = 0;
+      for (uint32_t k = 0; k < K; ++k) {
+        sum_a += a[(uint64_t)i * K + k] * wa[(uint64_t)k * N + j];
+        sum_b += a[(uint64_t)i * K + k] * wb[(uint64_t)k * N + j];
+      }
+      float g = sum_a + ba[j];
+      float u = sum_b + bb[j];
+      float silu_g = g / (1.0f + expf(-g));
+      c[(uint64_t)i * N + j] = silu_g * u;
+    }
+}
+
+/* benchmarks/flash/main.cpp:52-85 (attention_cpu), per query row, plus a
+ * scale on each dot product (1.0f is exact, so scale=1 is the reference). */
+void oracle_flash(float* out, const float* q, const float* k, const float* v, uint32_t seq_len,
+                  uint32_t d, float scale, uint32_t row0, uint32_t row1) {
+  uint32_t N = seq_len;
+  float* scores = (float*)malloc(sizeof(float) * (N ? N : 1));
+  float* probs = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum = 0.0f;
+      for (uint32_t kk = 0; kk < d; ++kk) sum += q[(uint64_t)i * d + kk] * k[(uint64_t)j * d + kk];
+      scores[j] = sum * scale;
+    }
+    float mx = scores[0];
+    for (uint32_t j = 1; j < N; ++j) mx = (mx < scores[j]) ? scores[j] : mx; /* std::max */
+    float exp_sum = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      float e = expf(scores[j] - mx);
+      probs[j] = e;
+      exp_sum += e;
+    }
+    for (uint32_t j = 0; j < N; ++j) probs[j] /= exp_sum;
+    for (uint32_t kk = 0; kk < d; ++kk) {
+      float sum = 0.0f;
+      for (uint32_t j = 0; j < N; ++j) sum += probs[j] * v[(uint64_t)j * d + kk];
+      out[(uint64_t)i * d + kk] = sum;
+    }
+  }
+  free(scores);
+  free(probs);
+}
+
+/* IEEE binary16 round-to-nearest-even, as the reference's f2h (`(__fp16)x`,
+ * benchmarks/kbt_sgemm/kernel.cpp:13-18) and CUDA's __float2half_rn do.
+ * Written from the format definition: 1 sign, 5 exponent (bias 15),
+ * 10 fraction bits; subnormals below 2^-14; overflow to infinity. */
+float oracle_round_f16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  uint32_t sign = u & 0x80000000u;
+  uint32_t absu = u & 0x7fffffffu;
+  float r;
+  if (absu >= 0x7f800000u) return x; /* inf / nan unchanged */
+  float ax;
+  memcpy(&ax, &absu, 4);
+  if (ax >= 65520.0f) { /* rounds to inf */
+    uint32_t inf = sign | 0x7f800000u;
+    memcpy(&r, &inf, 4);
+    return r;
+  }
+  if (ax < 6.103515625e-05f) { /* subnormal range: quantum 2^-24 */
+    const float q = 5.9604644775390625e-08f;
+    float t = ax / q;                 /* exact: power-of-two divide */
+    float n = nearbyintf(t);          /* ties-to-even under the default mode */
+    r = n * q;
+  } else {
+    /* keep 10 fraction bits: round the low 13 bits, ties to even */
+    uint32_t low = absu & 0x1fffu;
+    uint32_t base = absu & ~0x1fffu;
+    if (low > 0x1000u || (low == 0x1000u && (base & 0x2000u))) base += 0x2000u;
+    memcpy(&r, &base, 4);
+  }
+  uint32_t ru;
+  memcpy(&ru, &r, 4);
+  ru |= sign;
+  memcpy(&r, &ru, 4);
+  return r;
+}
+
+void oracle_round_f16_array(float* x, uint64_t n) {
+  for (uint64_t i = 0; i < n; ++i) x[i] = oracle_round_f16(x[i]);
+}
