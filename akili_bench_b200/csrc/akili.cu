@@ -1,0 +1,832 @@
+// akili.cu — the C ABI of include/akili.h: argument validation, scratch,
+// tensor-map construction and kernel launches for every kbt_* op and flash.
+//
+// Each akili_<bench>() replaces the Vortex launch of benchmarks/<bench>/
+// kernel.cpp (the vx_upload_bytes + vx_start + vx_ready_wait sequence of its
+// main.cpp).  The plain form keeps the reference semantics (fp32 buffers,
+// operands rounded to fp16 on the device, fp32 outputs); the _ex form takes
+// an akili_ex_t (fp16 I/O, flash batch/heads/scale, caller workspace).
+// Validation runs before any CUDA call, so a bad argument block is rejected
+// even where no GPU is present.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <mutex>
+#include <utility>
+
+#include "../../include/akili.h"
+#include "aux.cuh"
+#include "flash.cuh"
+#include "gemm.cuh"
+
+using namespace akili;
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+// ------------------------------------------------------------ arguments --
+struct Mode {
+  bool in_f32 = true;
+  bool out_f32 = true;
+  uint32_t batch = 1, heads = 1;
+  float scale = 1.0f;
+  void* workspace = nullptr;
+  uint64_t workspace_bytes = 0;
+};
+
+int parse_ex(const akili_ex_t* ex, Mode* md) {
+  *md = Mode{};
+  if (!ex) return AKILI_OK;
+  if (ex->abi_version != AKILI_ABI_VERSION) return AKILI_E_ABI;
+  if (ex->in_dtype > AKILI_DTYPE_F16 || ex->out_dtype > AKILI_DTYPE_F16) return AKILI_E_DTYPE;
+  if (ex->causal != 0 || ex->flags != 0) return AKILI_E_UNSUPPORTED;
+  md->in_f32 = ex->in_dtype == AKILI_DTYPE_F32;
+  md->out_f32 = ex->out_dtype == AKILI_DTYPE_F32;
+  md->batch = ex->batch ? ex->batch : 1;
+  md->heads = ex->heads ? ex->heads : 1;
+  md->scale = ex->softmax_scale != 0.0f ? ex->softmax_scale : 1.0f;
+  md->workspace = reinterpret_cast<void*>(ex->workspace);
+  md->workspace_bytes = ex->workspace ? ex->workspace_bytes : 0;
+  return AKILI_OK;
+}
+
+int check_dims(uint32_t N, uint32_t K) {
+  if (N == 0 || K == 0 || (N % 8) || (K % 8)) return AKILI_E_SHAPE;
+  return AKILI_OK;
+}
+int check_m(uint32_t M) { return (M % 8) ? AKILI_E_SHAPE : AKILI_OK; }
+
+int check_ptrs(std::initializer_list<uint64_t> ps) {
+  for (uint64_t p : ps)
+    if (p == 0) return AKILI_E_NULL_ARG;
+  for (uint64_t p : ps)
+    if (p % 16) return AKILI_E_ALIGN;
+  return AKILI_OK;
+}
+int check_opt_ptr(uint64_t p) { return (p % 16) ? AKILI_E_ALIGN : AKILI_OK; }
+
+// --------------------------------------------------------------- device --
+struct DevInfo {
+  int sms = 0;
+  bool sm100 = false;
+};
+
+int device_info(DevInfo* out) {
+  static std::mutex mu;
+  static std::map<int, DevInfo> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return AKILI_E_NO_DEVICE;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  auto it = cache.find(dev);
+  if (it == cache.end()) {
+    DevInfo d;
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return AKILI_E_NO_DEVICE;
+    }
+    d.sm100 = (major == 10 && minor == 0);
+    it = cache.emplace(dev, d).first;
+  }
+  *out = it->second;
+  return out->sm100 ? AKILI_OK : AKILI_E_NO_DEVICE;
+}
+
+// ----------------------------------------------------------- tensor maps --
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+
+// Row-major [outer x inner] tensor, tile [box_outer x box_inner].
+bool map2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+           uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [d2][d1][d0] tensor with contiguous d0.
+bool map3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, uint64_t d0, uint64_t d1, uint64_t d2,
+           uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw, uint32_t elem_bytes) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * elem_bytes, d0 * d1 * elem_bytes};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// --------------------------------------------------------------- scratch --
+// Internal scratch, one grow-only buffer per (device, stream): calls on one
+// stream are ordered, so they can share it.  Used when the caller gives no
+// akili_ex_t workspace.  Growing it frees the old buffer (a device sync).
+struct Pool {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+int pool_get(cudaStream_t st, size_t bytes, void** out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, Pool> pools;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  Pool& p = pools[{dev, st}];
+  if (p.bytes < bytes) {
+    if (p.ptr) cudaFree(p.ptr);
+    p.ptr = nullptr;
+    p.bytes = 0;
+    size_t want = bytes + bytes / 4 + (1u << 20);
+    if (cudaMalloc(&p.ptr, want) != cudaSuccess) {
+      cudaGetLastError();
+      return AKILI_E_ALLOC;
+    }
+    p.bytes = want;
+  }
+  *out = p.ptr;
+  return AKILI_OK;
+}
+
+struct Carve {
+  char* base = nullptr;
+  size_t off = 0;
+  size_t need(size_t n) {  // sizing pass when base == nullptr
+    size_t o = off;
+    off += (n + 255) & ~size_t(255);
+    return o;
+  }
+  void* take(size_t n) { return base + need(n); }
+};
+
+int acquire_scratch(const Mode& md, size_t bytes, cudaStream_t st, char** out) {
+  *out = nullptr;
+  if (bytes == 0) return AKILI_OK;
+  if (md.workspace) {
+    if (md.workspace_bytes < bytes) return AKILI_E_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(md.workspace) % 256) return AKILI_E_ALIGN;
+    *out = static_cast<char*>(md.workspace);
+    return AKILI_OK;
+  }
+  void* p = nullptr;
+  int rc = pool_get(st, bytes, &p);
+  *out = static_cast<char*>(p);
+  return rc;
+}
+
+int launch_status() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AKILI_OK : AKILI_E_LAUNCH;
+}
+
+int grid_for(const DevInfo& di, size_t work_items, int per_block, int waves = 4) {
+  size_t blocks = (work_items + per_block - 1) / per_block;
+  size_t cap = static_cast<size_t>(di.sms) * waves;
+  if (blocks > cap) blocks = cap;
+  return blocks < 1 ? 1 : static_cast<int>(blocks);
+}
+
+int cast_to_f16(const DevInfo& di, const float* src, __half* dst, size_t n, cudaStream_t st) {
+  cast_f32_to_f16_kernel<<<grid_for(di, n / 8 + 1, 256, 8), 256, 0, st>>>(src, dst, n);
+  return launch_status();
+}
+
+// ------------------------------------------------------------ GEMM jobs --
+struct GemmJob {
+  Epi epi = Epi::kPlain;
+  bool b_kmajor = false;
+  uint32_t M = 0, N = 0, K = 0;
+  const void* A = nullptr;   // [M x K] (in dtype)
+  const void* B0 = nullptr;  // [K x N] or, when b_kmajor, [N x K]
+  const void* B1 = nullptr;  // second weight of the dual GEMMs
+  const float* vec0 = nullptr;
+  const float* vec1 = nullptr;
+  float s0 = 0, s1 = 0, s2 = 0;
+  void* C = nullptr;                 // [M x N] or [M]
+  void* stats_hint = nullptr;        // caller scratch usable for partial stats
+  size_t stats_hint_bytes = 0;
+  // RMSNorm pre-pass (A = x_hat computed from X)
+  bool rmsnorm = false;
+  const float* rms_w = nullptr;
+  void* xhat_hint = nullptr;         // caller scratch for x_hat (norm_addr)
+  // finalisers
+  float final_scale = 1.0f;
+  float eps = 0.0f;
+  const float* ln_w = nullptr;
+  const float* ln_b = nullptr;
+};
+
+size_t stats_bytes(const GemmJob& j) {
+  const int bn = epi_bn(j.epi);
+  const size_t nt = (j.N + bn - 1) / bn;
+  return static_cast<size_t>(epi_stats(j.epi)) * nt * j.M * sizeof(float);
+}
+
+// Sizing and carving share one routine so they cannot disagree.
+struct JobBuffers {
+  const __half* A = nullptr;
+  const __half* B0 = nullptr;
+  const __half* B1 = nullptr;
+  __half* castA = nullptr;
+  __half* castB0 = nullptr;
+  __half* castB1 = nullptr;
+  float* stats = nullptr;
+};
+
+size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
+  const bool dual = epi_dual(j.epi);
+  const size_t nA = static_cast<size_t>(j.M) * j.K;
+  const size_t nB = static_cast<size_t>(j.K) * j.N;
+  auto grab = [&](size_t bytes) -> void* { return cv.base ? cv.take(bytes) : (cv.need(bytes), nullptr); };
+  if (j.rmsnorm) {
+    if (j.xhat_hint) jb->castA = static_cast<__half*>(j.xhat_hint);
+    else jb->castA = static_cast<__half*>(grab(nA * 2));
+    jb->A = jb->castA;
+  } else if (md.in_f32) {
+    jb->castA = static_cast<__half*>(grab(nA * 2));
+    jb->A = jb->castA;
+  } else {
+    jb->A = static_cast<const __half*>(j.A);
+  }
+  if (md.in_f32) {
+    jb->castB0 = static_cast<__half*>(grab(nB * 2));
+    jb->B0 = jb->castB0;
+    if (dual) {
+      jb->castB1 = static_cast<__half*>(grab(nB * 2));
+      jb->B1 = jb->castB1;
+    }
+  } else {
+    jb->B0 = static_cast<const __half*>(j.B0);
+    jb->B1 = static_cast<const __half*>(j.B1);
+  }
+  const size_t sb = stats_bytes(j);
+  if (sb) {
+    if (j.stats_hint && j.stats_hint_bytes >= sb) jb->stats = static_cast<float*>(j.stats_hint);
+    else jb->stats = static_cast<float*>(grab(sb));
+  }
+  return cv.off;
+}
+
+template <Epi E, typename OutT, bool BK>
+int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaStream_t st) {
+  constexpr bool kStore = epi_stores(E);
+  constexpr int BN = epi_bn(E);
+  CUtensorMap tmA, tmB0, tmB1, tmC;
+  const uint64_t M = j.M, N = j.N, K = j.K;
+  bool ok = map2d(&tmA, jb.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, K * 2, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (BK) {
+    ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, N, K * 2, 64, BN,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K, N * 2, 64, 64,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (epi_dual(E)) {
+    ok = ok && map2d(&tmB1, jb.B1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K, N * 2, 64, 64,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    tmB1 = tmB0;
+  }
+  if (kStore) {
+    if (sizeof(OutT) == 2)
+      ok = ok && map2d(&tmC, j.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, M, N * 2, 32, kBM, CU_TENSOR_MAP_SWIZZLE_64B);
+    else
+      ok = ok && map2d(&tmC, j.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, N * 4, 32, kBM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    tmC = tmA;
+  }
+  if (!ok) return AKILI_E_LAUNCH;
+
+  EpiArgs ea;
+  ea.vec0 = j.vec0;
+  ea.vec1 = j.vec1;
+  ea.s0 = j.s0;
+  ea.s1 = j.s1;
+  ea.s2 = j.s2;
+  ea.s3 = 0.0f;
+  ea.row_ws = jb.stats;
+  ea.M = static_cast<int>(M);
+  ea.N = static_cast<int>(N);
+  ea.K = static_cast<int>(K);
+  ea.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+
+  const int smem = gemm_smem_bytes(kStore, sizeof(OutT));
+  static std::mutex mu;
+  static std::map<int, bool> attr_done;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (!attr_done[dev]) {
+      if (cudaFuncSetAttribute(gemm_kernel<E, OutT, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess) {
+        cudaGetLastError();
+        return AKILI_E_LAUNCH;
+      }
+      attr_done[dev] = true;
+    }
+  }
+  const int tiles = static_cast<int>(((M + kBM - 1) / kBM) * ((N + BN - 1) / BN));
+  const int grid = tiles < di.sms ? tiles : di.sms;
+  gemm_kernel<E, OutT, BK><<<grid, kGemmThreads, smem, st>>>(tmA, tmB0, tmB1, tmC, ea);
+  return launch_status();
+}
+
+template <Epi E, bool BK = false>
+int launch_gemm_out(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, bool out_f32, cudaStream_t st) {
+  if constexpr (!epi_stores(E)) {
+    return launch_gemm<E, float, BK>(di, j, jb, st);
+  } else {
+    return out_f32 ? launch_gemm<E, float, BK>(di, j, jb, st) : launch_gemm<E, __half, BK>(di, j, jb, st);
+  }
+}
+
+int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
+  if (j.M == 0) return AKILI_OK;
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+
+  JobBuffers jb;
+  Carve sizing;
+  const size_t bytes = layout_job(j, md, sizing, &jb);
+  char* base = nullptr;
+  rc = acquire_scratch(md, bytes, st, &base);
+  if (rc) return rc;
+  Carve cv;
+  cv.base = base;
+  jb = JobBuffers{};
+  layout_job(j, md, cv, &jb);
+
+  const size_t nA = static_cast<size_t>(j.M) * j.K;
+  const size_t nB = static_cast<size_t>(j.K) * j.N;
+  // 1. operand preparation
+  if (j.rmsnorm) {
+    const int rows_per_block = 8;
+    const int grid = grid_for(di, j.M, rows_per_block, 8);
+    if (md.in_f32)
+      rmsnorm_prepass_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(j.A), j.rms_w, jb.castA,
+                                                          static_cast<int>(j.M), static_cast<int>(j.K), j.eps);
+    else
+      rmsnorm_prepass_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(j.A), j.rms_w, jb.castA,
+                                                           static_cast<int>(j.M), static_cast<int>(j.K), j.eps);
+    if ((rc = launch_status())) return rc;
+  } else if (md.in_f32) {
+    if ((rc = cast_to_f16(di, static_cast<const float*>(j.A), jb.castA, nA, st))) return rc;
+  }
+  if (md.in_f32) {
+    if ((rc = cast_to_f16(di, static_cast<const float*>(j.B0), jb.castB0, nB, st))) return rc;
+    if (epi_dual(j.epi) && (rc = cast_to_f16(di, static_cast<const float*>(j.B1), jb.castB1, nB, st))) return rc;
+  }
+  // 2. the fused GEMM
+  switch (j.epi) {
+    case Epi::kPlain: rc = launch_gemm_out<Epi::kPlain>(di, j, jb, md.out_f32, st); break;
+    case Epi::kBiasRelu: rc = launch_gemm_out<Epi::kBiasRelu>(di, j, jb, md.out_f32, st); break;
+    case Epi::kBiasMulLeaky: rc = launch_gemm_out<Epi::kBiasMulLeaky>(di, j, jb, md.out_f32, st); break;
+    case Epi::kRowSumHalf: rc = launch_gemm_out<Epi::kRowSumHalf>(di, j, jb, md.out_f32, st); break;
+    case Epi::kRowSumBias: rc = launch_gemm_out<Epi::kRowSumBias>(di, j, jb, md.out_f32, st); break;
+    case Epi::kLnPre: rc = launch_gemm_out<Epi::kLnPre>(di, j, jb, md.out_f32, st); break;
+    case Epi::kSoftmaxPre:
+      rc = j.b_kmajor ? launch_gemm_out<Epi::kSoftmaxPre, true>(di, j, jb, md.out_f32, st)
+                      : launch_gemm_out<Epi::kSoftmaxPre, false>(di, j, jb, md.out_f32, st);
+      break;
+    case Epi::kLseClamp: rc = launch_gemm_out<Epi::kLseClamp>(di, j, jb, md.out_f32, st); break;
+    case Epi::kSiluMulBias: rc = launch_gemm_out<Epi::kSiluMulBias>(di, j, jb, md.out_f32, st); break;
+    case Epi::kSwiglu: rc = launch_gemm_out<Epi::kSwiglu>(di, j, jb, md.out_f32, st); break;
+  }
+  if (rc) return rc;
+  // 3. finalisers
+  const int M = static_cast<int>(j.M), N = static_cast<int>(j.N);
+  const int nt = (N + epi_bn(j.epi) - 1) / epi_bn(j.epi);
+  switch (j.epi) {
+    case Epi::kRowSumHalf:
+    case Epi::kRowSumBias:
+      if (md.out_f32)
+        finalize_rowsum_kernel<float><<<grid_for(di, M, 256), 256, 0, st>>>(jb.stats, static_cast<float*>(j.C),
+                                                                            M, nt, j.final_scale);
+      else
+        finalize_rowsum_kernel<__half><<<grid_for(di, M, 256), 256, 0, st>>>(jb.stats, static_cast<__half*>(j.C),
+                                                                             M, nt, j.final_scale);
+      return launch_status();
+    case Epi::kLseClamp:
+      if (md.out_f32)
+        finalize_lse_mish_kernel<float><<<grid_for(di, M, 256), 256, 0, st>>>(jb.stats, static_cast<float*>(j.C),
+                                                                              M, nt);
+      else
+        finalize_lse_mish_kernel<__half><<<grid_for(di, M, 256), 256, 0, st>>>(
+            jb.stats, static_cast<__half*>(j.C), M, nt);
+      return launch_status();
+    case Epi::kLnPre:
+      if (md.out_f32)
+        layernorm_finalize_kernel<float><<<grid_for(di, M, 8, 8), 256, 0, st>>>(
+            static_cast<float*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi), j.eps);
+      else
+        layernorm_finalize_kernel<__half><<<grid_for(di, M, 8, 8), 256, 0, st>>>(
+            static_cast<__half*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi), j.eps);
+      return launch_status();
+    case Epi::kSoftmaxPre:
+      if (md.out_f32)
+        softmax_finalize_kernel<float><<<grid_for(di, M, 8, 8), 256, 0, st>>>(static_cast<float*>(j.C), jb.stats,
+                                                                              M, N, nt);
+      else
+        softmax_finalize_kernel<__half><<<grid_for(di, M, 8, 8), 256, 0, st>>>(static_cast<__half*>(j.C),
+                                                                               jb.stats, M, N, nt);
+      return launch_status();
+    default:
+      return AKILI_OK;
+  }
+}
+
+size_t job_scratch_bytes(const GemmJob& j, const Mode& md) {
+  if (j.M == 0) return 0;
+  Carve c;
+  JobBuffers jb;
+  return layout_job(j, md, c, &jb);
+}
+
+template <class T>
+const void* P(T v) {
+  return reinterpret_cast<const void*>(static_cast<uintptr_t>(v));
+}
+template <class T>
+void* W(T v) {
+  return reinterpret_cast<void*>(static_cast<uintptr_t>(v));
+}
+const float* F(uint64_t v) { return reinterpret_cast<const float*>(static_cast<uintptr_t>(v)); }
+
+// ---------------------------------------------------------- job builders --
+// Each returns 0 and fills `j`, or an AKILI_E_* code.  No CUDA calls.
+
+int job_sgemm(const kbt_sgemm_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->b_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kPlain;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->b_addr); j.C = W(a->c_addr);
+  return AKILI_OK;
+}
+
+int job_add_relu(const kbt_gemm_add_relu_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kBiasRelu;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  return AKILI_OK;
+}
+
+int job_mul_leakyrelu(const kbt_gemm_mul_leakyrelu_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kBiasMulLeaky;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.s0 = a->multiplier; j.s1 = a->negative_slope;
+  return AKILI_OK;
+}
+
+int job_div_sum_scale(const kbt_gemm_div_sum_scale_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kRowSumHalf;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.C = W(a->c_addr);
+  j.final_scale = a->scaling_factor;
+  return AKILI_OK;
+}
+
+int job_layernorm(const kbt_gemm_layernorm_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->ln_w_addr, a->ln_b_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kLnPre;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.ln_w = F(a->ln_w_addr); j.ln_b = F(a->ln_b_addr); j.eps = a->eps;
+  return AKILI_OK;
+}
+
+int job_attention_score(const kbt_attention_score_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->D))) return rc;
+  if (chk && (rc = check_ptrs({a->q_addr, a->k_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kSoftmaxPre;
+  j.b_kmajor = true;
+  j.M = a->M; j.N = a->N; j.K = a->D;
+  j.A = P(a->q_addr); j.B0 = P(a->k_addr); j.C = W(a->c_addr);
+  j.s0 = 1.0f / sqrtf(static_cast<float>(a->D));  // kbt_attention_score/main.cpp:117
+  return AKILI_OK;
+}
+
+int job_matmul_softmax(const kbt_matmul_softmax_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->b_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kSoftmaxPre;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->b_addr); j.C = W(a->c_addr);
+  j.s0 = 1.0f;
+  return AKILI_OK;
+}
+
+int job_clamp(const kbt_matmul_scale_residadd_clamp_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && ((rc = check_ptrs({a->a_addr, a->b_addr, a->c_addr})) || (rc = check_opt_ptr(a->temp_addr)))) return rc;
+  j.epi = Epi::kLseClamp;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->b_addr); j.C = W(a->c_addr);
+  j.s0 = a->scale_factor; j.s1 = a->clamp_min; j.s2 = a->clamp_max;
+  // temp_addr is the reference's [M x N] fp32 scratch; it holds the partials.
+  j.stats_hint = W(a->temp_addr);
+  j.stats_hint_bytes = a->temp_addr ? static_cast<size_t>(a->M) * a->N * sizeof(float) : 0;
+  return AKILI_OK;
+}
+
+int job_sum_max_avgpool(const kbt_matmul_sum_max_avgpool_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kRowSumBias;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.final_scale = 1.0f;
+  return AKILI_OK;
+}
+
+int job_rmsnorm_swiglu(const kbt_gemm_rmsnorm_swiglu_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->x_addr, a->rms_w_addr, a->wg_addr, a->wu_addr, a->c_addr})) ||
+      (chk && ((rc = check_opt_ptr(a->norm_addr)) || (rc = check_opt_ptr(a->gate_addr)))))
+    return rc;
+  j.epi = Epi::kSwiglu;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->x_addr); j.B0 = P(a->wg_addr); j.B1 = P(a->wu_addr); j.C = W(a->c_addr);
+  j.rmsnorm = true; j.rms_w = F(a->rms_w_addr); j.eps = a->eps;
+  j.xhat_hint = W(a->norm_addr);  // the reference's [M x K] normalised-x scratch
+  return AKILI_OK;
+}
+
+int job_silu_mul(const kbt_gemm_silu_mul_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->wa_addr, a->ba_addr, a->wb_addr, a->bb_addr, a->c_addr})) ||
+      (chk && (rc = check_opt_ptr(a->gate_addr))))
+    return rc;
+  j.epi = Epi::kSiluMulBias;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->wa_addr); j.B1 = P(a->wb_addr); j.C = W(a->c_addr);
+  j.vec0 = F(a->ba_addr); j.vec1 = F(a->bb_addr);
+  return AKILI_OK;
+}
+
+// -------------------------------------------------------------- flash --
+struct FlashJob {
+  uint32_t seq_len = 0, head_dim = 0;
+  const void *Q = nullptr, *K = nullptr, *V = nullptr;
+  void* O = nullptr;
+};
+
+int job_flash(const flash_arg_t* a, FlashJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  if (a->seq_len == 0 || a->head_dim == 0 || (a->head_dim % 8)) return AKILI_E_SHAPE;
+  if (a->head_dim > 128) return AKILI_E_UNSUPPORTED;
+  int rc;
+  if (chk && (rc = check_ptrs({a->Q_addr, a->K_addr, a->V_addr, a->O_addr}))) return rc;
+  j.seq_len = a->seq_len; j.head_dim = a->head_dim;
+  j.Q = P(a->Q_addr); j.K = P(a->K_addr); j.V = P(a->V_addr); j.O = W(a->O_addr);
+  return AKILI_OK;
+}
+
+size_t flash_scratch_bytes(const FlashJob& j, const Mode& md) {
+  if (!md.in_f32) return 0;
+  const size_t n = static_cast<size_t>(md.batch) * md.heads * j.seq_len * j.head_dim;
+  Carve c;
+  c.need(n * 2); c.need(n * 2); c.need(n * 2);
+  return c.off;
+}
+
+int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const size_t n = static_cast<size_t>(md.batch) * md.heads * j.seq_len * j.head_dim;
+  const __half *q = static_cast<const __half*>(j.Q), *k = static_cast<const __half*>(j.K),
+               *v = static_cast<const __half*>(j.V);
+  if (md.in_f32) {
+    char* base = nullptr;
+    if ((rc = acquire_scratch(md, flash_scratch_bytes(j, md), st, &base))) return rc;
+    Carve cv;
+    cv.base = base;
+    __half* cq = static_cast<__half*>(cv.take(n * 2));
+    __half* ck = static_cast<__half*>(cv.take(n * 2));
+    __half* cvv = static_cast<__half*>(cv.take(n * 2));
+    if ((rc = cast_to_f16(di, static_cast<const float*>(j.Q), cq, n, st))) return rc;
+    if ((rc = cast_to_f16(di, static_cast<const float*>(j.K), ck, n, st))) return rc;
+    if ((rc = cast_to_f16(di, static_cast<const float*>(j.V), cvv, n, st))) return rc;
+    q = cq; k = ck; v = cvv;
+  }
+  const uint32_t bh = md.batch * md.heads;
+  const uint32_t D = j.head_dim;
+  const uint32_t dpad = D <= 64 ? 64 : 128;
+  CUtensorMap tq, tk, tv, to;
+  bool ok = map3d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 64, kFlashBM,
+                  CU_TENSOR_MAP_SWIZZLE_128B, 2) &&
+            map3d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 64, kFlashBN,
+                  CU_TENSOR_MAP_SWIZZLE_128B, 2) &&
+            map3d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 64, kFlashBN,
+                  CU_TENSOR_MAP_SWIZZLE_128B, 2);
+  if (md.out_f32)
+    ok = ok && map3d(&to, j.O, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D, j.seq_len, bh, 32, kFlashBM,
+                     CU_TENSOR_MAP_SWIZZLE_128B, 4);
+  else
+    ok = ok && map3d(&to, j.O, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 32, kFlashBM,
+                     CU_TENSOR_MAP_SWIZZLE_64B, 2);
+  if (!ok) return AKILI_E_LAUNCH;
+  FlashArgs fa;
+  fa.seq_len = static_cast<int>(j.seq_len);
+  fa.head_dim = static_cast<int>(D);
+  fa.scale_log2 = md.scale * 1.4426950408889634f;
+  dim3 grid((j.seq_len + kFlashBM - 1) / kFlashBM, bh);
+  if (dpad == 64) rc = launch_flash<64>(grid, md.out_f32, tq, tk, tv, to, fa, st);
+  else rc = launch_flash<128>(grid, md.out_f32, tq, tk, tv, to, fa, st);
+  if (rc == AKILI_OK) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return rc;
+}
+
+cudaStream_t S(akili_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+template <class Arg, int (*Build)(const Arg*, GemmJob&, bool)>
+int entry(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  if (!a) return AKILI_E_NULL_ARG;
+  GemmJob j;
+  // An empty batch (M == 0) is a no-op; its buffers may legitimately be null.
+  if ((rc = Build(a, j, a->M != 0))) return rc;
+  return run_job(j, md, S(s));
+}
+
+}  // namespace
+
+// ===================================================================== ABI ==
+extern "C" {
+
+#define AKILI_GEMM_ENTRY(name, T, build)                                                       \
+  int akili_##name(const T* a, akili_stream_t s) { return entry<T, build>(a, nullptr, s); }   \
+  int akili_##name##_ex(const T* a, const akili_ex_t* ex, akili_stream_t s) {                 \
+    if (!ex) return AKILI_E_NULL_ARG;                                                          \
+    return entry<T, build>(a, ex, s);                                                          \
+  }
+
+AKILI_GEMM_ENTRY(kbt_sgemm, kbt_sgemm_arg_t, job_sgemm)
+AKILI_GEMM_ENTRY(kbt_gemm_add_relu, kbt_gemm_add_relu_arg_t, job_add_relu)
+AKILI_GEMM_ENTRY(kbt_gemm_mul_leakyrelu, kbt_gemm_mul_leakyrelu_arg_t, job_mul_leakyrelu)
+AKILI_GEMM_ENTRY(kbt_gemm_div_sum_scale, kbt_gemm_div_sum_scale_arg_t, job_div_sum_scale)
+AKILI_GEMM_ENTRY(kbt_gemm_layernorm, kbt_gemm_layernorm_arg_t, job_layernorm)
+AKILI_GEMM_ENTRY(kbt_attention_score, kbt_attention_score_arg_t, job_attention_score)
+AKILI_GEMM_ENTRY(kbt_matmul_softmax, kbt_matmul_softmax_arg_t, job_matmul_softmax)
+AKILI_GEMM_ENTRY(kbt_matmul_scale_residadd_clamp, kbt_matmul_scale_residadd_clamp_arg_t, job_clamp)
+AKILI_GEMM_ENTRY(kbt_matmul_sum_max_avgpool, kbt_matmul_sum_max_avgpool_arg_t, job_sum_max_avgpool)
+AKILI_GEMM_ENTRY(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t, job_rmsnorm_swiglu)
+AKILI_GEMM_ENTRY(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t, job_silu_mul)
+#undef AKILI_GEMM_ENTRY
+
+int akili_flash_ex(const flash_arg_t* a, const akili_ex_t* ex, akili_stream_t s) {
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  FlashJob j;
+  if ((rc = job_flash(a, j))) return rc;
+  return run_flash(j, md, S(s));
+}
+int akili_flash(const flash_arg_t* a, akili_stream_t s) { return akili_flash_ex(a, nullptr, s); }
+
+const char* akili_strerror(int code) {
+  switch (code) {
+    case AKILI_OK: return "ok";
+    case AKILI_E_NULL_ARG: return "null argument block or buffer address";
+    case AKILI_E_SHAPE: return "invalid shape (sizes must be non-zero multiples of 8; M may be 0)";
+    case AKILI_E_ALIGN: return "buffer address not 16-byte aligned";
+    case AKILI_E_DTYPE: return "unsupported dtype";
+    case AKILI_E_UNSUPPORTED: return "unsupported option";
+    case AKILI_E_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case AKILI_E_ALLOC: return "scratch allocation failed";
+    case AKILI_E_LAUNCH: return "kernel launch or tensor-map encode failed";
+    case AKILI_E_DEVICE_TIMEOUT: return "a device-side wait timed out";
+    case AKILI_E_ABI: return "akili_ex_t.abi_version mismatch";
+    case AKILI_E_WORKSPACE: return "workspace smaller than required";
+    default: return "unknown error";
+  }
+}
+
+int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex, uint64_t* bytes) {
+  if (!op || !arg || !bytes) return AKILI_E_NULL_ARG;
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  md.workspace = nullptr;
+  GemmJob j;
+  const std::string name(op);
+#define AKILI_WS(nm, T, build) \
+  if (name == #nm) {           \
+    rc = build(static_cast<const T*>(arg), j, false); \
+    if (rc) return rc;         \
+    *bytes = job_scratch_bytes(j, md); \
+    return AKILI_OK;           \
+  }
+  AKILI_WS(kbt_sgemm, kbt_sgemm_arg_t, job_sgemm)
+  AKILI_WS(kbt_gemm_add_relu, kbt_gemm_add_relu_arg_t, job_add_relu)
+  AKILI_WS(kbt_gemm_mul_leakyrelu, kbt_gemm_mul_leakyrelu_arg_t, job_mul_leakyrelu)
+  AKILI_WS(kbt_gemm_div_sum_scale, kbt_gemm_div_sum_scale_arg_t, job_div_sum_scale)
+  AKILI_WS(kbt_gemm_layernorm, kbt_gemm_layernorm_arg_t, job_layernorm)
+  AKILI_WS(kbt_attention_score, kbt_attention_score_arg_t, job_attention_score)
+  AKILI_WS(kbt_matmul_softmax, kbt_matmul_softmax_arg_t, job_matmul_softmax)
+  AKILI_WS(kbt_matmul_scale_residadd_clamp, kbt_matmul_scale_residadd_clamp_arg_t, job_clamp)
+  AKILI_WS(kbt_matmul_sum_max_avgpool, kbt_matmul_sum_max_avgpool_arg_t, job_sum_max_avgpool)
+  AKILI_WS(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t, job_rmsnorm_swiglu)
+  AKILI_WS(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t, job_silu_mul)
+#undef AKILI_WS
+  if (name == "flash") {
+    FlashJob fj;
+    if ((rc = job_flash(static_cast<const flash_arg_t*>(arg), fj, false))) return rc;
+    *bytes = flash_scratch_bytes(fj, md);
+    return AKILI_OK;
+  }
+  return AKILI_E_UNSUPPORTED;
+}
+
+int akili_device_status(uint32_t* status, int clear) {
+  if (!status) return AKILI_E_NULL_ARG;
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_status, sizeof(v)) != cudaSuccess) return AKILI_E_LAUNCH;
+  *status = v;
+  if (clear) {
+    unsigned int z = 0;
+    if (cudaMemcpyToSymbol(g_status, &z, sizeof(z)) != cudaSuccess) return AKILI_E_LAUNCH;
+  }
+  return v ? AKILI_E_DEVICE_TIMEOUT : AKILI_OK;
+}
+
+uint64_t akili_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+uint32_t akili_abi_version(void) { return AKILI_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,244 @@
+// aux.cuh — the bandwidth-bound helpers around the tcgen05 GEMM:
+//   * fp32 -> fp16 operand conversion (the reference kernels' f2h, done once
+//     per operand instead of per tile load),
+//   * the RMSNorm pre-pass of kbt_gemm_rmsnorm_swiglu (writes fp16 x_hat, the
+//     operand the reference rounds at its GEMM load),
+//   * finalisers that merge per-(row, column-tile) partial statistics written
+//     by the GEMM epilogue: row sums, log-sum-exp + Mish, and the in-place
+//     LayerNorm / softmax normalisation passes.
+// All are grid-stride kernels sized to a multiple of the SM count; rows are
+// handled one warp each with 16-byte vector accesses.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "sm100.cuh"
+
+namespace akili {
+
+__global__ void cast_f32_to_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, size_t n) {
+  const size_t n8 = n / 8;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n8; i += stride) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src) + 2 * i);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 2 * i + 1);
+    uint4 q;
+    q.x = pack_half2(a.x, a.y);
+    q.y = pack_half2(a.z, a.w);
+    q.z = pack_half2(b.x, b.y);
+    q.w = pack_half2(b.z, b.w);
+    reinterpret_cast<uint4*>(dst)[i] = q;
+  }
+  for (size_t i = n8 * 8 + blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    dst[i] = __float2half_rn(src[i]);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// x_hat[i, k] = fp16( x[i,k] * (1 / sqrtf(sum_k x^2 / K + eps)) * w[k] )
+// (benchmarks/kbt_gemm_rmsnorm_swiglu/kernel.cpp:95-105, with the f2h of its
+// GEMM load, kernel.cpp:48, applied at the store).  One warp per row; K % 8 == 0.
+template <typename InT>
+__global__ void rmsnorm_prepass_kernel(const InT* __restrict__ x, const float* __restrict__ w,
+                                       __half* __restrict__ xhat, int M, int K, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    const InT* xr = x + static_cast<size_t>(row) * K;
+    float ss = 0.0f;
+    for (int k = lane * 8; k < K; k += 256) {
+      float f[8];
+      if constexpr (sizeof(InT) == 2) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + k));
+        const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 t = __half22float2(h[i]);
+          f[2 * i] = t.x;
+          f[2 * i + 1] = t.y;
+        }
+      } else {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k) + 1);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+    ss = warp_sum(ss);
+    const float inv_rms = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+    __half* out = xhat + static_cast<size_t>(row) * K;
+    for (int k = lane * 8; k < K; k += 256) {
+      float f[8];
+      if constexpr (sizeof(InT) == 2) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + k));
+        const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 t = __half22float2(h[i]);
+          f[2 * i] = t.x;
+          f[2 * i + 1] = t.y;
+        }
+      } else {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(xr + k));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(xr + k) + 1);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+      }
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + k));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + k) + 1);
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint4 q;
+      q.x = pack_half2(f[0] * inv_rms * ww[0], f[1] * inv_rms * ww[1]);
+      q.y = pack_half2(f[2] * inv_rms * ww[2], f[3] * inv_rms * ww[3]);
+      q.z = pack_half2(f[4] * inv_rms * ww[4], f[5] * inv_rms * ww[5]);
+      q.w = pack_half2(f[6] * inv_rms * ww[6], f[7] * inv_rms * ww[7]);
+      *reinterpret_cast<uint4*>(out + k) = q;
+    }
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store_scalar(OutT* p, float v) {
+  if constexpr (sizeof(OutT) == 2) *p = __float2half_rn(v);
+  else *p = v;
+}
+
+// out[i] = scale * sum_t ws[t][i]   (tiles summed in a fixed order: deterministic)
+template <typename OutT>
+__global__ void finalize_rowsum_kernel(const float* __restrict__ ws, OutT* __restrict__ out, int M, int ntiles,
+                                       float scale) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M; i += gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int t = 0; t < ntiles; ++t) s += ws[static_cast<size_t>(t) * M + i];
+    store_scalar(out + i, s * scale);
+  }
+}
+
+// Merge per-tile (max, sumexp) into the row's log-sum-exp and apply
+// out = lse * (lse * tanh(log(1 + exp(lse))))
+// (benchmarks/kbt_matmul_scale_residadd_clamp/main.cpp:145-151 semantics).
+template <typename OutT>
+__global__ void finalize_lse_mish_kernel(const float* __restrict__ ws, OutT* __restrict__ out, int M,
+                                         int ntiles) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M; i += gridDim.x * blockDim.x) {
+    float m = -INFINITY;
+    for (int t = 0; t < ntiles; ++t) m = fmaxf(m, ws[static_cast<size_t>(t) * M + i]);
+    float l = 0.0f;
+    const float* lt = ws + static_cast<size_t>(ntiles) * M;
+    for (int t = 0; t < ntiles; ++t) {
+      const float mt = ws[static_cast<size_t>(t) * M + i];
+      if (mt != -INFINITY) l += lt[static_cast<size_t>(t) * M + i] * expf(mt - m);
+    }
+    const float lse = m + logf(l);
+    const float mish = lse * tanhf(logf(1.0f + expf(lse)));
+    store_scalar(out + i, lse * mish);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint4 q = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    uint4 q;
+    q.x = pack_half2(f[0], f[1]);
+    q.y = pack_half2(f[2], f[3]);
+    q.z = pack_half2(f[4], f[5]);
+    q.w = pack_half2(f[6], f[7]);
+    *reinterpret_cast<uint4*>(p) = q;
+  } else {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+    *(reinterpret_cast<float4*>(p) + 1) = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+// In-place LayerNorm of the pre-normalised rows y = x.W + b written by the
+// GEMM epilogue.  Per-tile (mean, M2) partials over `tile_n` columns are
+// merged with Chan et al.'s pairwise formula; var = M2 / N (biased, as
+// benchmarks/kbt_gemm_layernorm/main.cpp:159-166); inv_std = 1/sqrtf(var+eps).
+template <typename T>
+__global__ void layernorm_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws,
+                                          const float* __restrict__ ln_w, const float* __restrict__ ln_b, int M,
+                                          int N, int ntiles, int tile_n, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    float n = 0.0f, mean = 0.0f, m2 = 0.0f;
+    for (int t = 0; t < ntiles; ++t) {
+      const float nt = static_cast<float>(min(tile_n, N - t * tile_n));
+      const float mt = ws[static_cast<size_t>(t) * M + row];
+      const float m2t = ws[static_cast<size_t>(ntiles + t) * M + row];
+      const float ntot = n + nt;
+      const float delta = mt - mean;
+      mean += delta * (nt / ntot);
+      m2 += m2t + delta * delta * (n * nt / ntot);
+      n = ntot;
+    }
+    const float var = m2 / static_cast<float>(N);
+    const float inv_std = 1.0f / sqrtf(var + eps);
+    T* cr = c + static_cast<size_t>(row) * N;
+    for (int j = lane * 8; j < N; j += 256) {
+      float f[8];
+      load8(cr + j, f);
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(ln_w + j));
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(ln_w + j) + 1);
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(ln_b + j));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(ln_b + j) + 1);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = ((f[i] - mean) * inv_std) * g[i] + b[i];
+      store8(cr + j, f);
+    }
+  }
+}
+
+// In-place softmax of the rows y written by the GEMM epilogue, from the
+// per-tile (max, sumexp) partials: out = expf(y - m) * (1 / l).
+template <typename T>
+__global__ void softmax_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws, int M, int N,
+                                        int ntiles) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    float m = -INFINITY;
+    for (int t = 0; t < ntiles; ++t) m = fmaxf(m, ws[static_cast<size_t>(t) * M + row]);
+    float l = 0.0f;
+    for (int t = 0; t < ntiles; ++t) {
+      const float mt = ws[static_cast<size_t>(t) * M + row];
+      if (mt != -INFINITY) l += ws[static_cast<size_t>(ntiles + t) * M + row] * expf(mt - m);
+    }
+    const float inv = 1.0f / l;
+    T* cr = c + static_cast<size_t>(row) * N;
+    for (int j = lane * 8; j < N; j += 256) {
+      float f[8];
+      load8(cr + j, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = expf(f[i] - m) * inv;
+      store8(cr + j, f);
+    }
+  }
+}
+
+}  // namespace akili

@@ -1,0 +1,446 @@
+// gemm.cuh — persistent, warp-specialised tcgen05 GEMM with fused epilogues,
+// the engine behind every kbt_* op.
+//
+//   C-tile[128 x BN] = A[128 x K] . B[K x BN]   (fp16 operands, fp32 in TMEM)
+//
+// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+//   warp 0      TMA producer: A tile (K-major, 128B swizzle) and B tile
+//               (W[K x N] row-major = MN-major B, or K-major B for Q.K^T)
+//               into a kStages-deep shared-memory ring (full/empty mbarriers).
+//   warp 1      allocates 512 TMEM columns (two 256-column accumulators) and
+//               issues tcgen05.mma (M=128, N=256 or 2 x N=128 for the dual
+//               GEMMs, K=16 per instruction) from one thread; tcgen05.commit
+//               frees ring slots and publishes finished accumulators.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one thread per
+//               output row), apply the op, and either stage the tile through
+//               swizzled shared memory for a TMA store (which also clips the
+//               M/N edges) or reduce it to per-row partial statistics.
+// The double-buffered accumulator lets the epilogue of tile i overlap the
+// main loop of tile i+1.  Tiles are visited in groups of 16 row-blocks so
+// the A and B panels in flight stay L2-resident.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "sm100.cuh"
+
+namespace akili {
+
+constexpr int kBM = 128;          // rows per tile (UMMA M)
+constexpr int kBK = 64;           // K per ring slot: 64 fp16 = one 128-byte swizzle row
+constexpr int kStages = 4;        // ring depth
+constexpr int kGemmThreads = 192; // 6 warps
+constexpr int kATileBytes = kBM * kBK * 2;       // 16 KB
+constexpr int kBTileBytes = 256 * kBK * 2;       // 32 KB (256 columns, or 2 x 128 for dual)
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kAccCols = 256;     // TMEM columns per accumulator buffer
+constexpr int kTmemCols = 512;
+constexpr int kGroupM = 16;       // tile raster: row-blocks per group
+
+enum class Epi : int {
+  kPlain = 0,        // C = acc                                   (kbt_sgemm)
+  kBiasRelu,         // C = max(acc + b, 0)                       (kbt_gemm_add_relu)
+  kBiasMulLeaky,     // v=(acc+b)*s0; C = v>=0 ? v : v*s1         (kbt_gemm_mul_leakyrelu)
+  kRowSumHalf,       // partial: sum_j acc*0.5                    (kbt_gemm_div_sum_scale)
+  kRowSumBias,       // partial: sum_j (acc + b)                  (kbt_matmul_sum_max_avgpool)
+  kLnPre,            // C = y = acc + b; partial (mean, M2)       (kbt_gemm_layernorm)
+  kSoftmaxPre,       // C = y = acc*s0; partial (max, sumexp)     (kbt_attention_score, kbt_matmul_softmax)
+  kLseClamp,         // t=clamp(2*(acc*s0)); partial (max, sumexp)(kbt_matmul_scale_residadd_clamp)
+  kSiluMulBias,      // dual: g=acc0+b0, u=acc1+b1, C=silu(g)*u   (kbt_gemm_silu_mul)
+  kSwiglu,           // dual: C = silu(acc0)*acc1                 (kbt_gemm_rmsnorm_swiglu)
+};
+
+__host__ __device__ constexpr bool epi_dual(Epi e) { return e == Epi::kSiluMulBias || e == Epi::kSwiglu; }
+__host__ __device__ constexpr bool epi_stores(Epi e) {
+  return !(e == Epi::kRowSumHalf || e == Epi::kRowSumBias || e == Epi::kLseClamp);
+}
+__host__ __device__ constexpr int epi_stats(Epi e) {
+  return (e == Epi::kRowSumHalf || e == Epi::kRowSumBias) ? 1
+         : (e == Epi::kLnPre || e == Epi::kSoftmaxPre || e == Epi::kLseClamp) ? 2
+                                                                              : 0;
+}
+// Output columns per tile.
+__host__ __device__ constexpr int epi_bn(Epi e) { return epi_dual(e) ? 128 : 256; }
+
+struct EpiArgs {
+  const float* vec0;  // per-column vector (bias / ba)
+  const float* vec1;  // per-column vector (bb)
+  float s0, s1, s2, s3;
+  float* row_ws;      // partial stats: [stat][n_tile][M]
+  int M, N, K;
+  int num_n_tiles;
+};
+
+__host__ __device__ inline int gemm_smem_bytes(bool stores, int out_bytes) {
+  int s = kStages * kStageBytes;
+  if (stores) s += 2 * kBM * 32 * out_bytes;
+  s += 256;   // barriers + TMEM address
+  s += 1024;  // alignment slack
+  return s;
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& m_blk, int& n_blk) {
+  const int per_group = kGroupM * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, num_m - first_m);
+  const int idx = tile - group * per_group;
+  m_blk = first_m + idx % gm;
+  n_blk = idx / gm;
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+template <typename OutT>
+__device__ __forceinline__ float round_out(float x) {
+  if constexpr (sizeof(OutT) == 2) return __half2float(__float2half_rn(x));
+  return x;
+}
+
+// Per-row running statistics of one tile.
+struct RowState {
+  float a, b, n;
+};
+
+template <Epi E, typename OutT>
+__device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvalid, float (&v)[32],
+                                          const float (&u)[32], RowState& st) {
+  if constexpr (E == Epi::kPlain) {
+    (void)u;
+  } else if constexpr (E == Epi::kBiasRelu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+      const float s = v[j] + b;
+      v[j] = s > 0.0f ? s : 0.0f;
+    }
+  } else if constexpr (E == Epi::kBiasMulLeaky) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+      const float val = (v[j] + b) * ea.s0;
+      v[j] = val >= 0.0f ? val : val * ea.s1;
+    }
+  } else if constexpr (E == Epi::kRowSumHalf) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s += (j < nvalid) ? v[j] * 0.5f : 0.0f;
+    st.a += s;
+  } else if constexpr (E == Epi::kRowSumBias) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) s += (j < nvalid) ? (v[j] + __ldg(ea.vec0 + col0 + j)) : 0.0f;
+    st.a += s;
+  } else if constexpr (E == Epi::kLnPre) {
+    // y = acc + b, rounded to the stored precision; chunk mean/M2 merged into
+    // the running (n, mean, M2) with Chan et al.'s pairwise update.
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+      v[j] = round_out<OutT>(v[j] + b);
+      sum += (j < nvalid) ? v[j] : 0.0f;
+    }
+    if (nvalid > 0) {
+      const float nc = static_cast<float>(nvalid);
+      const float mc = sum / nc;
+      float m2 = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float d = v[j] - mc;
+        m2 += (j < nvalid) ? d * d : 0.0f;
+      }
+      const float ntot = st.n + nc;
+      const float delta = mc - st.a;
+      st.a += delta * (nc / ntot);
+      st.b += m2 + delta * delta * (st.n * nc / ntot);
+      st.n = ntot;
+    }
+  } else if constexpr (E == Epi::kSoftmaxPre || E == Epi::kLseClamp) {
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float y;
+      if constexpr (E == Epi::kSoftmaxPre) {
+        y = round_out<OutT>(v[j] * ea.s0);
+      } else {
+        const float scaled = v[j] * ea.s0;
+        float t = scaled + scaled;
+        if (t < ea.s1) t = ea.s1;
+        if (t > ea.s2) t = ea.s2;
+        y = t;
+      }
+      v[j] = y;
+      if (j < nvalid) cmax = fmaxf(cmax, y);
+    }
+    if (nvalid > 0) {
+      const float mnew = fmaxf(st.a, cmax);
+      float l = (st.a == -INFINITY) ? 0.0f : st.b * expf(st.a - mnew);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) l += (j < nvalid) ? expf(v[j] - mnew) : 0.0f;
+      st.a = mnew;
+      st.b = l;
+    }
+  } else if constexpr (E == Epi::kSiluMulBias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const bool ok = j < nvalid;
+      const float g = v[j] + (ok ? __ldg(ea.vec0 + col0 + j) : 0.0f);
+      const float uu = u[j] + (ok ? __ldg(ea.vec1 + col0 + j) : 0.0f);
+      v[j] = silu(g) * uu;
+    }
+  } else if constexpr (E == Epi::kSwiglu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]) * u[j];
+  }
+}
+
+// Write this thread's 32 values (row r of the 128-row staging tile) in the
+// swizzle the TMA store map uses: 64-byte rows (fp16) with the 64B pattern,
+// 128-byte rows (fp32) with the 128B pattern.
+template <typename OutT>
+__device__ __forceinline__ void stage_row(uint8_t* stage, int r, const float (&v)[32]) {
+  if constexpr (sizeof(OutT) == 2) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 q;
+      q.x = pack_half2(v[8 * c + 0], v[8 * c + 1]);
+      q.y = pack_half2(v[8 * c + 2], v[8 * c + 3]);
+      q.z = pack_half2(v[8 * c + 4], v[8 * c + 5]);
+      q.w = pack_half2(v[8 * c + 6], v[8 * c + 7]);
+      const int phys = c ^ ((r >> 1) & 3);
+      *reinterpret_cast<uint4*>(stage + r * 64 + phys * 16) = q;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float4 q = make_float4(v[4 * c + 0], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+      const int phys = c ^ (r & 7);
+      *reinterpret_cast<float4*>(stage + r * 128 + phys * 16) = q;
+    }
+  }
+}
+
+template <Epi E, typename OutT, bool kBKMajor>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmC,
+                const EpiArgs ea) {
+  constexpr bool kDual = epi_dual(E);
+  constexpr bool kStore = epi_stores(E);
+  constexpr int kStats = epi_stats(E);
+  constexpr int BN = epi_bn(E);
+  constexpr int kOutBytes = sizeof(OutT);
+  constexpr int kStageOut = kBM * 32 * kOutBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* staging = ring + kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + (kStore ? 2 * kStageOut : 0));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* acc_full = bars + 2 * kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int M = ea.M, N = ea.N, K = ea.K;
+  const int num_m = (M + kBM - 1) / kBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB0);
+    if constexpr (kDual) tma_prefetch_desc(&tmB1);
+    if constexpr (kStore) tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int m_blk, n_blk;
+      tile_coords(tile, num_m, num_n, m_blk, n_blk);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (lane == 0) {
+          ok = mbar_wait(&empty[stage], phase ^ 1, kSiteProducerEmpty);
+          if (ok) {
+            uint8_t* sa = ring + stage * kStageBytes;
+            uint8_t* sb = sa + kATileBytes;
+            mbar_expect_tx(&full[stage], kStageBytes);
+            tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
+            if constexpr (kBKMajor) {
+              tma_load_2d(sb, &tmB0, &full[stage], kb * kBK, n_blk * BN);
+            } else if constexpr (kDual) {
+              tma_load_2d(sb, &tmB0, &full[stage], n_blk * BN, kb * kBK);
+              tma_load_2d(sb + 8192, &tmB0, &full[stage], n_blk * BN + 64, kb * kBK);
+              tma_load_2d(sb + 16384, &tmB1, &full[stage], n_blk * BN, kb * kBK);
+              tma_load_2d(sb + 24576, &tmB1, &full[stage], n_blk * BN + 64, kb * kBK);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                tma_load_2d(sb + q * 8192, &tmB0, &full[stage], n_blk * BN + q * 64, kb * kBK);
+            }
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    constexpr uint32_t idesc = kDual ? make_idesc_f16(kBM, 128, false, !kBKMajor)
+                                     : make_idesc_f16(kBM, 256, false, !kBKMajor);
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * kAccCols;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (lane == 0) ok = mbar_wait(&full[stage], phase, kSiteMmaFull);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = smem_u32(ring + stage * kStageBytes);
+          const uint32_t sb = sa + kATileBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
+            const uint32_t accum = (kb | k) != 0;
+            if constexpr (kBKMajor) {
+              umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
+            } else if constexpr (kDual) {
+              umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+              umma_f16_ss(d_tmem + 128, ad, make_sdesc(sb + 16384 + k * 2048, 8192, 1024, kSw128), idesc,
+                          accum);
+            } else {
+              umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+            }
+          }
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&acc_full[acc]);
+      __syncwarp();
+    }
+    // Drain: every issued MMA has completed before TMEM is released.
+    if (lane == 0) {
+      umma_commit(drain);
+      mbar_wait(drain, 0, kSiteDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ep_tid = threadIdx.x - 64;          // 0..127
+    const int wq = static_cast<int>(warp & 3);    // TMEM lane quarter this warp may access
+    const int r = wq * 32 + static_cast<int>(lane);
+    int it = 0;
+    int chunk_ctr = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      int m_blk, n_blk;
+      tile_coords(tile, num_m, num_n, m_blk, n_blk);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, kSiteEpiAccFull)) *abort_flag = 1;
+      named_bar_sync(1, 128);
+      if (*abort_flag) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
+      const int n0 = n_blk * BN;
+      const int row = m_blk * kBM + r;
+      const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
+      RowState st;
+      st.a = (kStats == 2 && E != Epi::kLnPre) ? -INFINITY : 0.0f;
+      st.b = 0.0f;
+      st.n = 0.0f;
+      for (int c = 0; c < nchunks; ++c) {
+        float v[32];
+        float u[32];
+        tmem_ld32(tbase + c * 32, v);
+        if constexpr (kDual) tmem_ld32(tbase + 128 + c * 32, u);
+        const int col0 = n0 + c * 32;
+        const int nvalid = min(32, N - col0);
+        epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
+        if constexpr (kStore) {
+          uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
+          if (ep_tid == 0) bulk_wait_read<1>();
+          named_bar_sync(1, 128);
+          stage_row<OutT>(stg, r, v);
+          fence_async_shared();
+          named_bar_sync(1, 128);
+          if (ep_tid == 0) {
+            tma_store_2d(&tmC, stg, col0, m_blk * kBM);
+            bulk_commit();
+          }
+          ++chunk_ctr;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if constexpr (kStats > 0) {
+        if (row < M) {
+          float* ws = ea.row_ws;
+          const size_t plane = static_cast<size_t>(ea.num_n_tiles) * M;
+          ws[static_cast<size_t>(n_blk) * M + row] = st.a;
+          if constexpr (kStats == 2) ws[plane + static_cast<size_t>(n_blk) * M + row] = st.b;
+        }
+      }
+    }
+    if constexpr (kStore) {
+      if (ep_tid == 0) bulk_wait<0>();
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace akili

@@ -1,0 +1,213 @@
+// vortex_shim.cpp — the Vortex runtime API (include/vortex.h) on a B200.
+//
+// akili-bench's harnesses (benchmarks/<bench>/main.cpp) drive a device only
+// through this API: allocate buffers, copy inputs, upload a kernel image and
+// the kernel_arg_t bytes, start, wait, copy back.  Here
+//   vx_mem_alloc / vx_mem_address   cudaMalloc; the "device address" is the
+//                                   CUDA pointer, so the harness writes real
+//                                   device pointers into its kernel_arg_t;
+//   vx_upload_kernel_file           selects the op: a file whose text starts
+//                                   with "akili:<bench>" names it, otherwise
+//                                   AKILI_OP, otherwise the executable's name
+//                                   (the reference builds each harness as
+//                                   benchmarks/<bench>/<bench>);
+//   vx_upload_bytes                 keeps the argument block on the host;
+//   vx_start                        akili_<bench>(arg, default stream);
+//   vx_ready_wait                   stream synchronise, then the library's
+//                                   device status word (a timed-out device
+//                                   wait becomes a non-zero return).
+// vx_dev_caps reports the configuration the reference recorded its results
+// on (README.md:349-368: 8 threads, 4 warps, 1 core) so the harnesses'
+// launch-hint arithmetic stays unchanged; the B200 kernels ignore those hints.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "akili.h"
+#include "vortex.h"
+
+extern "C" char* program_invocation_short_name;
+
+namespace {
+
+struct Buf {
+  void* dptr = nullptr;
+  uint64_t size = 0;
+  std::vector<unsigned char> host;  // argument blocks and kernel "images"
+  std::string op;
+};
+
+struct Dev {
+  std::string op;
+  std::vector<unsigned char> args;
+  int last_rc = 0;
+};
+
+std::string resolve_op(const char* filename) {
+  if (filename) {
+    if (FILE* f = std::fopen(filename, "rb")) {
+      char head[128] = {0};
+      size_t n = std::fread(head, 1, sizeof(head) - 1, f);
+      std::fclose(f);
+      std::string s(head, n);
+      if (s.rfind("akili:", 0) == 0) {
+        std::string op = s.substr(6);
+        op.erase(op.find_last_not_of(" \r\n\t") + 1);
+        return op;
+      }
+    }
+  }
+  if (const char* e = std::getenv("AKILI_OP")) return e;
+  return program_invocation_short_name ? program_invocation_short_name : "";
+}
+
+int dispatch(const std::string& op, const void* a) {
+#define AKILI_DISPATCH(name, T) \
+  if (op == #name) return akili_##name(static_cast<const T*>(a), nullptr);
+  AKILI_DISPATCH(kbt_sgemm, kbt_sgemm_arg_t)
+  AKILI_DISPATCH(kbt_gemm_add_relu, kbt_gemm_add_relu_arg_t)
+  AKILI_DISPATCH(kbt_gemm_mul_leakyrelu, kbt_gemm_mul_leakyrelu_arg_t)
+  AKILI_DISPATCH(kbt_gemm_div_sum_scale, kbt_gemm_div_sum_scale_arg_t)
+  AKILI_DISPATCH(kbt_gemm_layernorm, kbt_gemm_layernorm_arg_t)
+  AKILI_DISPATCH(kbt_attention_score, kbt_attention_score_arg_t)
+  AKILI_DISPATCH(kbt_matmul_softmax, kbt_matmul_softmax_arg_t)
+  AKILI_DISPATCH(kbt_matmul_scale_residadd_clamp, kbt_matmul_scale_residadd_clamp_arg_t)
+  AKILI_DISPATCH(kbt_matmul_sum_max_avgpool, kbt_matmul_sum_max_avgpool_arg_t)
+  AKILI_DISPATCH(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t)
+  AKILI_DISPATCH(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t)
+  AKILI_DISPATCH(flash, flash_arg_t)
+#undef AKILI_DISPATCH
+  std::fprintf(stderr, "akili vortex shim: no akili op named '%s'\n", op.c_str());
+  return AKILI_E_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vx_dev_open(vx_device_h* hdevice) {
+  if (!hdevice) return -1;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return -1;
+  *hdevice = new Dev;
+  return 0;
+}
+
+int vx_dev_close(vx_device_h hdevice) {
+  delete static_cast<Dev*>(hdevice);
+  return 0;
+}
+
+int vx_dev_caps(vx_device_h, uint32_t caps_id, uint64_t* value) {
+  if (!value) return -1;
+  switch (caps_id) {
+    case VX_CAPS_NUM_THREADS: *value = 8; return 0;
+    case VX_CAPS_NUM_WARPS: *value = 4; return 0;
+    case VX_CAPS_NUM_CORES: *value = 1; return 0;
+    case VX_CAPS_CACHE_LINE_SIZE: *value = 128; return 0;
+    case VX_CAPS_LOCAL_MEM_SIZE: *value = 16384; return 0;
+    case VX_CAPS_GLOBAL_MEM_SIZE: {
+      size_t fr = 0, tot = 0;
+      cudaMemGetInfo(&fr, &tot);
+      *value = tot;
+      return 0;
+    }
+    default: *value = 0; return 0;
+  }
+}
+
+int vx_mem_alloc(vx_device_h, uint64_t size, int, vx_buffer_h* hbuffer) {
+  if (!hbuffer) return -1;
+  auto* b = new Buf;
+  b->size = size;
+  if (cudaMalloc(&b->dptr, size ? size : 1) != cudaSuccess) {
+    delete b;
+    return -1;
+  }
+  *hbuffer = b;
+  return 0;
+}
+
+int vx_mem_free(vx_buffer_h hbuffer) {
+  auto* b = static_cast<Buf*>(hbuffer);
+  if (!b) return 0;
+  if (b->dptr) cudaFree(b->dptr);
+  delete b;
+  return 0;
+}
+
+int vx_mem_address(vx_buffer_h hbuffer, uint64_t* address) {
+  auto* b = static_cast<Buf*>(hbuffer);
+  if (!b || !address) return -1;
+  *address = reinterpret_cast<uint64_t>(b->dptr);
+  return 0;
+}
+
+int vx_copy_to_dev(vx_buffer_h hbuffer, const void* host_ptr, uint64_t off, uint64_t size) {
+  auto* b = static_cast<Buf*>(hbuffer);
+  if (!b || !b->dptr || off + size > b->size) return -1;
+  return cudaMemcpy(static_cast<char*>(b->dptr) + off, host_ptr, size, cudaMemcpyHostToDevice) == cudaSuccess ? 0
+                                                                                                               : -1;
+}
+
+int vx_copy_from_dev(void* host_ptr, vx_buffer_h hbuffer, uint64_t off, uint64_t size) {
+  auto* b = static_cast<Buf*>(hbuffer);
+  if (!b || !b->dptr || off + size > b->size) return -1;
+  return cudaMemcpy(host_ptr, static_cast<char*>(b->dptr) + off, size, cudaMemcpyDeviceToHost) == cudaSuccess ? 0
+                                                                                                               : -1;
+}
+
+int vx_upload_kernel_file(vx_device_h hdevice, const char* filename, vx_buffer_h* hbuffer) {
+  auto* d = static_cast<Dev*>(hdevice);
+  if (!d || !hbuffer) return -1;
+  auto* b = new Buf;
+  b->op = resolve_op(filename);
+  d->op = b->op;
+  *hbuffer = b;
+  return 0;
+}
+
+int vx_upload_bytes(vx_device_h hdevice, const void* content, uint64_t size, vx_buffer_h* hbuffer) {
+  auto* d = static_cast<Dev*>(hdevice);
+  if (!d || !hbuffer || !content) return -1;
+  auto* b = new Buf;
+  b->host.assign(static_cast<const unsigned char*>(content), static_cast<const unsigned char*>(content) + size);
+  d->args = b->host;
+  *hbuffer = b;
+  return 0;
+}
+
+int vx_start(vx_device_h hdevice, vx_buffer_h hkernel, vx_buffer_h harguments) {
+  auto* d = static_cast<Dev*>(hdevice);
+  auto* k = static_cast<Buf*>(hkernel);
+  auto* a = static_cast<Buf*>(harguments);
+  if (!d || !k || !a || a->host.empty()) return -1;
+  d->last_rc = dispatch(k->op, a->host.data());
+  if (d->last_rc != AKILI_OK)
+    std::fprintf(stderr, "akili_%s: %s\n", k->op.c_str(), akili_strerror(d->last_rc));
+  return d->last_rc == AKILI_OK ? 0 : -1;
+}
+
+int vx_ready_wait(vx_device_h hdevice, uint64_t) {
+  auto* d = static_cast<Dev*>(hdevice);
+  if (!d) return -1;
+  if (d->last_rc != AKILI_OK) return -1;
+  uint32_t status = 0;
+  const int rc = akili_device_status(&status, 1);  // synchronises the device
+  if (rc != AKILI_OK) {
+    std::fprintf(stderr, "akili device status: %s (0x%x)\n", akili_strerror(rc), status);
+    return -1;
+  }
+  return 0;
+}
+
+int vx_check_occupancy(vx_device_h, uint32_t, uint32_t* max_localmem) {
+  if (max_localmem) *max_localmem = 227 * 1024;
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,218 @@
+"""torch front end of the C ABI: one function per akili-bench op.
+
+Each function fills the op's reference ``kernel_arg_t`` (abi.OPS) with the
+device addresses of CUDA tensors and calls ``akili_<bench>`` (fp32 tensors,
+reference semantics) or ``akili_<bench>_ex`` (fp16 inputs and/or fp16
+output).  The CUDA path is the only path: a missing library or a non-zero
+status raises.  Shapes follow the reference: x/a [M, K], W [K, N] row-major,
+per-column vectors fp32 [N]; attention-score K is [N, D]; flash tensors are
+[B, H, S, D] (or [S, D] for one head).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import abi
+
+
+def _stream(stream) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def _addr(t: torch.Tensor | None) -> int:
+    if t is None:
+        return 0
+    assert t.is_cuda and t.is_contiguous(), "akili ops take contiguous CUDA tensors"
+    return int(t.data_ptr())
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == torch.float16:
+        return abi.DTYPE_F16
+    if t.dtype == torch.float32:
+        return abi.DTYPE_F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _launch(op: str, arg, in_t: torch.Tensor, out_t: torch.Tensor, stream=None, ex_extra=None,
+            workspace: torch.Tensor | None = None) -> None:
+    plain = in_t.dtype == torch.float32 and out_t.dtype == torch.float32 and not ex_extra and workspace is None
+    ex = None
+    if not plain:
+        ex = abi.make_ex(_dt(in_t), _dt(out_t), **(ex_extra or {}))
+        if workspace is not None:
+            ex.workspace = _addr(workspace)
+            ex.workspace_bytes = workspace.numel() * workspace.element_size()
+    abi.check(op, arg, ex, _stream(stream))
+
+
+def _hdr(st, M, N, K, kname="K"):
+    a = st()
+    a.grid_dim[0] = (M + 7) // 8
+    a.grid_dim[1] = a.grid_dim[2] = 1
+    a.block_dim[0] = 8
+    a.block_dim[1] = a.block_dim[2] = 1
+    a.M, a.N = M, N
+    setattr(a, kname, K)
+    return a
+
+
+def _out(x, M, N, out_dtype, out):
+    if out is not None:
+        return out
+    shape = (M, N) if N is not None else (M,)
+    return torch.empty(shape, device=x.device, dtype=out_dtype or x.dtype)
+
+
+def kbt_sgemm(a, b, out=None, out_dtype=None, stream=None):
+    M, K = a.shape
+    N = b.shape[1]
+    c = _out(a, M, N, out_dtype or torch.float32, out)
+    arg = _hdr(abi.KbtSgemmArg, M, N, K)
+    arg.a_addr, arg.b_addr, arg.c_addr = _addr(a), _addr(b), _addr(c)
+    _launch("kbt_sgemm", arg, a, c, stream)
+    return c
+
+
+def kbt_gemm_add_relu(x, w, bias, out=None, out_dtype=None, stream=None, workspace=None):
+    M, K = x.shape
+    N = w.shape[1]
+    c = _out(x, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtGemmAddReluArg, M, N, K)
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _addr(x), _addr(w), _addr(bias), _addr(c)
+    _launch("kbt_gemm_add_relu", arg, x, c, stream, workspace=workspace)
+    return c
+
+
+def kbt_gemm_mul_leakyrelu(x, w, bias, multiplier=1.5, negative_slope=0.01, out=None, out_dtype=None,
+                           stream=None):
+    M, K = x.shape
+    N = w.shape[1]
+    c = _out(x, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtGemmMulLeakyreluArg, M, N, K)
+    arg.multiplier, arg.negative_slope = multiplier, negative_slope
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _addr(x), _addr(w), _addr(bias), _addr(c)
+    _launch("kbt_gemm_mul_leakyrelu", arg, x, c, stream)
+    return c
+
+
+def kbt_gemm_div_sum_scale(x, w, scaling_factor=2.0, out=None, out_dtype=torch.float32, stream=None):
+    M, K = x.shape
+    N = w.shape[1]
+    c = _out(x, M, None, out_dtype, out)
+    arg = _hdr(abi.KbtGemmDivSumScaleArg, M, N, K)
+    arg.scaling_factor = scaling_factor
+    arg.a_addr, arg.w_addr, arg.c_addr = _addr(x), _addr(w), _addr(c)
+    _launch("kbt_gemm_div_sum_scale", arg, x, c, stream)
+    return c
+
+
+def kbt_gemm_layernorm(x, w, bias, ln_w, ln_b, eps=1e-5, out=None, out_dtype=None, stream=None, workspace=None):
+    M, K = x.shape
+    N = w.shape[1]
+    c = _out(x, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtGemmLayernormArg, M, N, K)
+    arg.eps = eps
+    arg.a_addr, arg.w_addr, arg.bias_addr = _addr(x), _addr(w), _addr(bias)
+    arg.ln_w_addr, arg.ln_b_addr, arg.c_addr = _addr(ln_w), _addr(ln_b), _addr(c)
+    _launch("kbt_gemm_layernorm", arg, x, c, stream, workspace=workspace)
+    return c
+
+
+def kbt_attention_score(q, k, out=None, out_dtype=None, stream=None):
+    M, D = q.shape
+    N = k.shape[0]
+    c = _out(q, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtAttentionScoreArg, M, N, D, kname="D")
+    arg.q_addr, arg.k_addr, arg.c_addr = _addr(q), _addr(k), _addr(c)
+    _launch("kbt_attention_score", arg, q, c, stream)
+    return c
+
+
+def kbt_matmul_softmax(a, b, out=None, out_dtype=None, stream=None):
+    M, K = a.shape
+    N = b.shape[1]
+    c = _out(a, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtMatmulSoftmaxArg, M, N, K)
+    arg.a_addr, arg.b_addr, arg.c_addr = _addr(a), _addr(b), _addr(c)
+    _launch("kbt_matmul_softmax", arg, a, c, stream)
+    return c
+
+
+def kbt_matmul_scale_residadd_clamp(a, b, scale_factor=0.5, clamp_min=-2.0, clamp_max=2.0, temp=None, out=None,
+                                    out_dtype=torch.float32, stream=None):
+    M, K = a.shape
+    N = b.shape[1]
+    c = _out(a, M, None, out_dtype, out)
+    arg = _hdr(abi.KbtMatmulScaleResidaddClampArg, M, N, K)
+    arg.scale_factor, arg.clamp_min, arg.clamp_max = scale_factor, clamp_min, clamp_max
+    arg.a_addr, arg.b_addr, arg.c_addr, arg.temp_addr = _addr(a), _addr(b), _addr(c), _addr(temp)
+    _launch("kbt_matmul_scale_residadd_clamp", arg, a, c, stream)
+    return c
+
+
+def kbt_matmul_sum_max_avgpool(x, w, bias, out=None, out_dtype=torch.float32, stream=None):
+    M, K = x.shape
+    N = w.shape[1]
+    c = _out(x, M, None, out_dtype, out)
+    arg = _hdr(abi.KbtMatmulSumMaxAvgpoolArg, M, N, K)
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _addr(x), _addr(w), _addr(bias), _addr(c)
+    _launch("kbt_matmul_sum_max_avgpool", arg, x, c, stream)
+    return c
+
+
+def kbt_gemm_rmsnorm_swiglu(x, rms_w, wg, wu, eps=1e-5, norm=None, out=None, out_dtype=None, stream=None):
+    M, K = x.shape
+    N = wg.shape[1]
+    c = _out(x, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtGemmRmsnormSwigluArg, M, N, K)
+    arg.eps = eps
+    arg.x_addr, arg.rms_w_addr, arg.wg_addr, arg.wu_addr = _addr(x), _addr(rms_w), _addr(wg), _addr(wu)
+    arg.norm_addr, arg.gate_addr, arg.c_addr = _addr(norm), 0, _addr(c)
+    _launch("kbt_gemm_rmsnorm_swiglu", arg, x, c, stream)
+    return c
+
+
+def kbt_gemm_silu_mul(x, wa, ba, wb, bb, out=None, out_dtype=None, stream=None):
+    M, K = x.shape
+    N = wa.shape[1]
+    c = _out(x, M, N, out_dtype, out)
+    arg = _hdr(abi.KbtGemmSiluMulArg, M, N, K)
+    arg.a_addr, arg.wa_addr, arg.ba_addr = _addr(x), _addr(wa), _addr(ba)
+    arg.wb_addr, arg.bb_addr, arg.gate_addr, arg.c_addr = _addr(wb), _addr(bb), 0, _addr(c)
+    _launch("kbt_gemm_silu_mul", arg, x, c, stream)
+    return c
+
+
+def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None):
+    """q/k/v [S, D] (one head, reference layout) or [B, H, S, D]."""
+    if q.dim() == 2:
+        B, H, (S, D) = 1, 1, q.shape
+    else:
+        B, H, S, D = q.shape
+    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=out_dtype or q.dtype)
+    arg = abi.FlashArg()
+    arg.grid_dim[0] = (S + 7) // 8
+    arg.block_dim[0] = 8
+    arg.kernel_type = 1
+    arg.seq_len, arg.head_dim = S, D
+    arg.block_size_r = arg.block_size_c = 8
+    arg.Q_addr, arg.K_addr, arg.V_addr, arg.O_addr = _addr(q), _addr(k), _addr(v), _addr(o)
+    extra = None
+    if B * H != 1 or softmax_scale is not None:
+        extra = {"batch": B, "heads": H, "softmax_scale": float(softmax_scale or 0.0)}
+    _launch("flash", arg, q, o, stream, ex_extra=extra)
+    return o
+
+
+def launch_count() -> int:
+    return int(abi.load().akili_launch_count())
+
+
+def device_status(clear: bool = True) -> int:
+    v = C.c_uint32(0)
+    abi.load().akili_device_status(C.byref(v), 1 if clear else 0)
+    return int(v.value)
