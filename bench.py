@@ -240,7 +240,7 @@ def reference_arm(args):
     threads = host_threads()
     rng = np.random.default_rng(42)
     M, N, K = 8192, 4096, 4096
-    rows_per_step = max(threads, 8)
+    rows_per_step = min(M, max(8, threads * 4))
     x = rng.standard_normal((rows_per_step, K), dtype=np.float32).astype(np.float16).astype(np.float32)
     w = (rng.standard_normal((K, N), dtype=np.float32) * K ** -0.5).astype(np.float16).astype(np.float32)
     b = (rng.standard_normal(N, dtype=np.float32) * 0.1).astype(np.float32)
@@ -273,7 +273,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from akili_bench_b200 import ops
+    from akili_bench_b200 import ops, shard
     from akili_bench_b200.parity import parity
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -371,31 +371,18 @@ def run_ours(args):
         # --- verification: sampled rows all-gathered to rank 0, checked against the oracle ---
         check = None
         if name == "kbt_gemm_add_relu":
-            sample = torch.tensor([0, 1, 4095, 8191], device="cuda")
-            rows_out = out.index_select(0, sample).float()
-            rows_x = d["x"].index_select(0, sample).float()
-            if world > 1:
-                go = [torch.empty_like(rows_out) for _ in range(world)]
-                gx = [torch.empty_like(rows_x) for _ in range(world)]
-                dist.all_gather(go, rows_out)
-                dist.all_gather(gx, rows_x)
-            else:
-                go, gx = [rows_out], [rows_x]
+            sample = torch.tensor(shard.sample_rows(out.shape[0]), device="cuda")
+            outs, ins = shard.gather_rows([out.index_select(0, sample).float(),
+                                           d["x"].index_select(0, sample).float()], world)
             if rank == 0:
                 sys.path.insert(0, os.path.join(ROOT, "oracle"))
                 import oracle_py
                 w_h = d["w"].float().cpu().numpy()
                 b_h = d["b"].float().cpu().numpy()
-                worst = None
-                for r in range(world):
-                    xr = gx[r].cpu().numpy()
-                    ref = oracle_py.kbt_gemm_add_relu(np.ascontiguousarray(xr), w_h, b_h, xr.shape[0], w_h.shape[1],
-                                                      w_h.shape[0], threads=4)
-                    p = parity(go[r].cpu().numpy(), ref)
-                    if worst is None or not p["ok"] or p["min_cos"] < worst["min_cos"]:
-                        worst = p
-                check = {"rows_checked": 4 * world, "ok": worst["ok"], "max_err_frac": worst["err_frac"],
-                         "min_row_cos": worst["min_cos"]}
+                worst = shard.check_gathered(outs, ins, lambda xr: oracle_py.kbt_gemm_add_relu(
+                    np.ascontiguousarray(xr), w_h, b_h, xr.shape[0], w_h.shape[1], w_h.shape[0], threads=4), parity)
+                check = {"rows_checked": len(sample) * world, "ok": worst["ok"], "max_err_frac": worst["err_frac"],
+                         "min_row_cos": worst["min_cos"], "gather": "all_gather" if world > 1 else "local"}
 
         # --- roofline of the dominant kernel ---
         if wl.bound == "tensor":
@@ -434,7 +421,7 @@ def run_ours(args):
         for name, line, d in results:
             if world == 1 and name == "kbt_gemm_add_relu" and not args.no_cpu:
                 threads = host_threads()
-                rows = max(8, threads * args.cpu_rows_per_thread)
+                rows = min(8192, max(8, threads * args.cpu_rows_per_thread))
                 dh = {"x": d["x"][:rows].float().cpu().numpy(), "w": d["w"].float().cpu().numpy(),
                       "b": d["b"].float().cpu().numpy()}
                 _, dt, fl = cpu_sample(name, dh, rows, threads)
