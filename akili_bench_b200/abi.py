@@ -31,6 +31,8 @@ E_LAUNCH = -8
 E_DEVICE_TIMEOUT = -9
 E_ABI = -10
 E_WORKSPACE = -11
+E_SCRATCH_LIMIT = -12
+NOALLOC_SCRATCH_BYTES = 4 << 20
 
 _u32, _u64, _f = C.c_uint32, C.c_uint64, C.c_float
 _HDR = [("grid_dim", _u32 * 3), ("block_dim", _u32 * 3), ("M", _u32), ("N", _u32), ("K", _u32)]
@@ -133,6 +135,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         fx = getattr(L, f"akili_{name}_ex")
         fx.argtypes = [C.POINTER(st), C.POINTER(AkiliEx), C.c_void_p]
         fx.restype = C.c_int
+    L.akili_kbt_gemm_layernorm_noalloc.argtypes = [C.POINTER(KbtGemmLayernormArg), C.POINTER(AkiliEx), C.c_void_p]
+    L.akili_kbt_gemm_layernorm_noalloc.restype = C.c_int
     L.akili_strerror.argtypes = [C.c_int]
     L.akili_strerror.restype = C.c_char_p
     L.akili_workspace_bytes.argtypes = [C.c_char_p, C.c_void_p, C.POINTER(AkiliEx), C.POINTER(C.c_uint64)]

@@ -706,6 +706,38 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
 
 cudaStream_t S(akili_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// ------------------------------------------------- no-alloc LayerNorm scratch --
+// Fixed device scratch of akili_kbt_gemm_layernorm_noalloc: the per-(row,
+// 256-column tile) (mean, M2) partials its GEMM epilogue writes and its
+// finaliser reads.  Every slot the finaliser reads is written earlier in the
+// same call, so nothing needs clearing between calls; concurrent calls race.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[AKILI_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch for the current device.  In host code
+// the array's name is only a host-side stand-in; the kernel must be given the
+// address cudaGetSymbolAddress returns, looked up once per device.
+int noalloc_scratch_ptr(void** out) {
+  static std::mutex mu;
+  static std::map<int, void*> addr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return AKILI_E_NO_DEVICE;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  auto it = addr.find(dev);
+  if (it == addr.end()) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return AKILI_E_LAUNCH;
+    }
+    it = addr.emplace(dev, p).first;
+  }
+  *out = it->second;
+  return AKILI_OK;
+}
+
 template <class Arg, int (*Build)(const Arg*, GemmJob&, bool)>
 int entry(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
   Mode md;
@@ -743,6 +775,29 @@ AKILI_GEMM_ENTRY(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t, job_rms
 AKILI_GEMM_ENTRY(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t, job_silu_mul)
 #undef AKILI_GEMM_ENTRY
 
+// kbt_gemm_layernorm with its scratch in g_noalloc_scratch: no cudaMalloc,
+// cudaFree or other device allocation on any path (fp16 operands need no
+// converted copies; the caller-workspace and internal-pool paths are unused).
+int akili_kbt_gemm_layernorm_noalloc(const kbt_gemm_layernorm_arg_t* a, const akili_ex_t* ex,
+                                     akili_stream_t s) {
+  if (!ex) return AKILI_E_NULL_ARG;
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  if (md.in_f32) return AKILI_E_DTYPE;
+  if (md.workspace) return AKILI_E_UNSUPPORTED;
+  if (!a) return AKILI_E_NULL_ARG;
+  GemmJob j;
+  if ((rc = job_layernorm(a, j, a->M != 0))) return rc;
+  if (j.M == 0) return AKILI_OK;
+  if (stats_bytes(j) > AKILI_NOALLOC_SCRATCH_BYTES) return AKILI_E_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch_ptr(&scratch))) return rc;
+  md.workspace = scratch;
+  md.workspace_bytes = AKILI_NOALLOC_SCRATCH_BYTES;
+  return run_job(j, md, S(s));
+}
+
 int akili_flash_ex(const flash_arg_t* a, const akili_ex_t* ex, akili_stream_t s) {
   Mode md;
   int rc = parse_ex(ex, &md);
@@ -767,6 +822,7 @@ const char* akili_strerror(int code) {
     case AKILI_E_DEVICE_TIMEOUT: return "a device-side wait timed out";
     case AKILI_E_ABI: return "akili_ex_t.abi_version mismatch";
     case AKILI_E_WORKSPACE: return "workspace smaller than required";
+    case AKILI_E_SCRATCH_LIMIT: return "problem exceeds the fixed no-alloc scratch (AKILI_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown error";
   }
 }

@@ -61,6 +61,7 @@ typedef struct CUstream_st* akili_stream_t;
 #define AKILI_E_DEVICE_TIMEOUT   (-9)  /* a device-side wait ran out (see device status)    */
 #define AKILI_E_ABI             (-10)  /* ex->abi_version != AKILI_ABI_VERSION              */
 #define AKILI_E_WORKSPACE       (-11)  /* ex->workspace given but smaller than required     */
+#define AKILI_E_SCRATCH_LIMIT   (-12)  /* problem needs more than the fixed no-alloc scratch */
 
 #define AKILI_DTYPE_F32 0u
 #define AKILI_DTYPE_F16 1u
@@ -217,6 +218,27 @@ int akili_kbt_gemm_div_sum_scale_ex(const kbt_gemm_div_sum_scale_arg_t* arg, con
 /* kbt_gemm_layernorm/main.cpp:136-140, kernel.cpp:24-113 */
 int akili_kbt_gemm_layernorm(const kbt_gemm_layernorm_arg_t* arg, akili_stream_t stream);
 int akili_kbt_gemm_layernorm_ex(const kbt_gemm_layernorm_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* No counterpart in the reference: a form of kbt_gemm_layernorm that never
+ * allocates device memory, for callers that cannot call cudaMalloc — e.g. a
+ * serving process whose allocator has already reserved the GPU's memory, or
+ * a plugin host whose execute callback must not allocate because cudaMalloc /
+ * cudaFree would synchronise the device in the middle of its stream work.
+ * The caller passes inputs and outputs as for akili_kbt_gemm_layernorm_ex;
+ * operands must be fp16 (ex->in_dtype = AKILI_DTYPE_F16, output fp16 or
+ * fp32) and ex->workspace must be 0.  The only scratch, the per-row LayerNorm
+ * partial statistics, lives in a fixed device array of
+ * AKILI_NOALLOC_SCRATCH_BYTES inside the library (held by every GPU that
+ * loads it until exit); a problem needing more, i.e.
+ * 8 * M * ceil(N / 256) bytes > AKILI_NOALLOC_SCRATCH_BYTES, returns
+ * AKILI_E_SCRATCH_LIMIT.  The first call on a device looks up that array's
+ * device address (once per device, with the device current); make that first
+ * call before any stream capture.  All calls share the array: calls that
+ * overlap on the GPU (different streams, or different host threads on one
+ * device) race on it and must be serialised by the caller. */
+#define AKILI_NOALLOC_SCRATCH_BYTES (4u << 20)
+int akili_kbt_gemm_layernorm_noalloc(const kbt_gemm_layernorm_arg_t* arg, const akili_ex_t* ex,
+                                     akili_stream_t stream);
 
 /* kbt_attention_score/main.cpp:107-111, kernel.cpp:25-113 */
 int akili_kbt_attention_score(const kbt_attention_score_arg_t* arg, akili_stream_t stream);
