@@ -68,6 +68,17 @@ class Workload:
         self.bound, self.io_bytes, self.host, self.cpu, self.kernel = bound, io_bytes, host, cpu, kernel
 
 
+class Gens:
+    """Seeded generators: `w` for weights and per-column vectors (identical on
+    every rank: replicated parameters), `x` for activations (per-rank shard)."""
+
+    def __init__(self, torch, rank: int):
+        self.w = torch.Generator(device="cuda")
+        self.w.manual_seed(1234)
+        self.x = torch.Generator(device="cuda")
+        self.x.manual_seed(99991 + 7919 * rank)
+
+
 def _rand(torch, gen, shape, std=1.0, mean=0.0, dtype=None):
     t = torch.randn(shape, generator=gen, device="cuda", dtype=torch.float32) * std + mean
     return t.to(dtype) if dtype is not None else t
@@ -79,11 +90,11 @@ def workloads(torch, ops):
 
     def gemm_inputs(M, N, K, bias_std=0.1, dual=False):
         def make(gen):
-            d = {"x": _rand(torch, gen, (M, K), dtype=f16), "w": _rand(torch, gen, (K, N), K ** -0.5, dtype=f16),
-                 "b": _rand(torch, gen, (N,), bias_std)}
+            d = {"x": _rand(torch, gen.x, (M, K), dtype=f16), "w": _rand(torch, gen.w, (K, N), K ** -0.5, dtype=f16),
+                 "b": _rand(torch, gen.w, (N,), bias_std)}
             if dual:
-                d["w2"] = _rand(torch, gen, (K, N), K ** -0.5, dtype=f16)
-                d["b2"] = _rand(torch, gen, (N,), bias_std)
+                d["w2"] = _rand(torch, gen.w, (K, N), K ** -0.5, dtype=f16)
+                d["b2"] = _rand(torch, gen.w, (N,), bias_std)
             return d
         return make
 
@@ -113,8 +124,8 @@ def workloads(torch, ops):
 
     def ln_make(gen):
         d = gemm_inputs(M3, N2, K2, 0.02)(gen)
-        d["g"] = _rand(torch, gen, (N2,), 0.02, 1.0)
-        d["beta"] = _rand(torch, gen, (N2,), 0.02)
+        d["g"] = _rand(torch, gen.w, (N2,), 0.02, 1.0)
+        d["beta"] = _rand(torch, gen.w, (N2,), 0.02)
         return d
     W["kbt_gemm_layernorm"] = Workload(
         "kbt_gemm_layernorm", {"M": M3, "N": N2, "K": K2}, 2.0 * M3 * N2 * K2, ln_make,
@@ -124,9 +135,9 @@ def workloads(torch, ops):
     N4 = 11008
 
     def sw_make(gen):
-        return {"x": _rand(torch, gen, (M3, K2), dtype=f16), "rw": _rand(torch, gen, (K2,), 0.02, 1.0),
-                "wg": _rand(torch, gen, (K2, N4), K2 ** -0.5, dtype=f16),
-                "wu": _rand(torch, gen, (K2, N4), K2 ** -0.5, dtype=f16),
+        return {"x": _rand(torch, gen.x, (M3, K2), dtype=f16), "rw": _rand(torch, gen.w, (K2,), 0.02, 1.0),
+                "wg": _rand(torch, gen.w, (K2, N4), K2 ** -0.5, dtype=f16),
+                "wu": _rand(torch, gen.w, (K2, N4), K2 ** -0.5, dtype=f16),
                 "norm": torch.empty((M3, K2), device="cuda", dtype=f16)}
     W["kbt_gemm_rmsnorm_swiglu"] = Workload(
         "kbt_gemm_rmsnorm_swiglu", {"M": M3, "N": N4, "K": K2}, 4.0 * M3 * N4 * K2, sw_make,
@@ -139,15 +150,15 @@ def workloads(torch, ops):
     Ma, Na, Da = 16384, 4096, 128
 
     def as_make(gen):
-        return {"q": _rand(torch, gen, (Ma, Da), dtype=f16), "k": _rand(torch, gen, (Na, Da), dtype=f16)}
+        return {"q": _rand(torch, gen.x, (Ma, Da), dtype=f16), "k": _rand(torch, gen.w, (Na, Da), dtype=f16)}
     W["kbt_attention_score"] = Workload(
         "kbt_attention_score", {"M": Ma, "N": Na, "D": Da}, 2.0 * Ma * Na * Da, as_make,
         lambda d, out, st: ops.kbt_attention_score(d["q"], d["k"], out=out, stream=st), bound="hbm",
         io_bytes=2.0 * (Ma * Da + Na * Da) + 2.0 * Ma * Na)
 
     def sg_make(gen):
-        return {"a": (torch.rand((128, 128), generator=gen, device="cuda") * 2 - 1).to(f16),
-                "bm": (torch.rand((128, 128), generator=gen, device="cuda") * 2 - 1).to(f16)}
+        return {"a": (torch.rand((128, 128), generator=gen.x, device="cuda") * 2 - 1).to(f16),
+                "bm": (torch.rand((128, 128), generator=gen.w, device="cuda") * 2 - 1).to(f16)}
     W["kbt_sgemm"] = Workload(
         "kbt_sgemm", {"M": 128, "N": 128, "K": 128}, 2.0 * 128 ** 3, sg_make,
         lambda d, out, st: ops.kbt_sgemm(d["a"], d["bm"], out=out, out_dtype=f32, stream=st))
@@ -155,7 +166,7 @@ def workloads(torch, ops):
     B, H, S, D = 8, 32, 4096, 128
 
     def fl_make(gen):
-        return {k: _rand(torch, gen, (B, H, S, D), dtype=f16) for k in ("q", "k", "v")}
+        return {k: _rand(torch, gen.x, (B, H, S, D), dtype=f16) for k in ("q", "k", "v")}
     W["flash"] = Workload(
         "flash", {"batch": B, "heads": H, "seq": S, "head_dim": D, "causal": False}, 4.0 * B * H * S * S * D,
         fl_make, lambda d, out, st: ops.flash(d["q"], d["k"], d["v"], softmax_scale=D ** -0.5, out=out, stream=st),
@@ -171,8 +182,8 @@ class ClockSampler:
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, index):
+        self.index = index  # nvidia-smi --id: a UUID ("GPU-...") or an index
         self.proc = None
 
     def __enter__(self):
@@ -297,9 +308,7 @@ def run_ours(args):
     results = []
     for name in names:
         wl = W[name]
-        gen = torch.Generator(device="cuda")
-        gen.manual_seed(1234 + 7919 * rank)
-        d = wl.make(gen)
+        d = wl.make(Gens(torch, rank))
         out = wl.call(d, None, None)  # allocates the output
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
@@ -319,7 +328,11 @@ def run_ours(args):
                     wl.call(d, out, stream)
                 torch.cuda.synchronize()
 
-        with ClockSampler(local) as clk:
+        try:
+            gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+        except Exception:
+            gpu_id = str(local)
+        with ClockSampler(gpu_id) as clk:
             soak(args.soak)
             torch.cuda.synchronize()
             barrier()
@@ -439,6 +452,11 @@ def run_ours(args):
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+    # A throughput number over wrong results is not a result: fail loudly.
+    bad = [name for name, line, _ in results if line.get("check") and not line["check"]["ok"]]
+    if bad:
+        print(f"verification failed for {bad}", file=sys.stderr)
+        return 3
     return 0
 
 
