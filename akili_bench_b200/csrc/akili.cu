@@ -697,7 +697,7 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
   fa.seq_len = static_cast<int>(j.seq_len);
   fa.head_dim = static_cast<int>(D);
   fa.scale_log2 = md.scale * 1.4426950408889634f;
-  dim3 grid((j.seq_len + kFlashBM - 1) / kFlashBM, bh);
+  dim3 grid((j.seq_len + kFlashBM * kFlashQTiles - 1) / (kFlashBM * kFlashQTiles), bh);
   if (dpad == 64) rc = launch_flash<64>(grid, md.out_f32, tq, tk, tv, to, fa, st);
   else rc = launch_flash<128>(grid, md.out_f32, tq, tk, tv, to, fa, st);
   if (rc == AKILI_OK) g_launches.fetch_add(1, std::memory_order_relaxed);

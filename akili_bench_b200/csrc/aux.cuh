@@ -119,7 +119,8 @@ __global__ void finalize_rowsum_kernel(const float* __restrict__ ws, OutT* __res
   }
 }
 
-// Merge per-tile (max, sumexp) into the row's log-sum-exp and apply
+// Merge per-tile (max, sumexp) partials — kept in the log2 domain by the GEMM
+// epilogue — into the row's natural log-sum-exp and apply
 // out = lse * (lse * tanh(log(1 + exp(lse))))
 // (benchmarks/kbt_matmul_scale_residadd_clamp/main.cpp:145-151 semantics).
 template <typename OutT>
@@ -132,9 +133,9 @@ __global__ void finalize_lse_mish_kernel(const float* __restrict__ ws, OutT* __r
     const float* lt = ws + static_cast<size_t>(ntiles) * M;
     for (int t = 0; t < ntiles; ++t) {
       const float mt = ws[static_cast<size_t>(t) * M + i];
-      if (mt != -INFINITY) l += lt[static_cast<size_t>(t) * M + i] * expf(mt - m);
+      if (mt != -INFINITY) l += lt[static_cast<size_t>(t) * M + i] * exp2f(mt - m);
     }
-    const float lse = m + logf(l);
+    const float lse = (m + log2f(l)) * 0.6931471805599453f;
     const float mish = lse * tanhf(logf(1.0f + expf(lse)));
     store_scalar(out + i, lse * mish);
   }
@@ -215,7 +216,8 @@ __global__ void layernorm_finalize_kernel(T* __restrict__ c, const float* __rest
 }
 
 // In-place softmax of the rows y written by the GEMM epilogue, from the
-// per-tile (max, sumexp) partials: out = expf(y - m) * (1 / l).
+// per-tile (max, sumexp) partials in the log2 domain:
+// out = exp2(y * log2 e - m2) * (1 / l).
 template <typename T>
 __global__ void softmax_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws, int M, int N,
                                         int ntiles) {
@@ -227,15 +229,16 @@ __global__ void softmax_finalize_kernel(T* __restrict__ c, const float* __restri
     float l = 0.0f;
     for (int t = 0; t < ntiles; ++t) {
       const float mt = ws[static_cast<size_t>(t) * M + row];
-      if (mt != -INFINITY) l += ws[static_cast<size_t>(ntiles + t) * M + row] * expf(mt - m);
+      if (mt != -INFINITY) l += ws[static_cast<size_t>(ntiles + t) * M + row] * exp2f(mt - m);
     }
     const float inv = 1.0f / l;
+    constexpr float kLog2e = 1.4426950408889634f;
     T* cr = c + static_cast<size_t>(row) * N;
     for (int j = lane * 8; j < N; j += 256) {
       float f[8];
       load8(cr + j, f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = expf(f[i] - m) * inv;
+      for (int i = 0; i < 8; ++i) f[i] = exp2f(fmaf(f[i], kLog2e, -m)) * inv;
       store8(cr + j, f);
     }
   }

@@ -3,22 +3,28 @@
 //
 //   O[bh, i, :] = sum_j softmax_j(scale * Q[bh,i,:].K[bh,j,:]) V[bh, j, :]
 //
-// One CTA per (128-query tile, batch*head).  192 threads:
-//   warp 0      TMA: the Q tile once, then K_j / V_j tiles (128 keys) into a
-//               two-deep ring.
-//   warp 1      TMEM owner and MMA issuer:  S_j = Q.K_j^T into one of two
-//               128-column TMEM buffers, then O += P_j.V_j into a TMEM
-//               accumulator (S_{j+1} is issued before O += P_j.V_j so the
-//               tensor core works on the next scores while softmax runs).
-//   warps 2..5  one thread per query row: read S_j from TMEM, online softmax
-//               in base 2 (exp2 of scale*log2(e)*s - m), write P_j as fp16 to
-//               a 128B-swizzled shared tile (the A operand of the P.V MMA),
-//               and rescale the O row in TMEM only when its running max
-//               grows by more than 2^8 (the stale max cancels in O / l).
-//               Finally O / l is staged in shared memory and TMA-stored.
-// The score matrix never touches HBM.  Head dims up to 64 use a 64-column
-// padded tile, up to 128 a 128-column tile; TMA zero-fills the padding and
-// the key tail, and keys >= seq_len are masked to -inf.
+// One CTA per (256 queries = two 128-row Q tiles, batch*head), 320 threads:
+//   warp 0      TMA: both Q tiles once, then K_j and V_j (128 keys each)
+//               into two-deep K and V rings.
+//   warp 1      TMEM owner and MMA issuer.  Per key block j and Q tile t:
+//                 O_t += P_t,j-1 . V_j-1   (A = P from TMEM, B = V, MN-major)
+//                 S_t,j  = Q_t . K_j^T     (into the columns P_t,j-1 occupied)
+//               Issued in that order on one thread, the MMAs run in order, so
+//               S may overwrite P once the P.V that reads it is ahead of it.
+//   warps 2..5  softmax of Q tile 0; warps 6..9 softmax of Q tile 1 (one
+//               thread per query row).  While one tile's softmax runs, the
+//               tensor core works on the other tile.  Per block: read S_t,j
+//               from TMEM (scores never leave the chip), take the row max in
+//               the log2 domain, write P = exp2(scale*log2e*s - m) as packed
+//               fp16 back into the first 64 columns of S_t, and rescale O_t
+//               in TMEM only when the running max grows by more than 2^8
+//               (the stale max cancels in O / l).  S_t,j being complete
+//               implies O_t += P_t,j-1 V_j-1 is complete, so the rescale
+//               never races the accumulation.
+// Finally each softmax group divides its O rows by l, stages them through
+// swizzled shared memory (the drained K ring) and TMA-stores them.  Head dims
+// up to 64 use a 64-column tile, up to 128 a 128-column tile; TMA zero-fills
+// the padding and the key tail; keys >= seq_len are masked to -inf.
 #pragma once
 #include <cuda_fp16.h>
 
@@ -28,9 +34,10 @@
 
 namespace akili {
 
-constexpr int kFlashBM = 128;  // query rows per CTA
-constexpr int kFlashBN = 128;  // keys per step
-constexpr int kFlashThreads = 192;
+constexpr int kFlashBM = 128;  // query rows per Q tile (two tiles per CTA)
+constexpr int kFlashBN = 128;  // keys per block
+constexpr int kFlashQTiles = 2;
+constexpr int kFlashThreads = 64 + 128 * kFlashQTiles;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct FlashArgs {
@@ -41,15 +48,15 @@ struct FlashArgs {
 
 template <int DP>
 struct FlashSmem {
-  static constexpr int kQ = kFlashBM * DP * 2;
-  static constexpr int kKV = kFlashBN * DP * 2;
-  static constexpr int kP = kFlashBM * kFlashBN * 2;
+  static constexpr int kQ = kFlashBM * DP * 2;   // one Q tile
+  static constexpr int kKV = kFlashBN * DP * 2;  // one K or V block
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQ;
+  static constexpr int kKOff = kQOff + kFlashQTiles * kQ;
   static constexpr int kVOff = kKOff + 2 * kKV;
-  static constexpr int kPOff = kVOff + 2 * kKV;
-  static constexpr int kBarOff = kPOff + kP;
+  static constexpr int kBarOff = kVOff + 2 * kKV;
   static constexpr int kBytes = kBarOff + 256 + 1024;
+  // the output staging of both softmax groups reuses the drained K/V rings
+  static_assert(2 * 2 * kFlashBM * 32 * 4 <= 4 * kKV, "staging must fit in the K/V rings");
 };
 
 template <int DP, typename OutT>
@@ -58,33 +65,31 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                      const FlashArgs fa) {
   using L = FlashSmem<DP>;
-  constexpr int kChunks = DP / 64;              // 64-column swizzle chunks of Q/K/V
-  constexpr int kOutBytes = sizeof(OutT);
-  constexpr int kStageOut = kFlashBM * 32 * kOutBytes;
-  constexpr uint32_t kColS0 = 0, kColO = 256;
+  constexpr int kChunks = DP / 64;  // 64-column swizzle chunks of Q/K/V
+  constexpr int kStageOut = kFlashBM * 32 * sizeof(OutT);
+  constexpr uint32_t kColO = 256;   // O_t at 256 + 128 t; S_t / P_t at 128 t
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQOff;
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
-  uint8_t* sP = smem + L::kPOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_free = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* pv_done = bars + 12;
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  uint64_t* k_empty = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per Q tile
+  uint64_t* p_full = bars + 11;   // [2] per Q tile
+  uint64_t* o_done = bars + 13;   // [2] per Q tile
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);  // [2]
 
   const int N = fa.seq_len;
   const int nkv = (N + kFlashBN - 1) / kFlashBN;
-  const int m0 = blockIdx.x * kFlashBM;
+  const int m0 = blockIdx.x * (kFlashBM * kFlashQTiles);
   const int bh = blockIdx.y;
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -94,14 +99,15 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_done[s], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    abort_flag[0] = 0;
+    abort_flag[1] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -121,15 +127,18 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ loads
     if (lane == 0) {
-      mbar_expect_tx(q_full, L::kQ);
-      for (int q = 0; q < kChunks; ++q) tma_load_3d(sQ + q * 16384, &tmQ, q_full, q * 64, m0, bh);
+      mbar_expect_tx(q_full, kFlashQTiles * L::kQ);
+      for (int t = 0; t < kFlashQTiles; ++t)
+        for (int q = 0; q < kChunks; ++q)
+          tma_load_3d(sQ + t * L::kQ + q * 16384, &tmQ, q_full, q * 64, m0 + t * kFlashBM, bh);
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, kSiteFlashFree)) break;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, kSiteFlashFree)) break;
         mbar_expect_tx(&k_full[st], L::kKV);
         for (int q = 0; q < kChunks; ++q)
           tma_load_3d(sK + st * L::kKV + q * 16384, &tmK, &k_full[st], q * 64, j * kFlashBN, bh);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, kSiteFlashFree)) break;
         mbar_expect_tx(&v_full[st], L::kKV);
         for (int q = 0; q < kChunks; ++q)
           tma_load_3d(sV + st * L::kKV + q * 16384, &tmV, &v_full[st], q * 64, j * kFlashBN, bh);
@@ -141,95 +150,98 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     constexpr uint32_t idesc_s = make_idesc_f16(kFlashBM, kFlashBN, false, false);  // K-major K
     constexpr uint32_t idesc_o = make_idesc_f16(kFlashBM, DP, false, true);         // MN-major V
     bool ok = true;
-    if (lane == 0) ok = mbar_wait(q_full, 0, kSiteFlashQ);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    const uint32_t q_addr = smem_u32(sQ);
-    const uint32_t p_addr = smem_u32(sP);
-    auto issue_pv = [&](int jj) -> bool {
-      const int st = jj & 1;
-      bool good = true;
-      if (lane == 0) {
-        good = mbar_wait(p_full, jj & 1, kSiteFlashP) && mbar_wait(&v_full[st], (jj >> 1) & 1, kSiteFlashKV);
-        if (good) {
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + st * L::kKV);
-#pragma unroll
-          for (int k = 0; k < kFlashBN / 16; ++k) {
-            const uint64_t ad = make_sdesc(p_addr + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024, kSw128);
-            const uint64_t bd = make_sdesc(v_addr + k * 2048, 16384, 1024, kSw128);
-            umma_f16_ss(tmem + kColO, ad, bd, idesc_o, (jj | k) != 0);
-          }
-          umma_commit(pv_done);
-          umma_commit(&kv_empty[st]);
-        }
-      }
-      return __shfl_sync(0xffffffffu, good, 0);
-    };
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int st = j & 1;
-      if (lane == 0) {
-        ok = mbar_wait(&k_full[st], (j >> 1) & 1, kSiteFlashKV) &&
-             mbar_wait(&s_free[st], ((j >> 1) & 1) ^ 1, kSiteFlashS);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * L::kKV);
-#pragma unroll
-          for (int k = 0; k < DP / 16; ++k) {
-            const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-            umma_f16_ss(tmem + kColS0 + st * kFlashBN, make_sdesc(q_addr + off, 16, 1024, kSw128),
-                        make_sdesc(k_addr + off, 16, 1024, kSw128), idesc_s, k != 0);
-          }
-          umma_commit(&s_full[st]);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok && j >= 1) ok = issue_pv(j - 1);
-    }
-    if (ok && nkv >= 1) issue_pv(nkv - 1);
     if (lane == 0) {
+      ok = mbar_wait(q_full, 0, kSiteFlashQ);
+      // O_t += P_t,jj . V_jj for both tiles, then release V_jj's slot.
+      auto issue_pv = [&](int jj, int t) -> bool {
+        if (!mbar_wait(&p_full[t], jj & 1, kSiteFlashP)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (jj & 1) * L::kKV);
+#pragma unroll
+        for (int k = 0; k < kFlashBN / 16; ++k)
+          umma_f16_ts(tmem + kColO + t * 128, tmem + t * 128 + k * 8,
+                      make_sdesc(v_addr + k * 2048, 16384, 1024, kSw128), idesc_o, (jj | k) != 0);
+        return true;
+      };
+      const uint32_t q_addr = smem_u32(sQ);
+      for (int j = 0; j <= nkv && ok; ++j) {
+        const int st = j & 1;
+        if (j < nkv) ok = mbar_wait(&k_full[st], (j >> 1) & 1, kSiteFlashKV);
+        if (ok && j >= 1) ok = mbar_wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1, kSiteFlashKV);
+        for (int t = 0; t < kFlashQTiles && ok; ++t) {
+          if (j >= 1) {
+            ok = issue_pv(j - 1, t);
+            if (!ok) break;
+            if (j == nkv) umma_commit(&o_done[t]);
+          }
+          if (j < nkv) {
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sK + st * L::kKV);
+#pragma unroll
+            for (int k = 0; k < DP / 16; ++k) {
+              const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+              umma_f16_ss(tmem + t * 128, make_sdesc(q_addr + t * L::kQ + off, 16, 1024, kSw128),
+                          make_sdesc(k_addr + off, 16, 1024, kSw128), idesc_s, k != 0);
+            }
+            umma_commit(&s_full[t]);
+          }
+        }
+        if (!ok) break;
+        if (j >= 1) umma_commit(&v_empty[(j - 1) & 1]);
+        if (j < nkv) umma_commit(&k_empty[st]);
+      }
       umma_commit(drain);
       mbar_wait(drain, 0, kSiteDrain);
     }
     __syncwarp();
   } else {
     // --------------------------------------------------- softmax / output
-    const int ep_tid = threadIdx.x - 64;
-    const int wq = static_cast<int>(warp & 3);
+    const int grp = (static_cast<int>(warp) - 2) >> 2;  // Q tile of this warpgroup
+    const int ep_tid = threadIdx.x - 64 - 128 * grp;    // 0..127 within the group
+    const int wq = static_cast<int>(warp & 3);          // TMEM lane quarter
     const int r = wq * 32 + static_cast<int>(lane);
+    const uint32_t bar_id = 1 + grp;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    float m_use = -INFINITY;  // max used for exponentiation (log2 domain)
+    const uint32_t tS = tmem + lane_off + grp * 128;
+    const uint32_t tO = tmem + lane_off + kColO + grp * 128;
+    const float sl = fa.scale_log2;
+    float m_use = -INFINITY;
     float l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, kSiteFlashS)) *abort_flag = 1;
-      named_bar_sync(1, 128);
-      if (*abort_flag) {
+      if (!mbar_wait(&s_full[grp], j & 1, kSiteFlashS)) abort_flag[grp] = 1;
+      named_bar_sync(bar_id, 128);
+      if (abort_flag[grp]) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t[32];
-        tmem_ld32(tmem + lane_off + kColS0 + sb * kFlashBN + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-      }
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      // scale into the log2 domain and mask keys past the end
       const int kv0 = j * kFlashBN;
+      // One wide TMEM load of the 128 scores of this row, then the row max in
+      // the log2 domain (keys past the end are masked).
+      float s[128];
+      tmem_ld128(tS, s);
       float rmax = -INFINITY;
+      const int nvalid = N - kv0;  // >= 1
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        s[i] = (kv0 + i < N) ? s[i] * fa.scale_log2 : -INFINITY;
+        s[i] = (i < nvalid) ? s[i] * sl : -INFINITY;
         rmax = fmaxf(rmax, s[i]);
       }
       const bool grow = rmax > m_use + kRescaleThreshold;
       const float m_new = grow ? rmax : m_use;
-      const float alpha = grow ? exp2f(m_use - m_new) : 1.0f;  // exp2(-inf) = 0 on the first block
+      const float alpha = grow ? exp2f(m_use - m_new) : 1.0f;  // 0 on the first block
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+        for (int c = 0; c < DP / 32; ++c) {
+          float o[32];
+          tmem_ld32(tO + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      // P = exp2(s - m) as packed fp16 into the first 64 columns of S (one store).
       float rsum = 0.0f;
       uint32_t pk[64];
 #pragma unroll
@@ -239,63 +251,35 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
         rsum += p0 + p1;
         pk[i] = pack_half2(p0, p1);
       }
-      // PV_{j-1} must be done: the P tile is reused and O is about to be rescaled.
-      if (j >= 1) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, kSiteFlashPV)) *abort_flag = 1;
-        named_bar_sync(1, 128);
-        if (*abort_flag) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, grow)) {
-#pragma unroll 1
-          for (int c = 0; c < DP / 32; ++c) {
-            float o[32];
-            tmem_ld32(tmem + lane_off + kColO + c * 32, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tmem + lane_off + kColO + c * 32, o);
-          }
-        }
-      }
-      // P_j -> shared memory, K-major with the 128B swizzle (two 64-key chunks)
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int chunk = u >> 3, unit = u & 7;
-        uint4 q;
-        q.x = pk[4 * u + 0];
-        q.y = pk[4 * u + 1];
-        q.z = pk[4 * u + 2];
-        q.w = pk[4 * u + 3];
-        *reinterpret_cast<uint4*>(sP + chunk * 16384 + r * 128 + ((unit ^ (r & 7)) * 16)) = q;
-      }
-      fence_async_shared();
+      tmem_st64(tS, pk);
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[grp]);
       l = l * alpha + rsum;
       m_use = m_new;
     }
     if (ok && nkv >= 1) {
-      if (!mbar_wait(pv_done, (nkv - 1) & 1, kSiteFlashPV)) *abort_flag = 1;
-      named_bar_sync(1, 128);
-      if (!*abort_flag) {
+      if (!mbar_wait(&o_done[grp], 0, kSiteFlashPV)) abort_flag[grp] = 1;
+      named_bar_sync(bar_id, 128);
+      if (!abort_flag[grp]) {
         tc_fence_after();
         const float inv_l = 1.0f / l;
+        // Staging: each group takes its own 2 x kStageOut span of the K/V rings,
+        // drained once o_done fires (both groups fit in the 4 ring slots).
+        uint8_t* stg_base = sK + grp * 2 * kStageOut;
         const int ncols = (fa.head_dim + 31) / 32;
         for (int c = 0; c < ncols; ++c) {
           float o[32];
-          tmem_ld32(tmem + lane_off + kColO + c * 32, o);
+          tmem_ld32(tO + c * 32, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= inv_l;
-          uint8_t* stg = sP + (c & 1) * kStageOut;
+          uint8_t* stg = stg_base + (c & 1) * kStageOut;
           if (ep_tid == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);
+          named_bar_sync(bar_id, 128);
           stage_row<OutT>(stg, r, o);
           fence_async_shared();
-          named_bar_sync(1, 128);
+          named_bar_sync(bar_id, 128);
           if (ep_tid == 0) {
-            tma_store_3d(&tmO, stg, c * 32, m0, bh);
+            tma_store_3d(&tmO, stg, c * 32, m0 + grp * kFlashBM, bh);
             bulk_commit();
           }
         }

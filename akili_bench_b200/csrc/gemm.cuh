@@ -43,8 +43,8 @@ enum class Epi : int {
   kRowSumHalf,       // partial: sum_j acc*0.5                    (kbt_gemm_div_sum_scale)
   kRowSumBias,       // partial: sum_j (acc + b)                  (kbt_matmul_sum_max_avgpool)
   kLnPre,            // C = y = acc + b; partial (mean, M2)       (kbt_gemm_layernorm)
-  kSoftmaxPre,       // C = y = acc*s0; partial (max, sumexp)     (kbt_attention_score, kbt_matmul_softmax)
-  kLseClamp,         // t=clamp(2*(acc*s0)); partial (max, sumexp)(kbt_matmul_scale_residadd_clamp)
+  kSoftmaxPre,       // C = y = acc*s0; partial (max, sumexp), log2 domain   (kbt_attention_score, kbt_matmul_softmax)
+  kLseClamp,         // t=clamp(2*(acc*s0)); partial (max, sumexp), log2 domain (kbt_matmul_scale_residadd_clamp)
   kSiluMulBias,      // dual: g=acc0+b0, u=acc1+b1, C=silu(g)*u   (kbt_gemm_silu_mul)
   kSwiglu,           // dual: C = silu(acc0)*acc1                 (kbt_gemm_rmsnorm_swiglu)
 };
@@ -156,6 +156,9 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
       st.n = ntot;
     }
   } else if constexpr (E == Epi::kSoftmaxPre || E == Epi::kLseClamp) {
+    // Running (max, sum of exp) kept in the log2 domain: m2 = max(y*log2 e),
+    // l = sum exp2(y*log2 e - m2), so each element costs one FMA + one ex2.
+    constexpr float kLog2e = 1.4426950408889634f;
     float cmax = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -173,10 +176,10 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
       if (j < nvalid) cmax = fmaxf(cmax, y);
     }
     if (nvalid > 0) {
-      const float mnew = fmaxf(st.a, cmax);
-      float l = (st.a == -INFINITY) ? 0.0f : st.b * expf(st.a - mnew);
+      const float mnew = fmaxf(st.a, cmax * kLog2e);
+      float l = (st.a == -INFINITY) ? 0.0f : st.b * exp2f(st.a - mnew);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) l += (j < nvalid) ? expf(v[j] - mnew) : 0.0f;
+      for (int j = 0; j < 32; ++j) l += (j < nvalid) ? exp2f(fmaf(v[j], kLog2e, -mnew)) : 0.0f;
       st.a = mnew;
       st.b = l;
     }
@@ -398,11 +401,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       st.a = (kStats == 2 && E != Epi::kLnPre) ? -INFINITY : 0.0f;
       st.b = 0.0f;
       st.n = 0.0f;
+      float v2[64];
+      float u2[kDual ? 64 : 1];
       for (int c = 0; c < nchunks; ++c) {
+        // TMEM is read 64 columns at a time: one load + wait per chunk pair.
+        if ((c & 1) == 0) {
+          tmem_ld64(tbase + c * 32, v2);
+          if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
+        }
         float v[32];
         float u[32];
-        tmem_ld32(tbase + c * 32, v);
-        if constexpr (kDual) tmem_ld32(tbase + 128 + c * 32, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = (c & 1) ? v2[32 + i] : v2[i];
+          if constexpr (kDual) u[i] = (c & 1) ? u2[32 + i] : u2[i];
+        }
         const int col0 = n0 + c * 32;
         const int nvalid = min(32, N - col0);
         epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
