@@ -51,6 +51,7 @@ int parse_ex(const akili_ex_t* ex, Mode* md) {
   md->out_f32 = ex->out_dtype == AKILI_DTYPE_F32;
   md->batch = ex->batch ? ex->batch : 1;
   md->heads = ex->heads ? ex->heads : 1;
+  if (ex->softmax_scale < 0.0f || ex->softmax_scale != ex->softmax_scale) return AKILI_E_UNSUPPORTED;
   md->scale = ex->softmax_scale != 0.0f ? ex->softmax_scale : 1.0f;
   md->workspace = reinterpret_cast<void*>(ex->workspace);
   md->workspace_bytes = ex->workspace ? ex->workspace_bytes : 0;

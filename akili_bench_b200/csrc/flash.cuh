@@ -40,6 +40,38 @@ constexpr int kFlashQTiles = 2;
 constexpr int kFlashThreads = 64 + 128 * kFlashQTiles;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// 2^x on the FMA pipe, to take part of the softmax's exponentials off the
+// MUFU unit (its throughput equals the tensor core's per key block here).
+// x = n + f with n = round(x) by the 1.5*2^23 magic-number addition and
+// f in [-0.5, 0.5]; 2^f by a cubic fitted for this kernel (iterated
+// reweighted least squares on the relative error: max 7.5e-5, well below
+// fp16's 4.9e-4 rounding of P); 2^n added into the exponent field.  Inputs
+// are clamped at -126, where the result is already below fp16's range.
+__device__ __forceinline__ float exp2_fma(float x) {
+  constexpr float kMagic = 12582912.0f;
+  x = fmaxf(x, -126.0f);
+  const float t = x + kMagic;
+  const float f = x - (t - kMagic);
+  const float p = fmaf(fmaf(fmaf(0.055174145847558975f, f, 0.24261757731437683f), f, 0.6932610869407654f), f,
+                       0.9999275803565979f);
+  return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - __float_as_int(kMagic)) << 23));
+}
+// 2^x by the MUFU unit in one instruction; results below the normal range
+// flush to zero (-inf gives 0), which fp16 P could not represent anyway.
+__device__ __forceinline__ float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Of each group of kExpGroup consecutive score pairs, the last is exponentiated
+// by exp2_fma, the others by the MUFU's exp2; 0 keeps every exponential on the
+// MUFU, which measured fastest once the softmax loop was trimmed (C5: 911 vs
+// 882 TFLOP/s with one pair in four on the FMA pipe).
+#ifndef AKILI_FLASH_EXP_GROUP
+#define AKILI_FLASH_EXP_GROUP 0
+#endif
+constexpr int kExpGroup = AKILI_FLASH_EXP_GROUP;
+
 struct FlashArgs {
   int seq_len;
   int head_dim;
@@ -221,13 +253,25 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       // the log2 domain (keys past the end are masked).
       float s[128];
       tmem_ld128(tS, s);
-      float rmax = -INFINITY;
       const int nvalid = N - kv0;  // >= 1
+      // Row max of the raw scores (the scale is positive, so it commutes with
+      // max); keys past the end exist only in the last block and are set to
+      // -inf there, so full blocks carry no per-element masking.
+      float mx[8];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        s[i] = (i < nvalid) ? s[i] * sl : -INFINITY;
-        rmax = fmaxf(rmax, s[i]);
+      for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
+      if (nvalid >= kFlashBN) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mx[i & 7] = fmaxf(mx[i & 7], s[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          if (i >= nvalid) s[i] = -INFINITY;
+          mx[i & 7] = fmaxf(mx[i & 7], s[i]);
+        }
       }
+      const float rmax = sl * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const bool grow = rmax > m_use + kRescaleThreshold;
       const float m_new = grow ? rmax : m_use;
       const float alpha = grow ? exp2f(m_use - m_new) : 1.0f;  // 0 on the first block
@@ -241,17 +285,24 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
           tmem_st32(tO + c * 32, o);
         }
       }
-      // P = exp2(s - m) as packed fp16 into the first 64 columns of S (one store).
-      float rsum = 0.0f;
+      // P = exp2(s * sl - m) as packed fp16 into the first 64 columns of S
+      // (one FFMA + one exponential per score; one store).
+      const float nm = -m_new;
+      float sm[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) sm[a] = 0.0f;
       uint32_t pk[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        const float p0 = exp2f(s[2 * i] - m_new);
-        const float p1 = exp2f(s[2 * i + 1] - m_new);
-        rsum += p0 + p1;
+        const bool fma_pipe = kExpGroup > 0 && (i % (kExpGroup > 0 ? kExpGroup : 1)) == kExpGroup - 1;
+        const float x0 = fmaf(s[2 * i], sl, nm), x1 = fmaf(s[2 * i + 1], sl, nm);
+        const float p0 = fma_pipe ? exp2_fma(x0) : ex2_mufu(x0);
+        const float p1 = fma_pipe ? exp2_fma(x1) : ex2_mufu(x1);
+        sm[i & 7] += p0 + p1;
         pk[i] = pack_half2(p0, p1);
       }
       tmem_st64(tS, pk);
+      const float rsum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
       tc_fence_before();
       mbar_arrive(&p_full[grp]);
       l = l * alpha + rsum;

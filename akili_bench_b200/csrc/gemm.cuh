@@ -96,6 +96,11 @@ __device__ __forceinline__ float round_out(float x) {
   return x;
 }
 
+// Reductions of a 32-value chunk with 4 independent accumulators (no 32-long
+// dependency chain in the epilogue's single warp per sub-partition).
+__device__ __forceinline__ float sum4(const float (&a)[4]) { return (a[0] + a[1]) + (a[2] + a[3]); }
+__device__ __forceinline__ float max4(const float (&a)[4]) { return fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])); }
+
 // Per-row running statistics of one tile.
 struct RowState {
   float a, b, n;
@@ -121,34 +126,35 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
       v[j] = val >= 0.0f ? val : val * ea.s1;
     }
   } else if constexpr (E == Epi::kRowSumHalf) {
-    float s = 0.0f;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s += (j < nvalid) ? v[j] * 0.5f : 0.0f;
-    st.a += s;
+    for (int j = 0; j < 32; ++j) s[j & 3] += (j < nvalid) ? v[j] * 0.5f : 0.0f;
+    st.a += sum4(s);
   } else if constexpr (E == Epi::kRowSumBias) {
-    float s = 0.0f;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s += (j < nvalid) ? (v[j] + __ldg(ea.vec0 + col0 + j)) : 0.0f;
-    st.a += s;
+    for (int j = 0; j < 32; ++j) s[j & 3] += (j < nvalid) ? (v[j] + __ldg(ea.vec0 + col0 + j)) : 0.0f;
+    st.a += sum4(s);
   } else if constexpr (E == Epi::kLnPre) {
     // y = acc + b, rounded to the stored precision; chunk mean/M2 merged into
     // the running (n, mean, M2) with Chan et al.'s pairwise update.
-    float sum = 0.0f;
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
       v[j] = round_out<OutT>(v[j] + b);
-      sum += (j < nvalid) ? v[j] : 0.0f;
+      sum[j & 3] += (j < nvalid) ? v[j] : 0.0f;
     }
     if (nvalid > 0) {
       const float nc = static_cast<float>(nvalid);
-      const float mc = sum / nc;
-      float m2 = 0.0f;
+      const float mc = sum4(sum) / nc;
+      float m2a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float d = v[j] - mc;
-        m2 += (j < nvalid) ? d * d : 0.0f;
+        m2a[j & 3] += (j < nvalid) ? d * d : 0.0f;
       }
+      const float m2 = sum4(m2a);
       const float ntot = st.n + nc;
       const float delta = mc - st.a;
       st.a += delta * (nc / ntot);
@@ -159,7 +165,7 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
     // Running (max, sum of exp) kept in the log2 domain: m2 = max(y*log2 e),
     // l = sum exp2(y*log2 e - m2), so each element costs one FMA + one ex2.
     constexpr float kLog2e = 1.4426950408889634f;
-    float cmax = -INFINITY;
+    float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       float y;
@@ -173,15 +179,15 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
         y = t;
       }
       v[j] = y;
-      if (j < nvalid) cmax = fmaxf(cmax, y);
+      if (j < nvalid) cm[j & 3] = fmaxf(cm[j & 3], y);
     }
     if (nvalid > 0) {
-      const float mnew = fmaxf(st.a, cmax * kLog2e);
-      float l = (st.a == -INFINITY) ? 0.0f : st.b * exp2f(st.a - mnew);
+      const float mnew = fmaxf(st.a, max4(cm) * kLog2e);
+      float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int j = 0; j < 32; ++j) l += (j < nvalid) ? exp2f(fmaf(v[j], kLog2e, -mnew)) : 0.0f;
+      for (int j = 0; j < 32; ++j) la[j & 3] += (j < nvalid) ? exp2f(fmaf(v[j], kLog2e, -mnew)) : 0.0f;
+      st.b = ((st.a == -INFINITY) ? 0.0f : st.b * exp2f(st.a - mnew)) + sum4(la);
       st.a = mnew;
-      st.b = l;
     }
   } else if constexpr (E == Epi::kSiluMulBias) {
 #pragma unroll

@@ -184,7 +184,7 @@ typedef struct {
   uint32_t out_dtype;       /* AKILI_DTYPE_F32 or AKILI_DTYPE_F16                          */
   uint32_t batch;           /* flash: batch size (0 means 1)                               */
   uint32_t heads;           /* flash: heads per batch entry (0 means 1)                    */
-  float    softmax_scale;   /* flash: scale of Q.K^T (0 means 1, the unscaled reference)   */
+  float    softmax_scale;   /* flash: scale of Q.K^T, >= 0 (0 means 1: the unscaled reference) */
   uint32_t causal;          /* reserved; must be 0                                         */
   uint32_t flags;           /* reserved; must be 0                                         */
   uint64_t workspace;       /* optional device scratch; 0 means the internal pool          */
