@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 METRIC = "fused fp16 GEMM+epilogue TFLOP/s & % tensor peak, 1/2/4/8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
+FLASH_SHAPE = [8, 32, 4096, 128]  # batch, heads, seq, head_dim; --flash-shape overrides
 
 # DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
 # capture summarised in profiles/ (None until captured for that workload).
@@ -163,7 +164,7 @@ def workloads(torch, ops):
         "kbt_sgemm", {"M": 128, "N": 128, "K": 128}, 2.0 * 128 ** 3, sg_make,
         lambda d, out, st: ops.kbt_sgemm(d["a"], d["bm"], out=out, out_dtype=f32, stream=st))
 
-    B, H, S, D = 8, 32, 4096, 128
+    B, H, S, D = FLASH_SHAPE
 
     def fl_make(gen):
         return {k: _rand(torch, gen.x, (B, H, S, D), dtype=f16) for k in ("q", "k", "v")}
@@ -471,7 +472,11 @@ def main():
     ap.add_argument("--cpu-rows-per-thread", type=int, default=48)
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed load before (and half after) the timed steps, for clock sampling")
+    ap.add_argument("--flash-shape", type=int, nargs=4, metavar=("B", "H", "S", "D"), default=None,
+                    help="flash workload shape (default: configs[4], 8 32 4096 128); smaller for profiling")
     args = ap.parse_args()
+    if args.flash_shape:
+        FLASH_SHAPE[:] = args.flash_shape
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
