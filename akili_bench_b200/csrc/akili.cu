@@ -301,6 +301,58 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
   return cv.off;
 }
 
+// Persistent launch of the CTA-pair kernel: clusters of 2, as many pairs as
+// can be resident at once (cudaOccupancyMaxActiveClusters), at most one per tile.
+template <Epi E, typename OutT, bool BK>
+int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1,
+                     const CUtensorMap& tmC, const EpiArgs& ea, cudaStream_t st) {
+  constexpr int BN = epi_bn(E);
+  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT));
+  auto kern = gemm_pair_kernel<E, OutT, BK>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::mutex mu;
+  static std::map<int, int> max_pairs;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int pairs_cap = 0;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = max_pairs.find(dev);
+    if (it == max_pairs.end()) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return AKILI_E_LAUNCH;
+      }
+      cfg.gridDim = dim3(di.sms & ~1);
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1) {
+        cudaGetLastError();
+        clusters = di.sms / 2;
+      }
+      it = max_pairs.emplace(dev, clusters).first;
+    }
+    pairs_cap = it->second;
+  }
+  const int tiles = ((ea.M + 2 * kBM - 1) / (2 * kBM)) * ((ea.N + BN - 1) / BN);
+  const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
+  cfg.gridDim = dim3(2 * pairs);
+  if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, ea) != cudaSuccess) {
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
+  return launch_status();
+}
+
 template <Epi E, typename OutT, bool BK>
 int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaStream_t st) {
   constexpr bool kStore = epi_stores(E);
@@ -308,8 +360,10 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   CUtensorMap tmA, tmB0, tmB1, tmC;
   const uint64_t M = j.M, N = j.N, K = j.K;
   bool ok = map2d(&tmA, jb.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, K * 2, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  // CTA pairs (two SMs per 256-row tile) whenever M fills more than one 128-row block.
+  const bool pair = M > static_cast<uint64_t>(kBM);
   if (BK) {
-    ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, N, K * 2, 64, BN,
+    ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, N, K * 2, 64, pair ? BN / 2 : BN,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
     ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K, N * 2, 64, 64,
@@ -345,6 +399,7 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.K = static_cast<int>(K);
   ea.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
 
+  if (pair) return launch_gemm_pair<E, OutT, BK>(di, tmA, tmB0, tmB1, tmC, ea, st);
   const int smem = gemm_smem_bytes(kStore, sizeof(OutT));
   static std::mutex mu;
   static std::map<int, bool> attr_done;

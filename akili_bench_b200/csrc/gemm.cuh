@@ -463,3 +463,269 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 }  // namespace akili
+
+namespace akili {
+
+// ---------------------------------------------------------------------------
+// gemm_pair_kernel — the same GEMM on a CTA pair (cluster of 2): one
+// tcgen05.mma.cta_group::2 (M = 256) per K-step covers a 256 x BN tile.  Each
+// CTA loads its own 128 rows of A and its half of the tile's B columns (no
+// TMA multicast), so the B operand bytes each SM pulls from L2/shared memory
+// per tensor-core cycle are halved against the single-CTA kernel, and the
+// ring can be 6 stages deep.  The even CTA issues the MMAs; its TMA-full
+// barriers count both CTAs' loads (the odd CTA's loads signal them through
+// the cluster address); one multicast tcgen05.commit frees both CTAs' ring
+// slots and publishes both CTAs' accumulators; the odd CTA's epilogue warps
+// release an accumulator with a remote arrive on the even CTA's barrier.
+// Each CTA's epilogue handles its own 128 rows exactly as in gemm_kernel.
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+constexpr int kPairStageBytes = kATileBytes + kBTileBytes / 2;  // 16 KB A + 16 KB half of B
+
+__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes) {
+  int s = kPairStages * kPairStageBytes;
+  if (stores) s += 2 * kBM * 32 * out_bytes;
+  s += 256 + 1024;
+  return s;
+}
+
+template <Epi E, typename OutT, bool kBKMajor>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmC,
+                     const EpiArgs ea) {
+  constexpr bool kDual = epi_dual(E);
+  constexpr bool kStore = epi_stores(E);
+  constexpr int kStats = epi_stats(E);
+  constexpr int BN = epi_bn(E);   // output columns per tile
+  constexpr int BNH = BN / 2;     // B columns (per operand) this CTA loads
+  constexpr int kOutBytes = sizeof(OutT);
+  constexpr int kStageOut = kBM * 32 * kOutBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* staging = ring + kPairStages * kPairStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + (kStore ? 2 * kStageOut : 0));
+  uint64_t* full = bars;                       // [stages], used in the even CTA
+  uint64_t* empty = bars + kPairStages;        // [stages]
+  uint64_t* acc_full = bars + 2 * kPairStages; // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2], used in the even CTA
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int M = ea.M, N = ea.N, K = ea.K;
+  const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kBK - 1) / kBK;
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // one arrive per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB0);
+    if constexpr (kDual) tma_prefetch_desc(&tmB1);
+    if constexpr (kStore) tma_prefetch_desc(&tmC);
+  }
+  cluster_sync();  // barriers initialised before the peer signals them
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint32_t full_c = mapa_shared(smem_u32(full), 0);  // the even CTA's full barriers
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        int m_blk, n_blk;
+        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        const int row0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int col0 = n_blk * BN + static_cast<int>(rank) * BNH;
+        for (int kb = 0; kb < num_kb && ok; ++kb) {
+          ok = mbar_wait_cluster(&empty[stage], phase ^ 1, kSiteProducerEmpty);
+          if (!ok) break;
+          uint8_t* sa = ring + stage * kPairStageBytes;
+          uint8_t* sb = sa + kATileBytes;
+          const uint32_t fb = full_c + stage * 8;
+          if (leader) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
+          tma_load_2d_pair(sa, &tmA, fb, kb * kBK, row0);
+          if constexpr (kBKMajor) {
+            tma_load_2d_pair(sb, &tmB0, fb, kb * kBK, col0);
+          } else if constexpr (kDual) {
+            tma_load_2d_pair(sb, &tmB0, fb, col0, kb * kBK);
+            tma_load_2d_pair(sb + 8192, &tmB1, fb, col0, kb * kBK);
+          } else {
+            tma_load_2d_pair(sb, &tmB0, fb, col0, kb * kBK);
+            tma_load_2d_pair(sb + 8192, &tmB0, fb, col0 + 64, kb * kBK);
+          }
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA (even CTA)
+    constexpr uint32_t idesc = kDual ? make_idesc_f16(2 * kBM, 128, false, !kBKMajor)
+                                     : make_idesc_f16(2 * kBM, 256, false, !kBKMajor);
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        ok = mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kAccCols;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          ok = mbar_wait_cluster(&full[stage], phase, kSiteMmaFull);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(ring + stage * kPairStageBytes);
+          const uint32_t sb = sa + kATileBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
+            const uint32_t accum = (kb | k) != 0;
+            if constexpr (kBKMajor) {
+              umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
+            } else if constexpr (kDual) {
+              umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+              umma_f16_ss_pair(d_tmem + 128, ad, make_sdesc(sb + 8192 + k * 2048, 8192, 1024, kSw128), idesc,
+                               accum);
+            } else {
+              umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+            }
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&acc_full[acc], 0x3);
+      }
+      // Drain: every issued MMA has completed before either CTA frees TMEM.
+      umma_commit_pair(drain, 0x1);
+      mbar_wait(drain, 0, kSiteDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ep_tid = threadIdx.x - 64;
+    const int wq = static_cast<int>(warp & 3);
+    const int r = wq * 32 + static_cast<int>(lane);
+    const uint32_t acc_empty_c = mapa_shared(smem_u32(acc_empty), 0);
+    int it = 0;
+    int chunk_ctr = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+      int m_blk, n_blk;
+      tile_coords(tile, num_m, num_n, m_blk, n_blk);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) *abort_flag = 1;
+      named_bar_sync(1, 128);
+      if (*abort_flag) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
+      const int n0 = n_blk * BN;
+      const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
+      const int row = mrow0 + r;
+      const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
+      RowState st;
+      st.a = (kStats == 2 && E != Epi::kLnPre) ? -INFINITY : 0.0f;
+      st.b = 0.0f;
+      st.n = 0.0f;
+      float v2[64];
+      float u2[kDual ? 64 : 1];
+      for (int c = 0; c < nchunks; ++c) {
+        if ((c & 1) == 0) {
+          tmem_ld64(tbase + c * 32, v2);
+          if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
+        }
+        float v[32];
+        float u[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = (c & 1) ? v2[32 + i] : v2[i];
+          if constexpr (kDual) u[i] = (c & 1) ? u2[32 + i] : u2[i];
+        }
+        const int col0 = n0 + c * 32;
+        const int nvalid = min(32, N - col0);
+        epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
+        if constexpr (kStore) {
+          uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
+          if (ep_tid == 0) bulk_wait_read<1>();
+          named_bar_sync(1, 128);
+          stage_row<OutT>(stg, r, v);
+          fence_async_shared();
+          named_bar_sync(1, 128);
+          if (ep_tid == 0) {
+            tma_store_2d(&tmC, stg, col0, mrow0);
+            bulk_commit();
+          }
+          ++chunk_ctr;
+        }
+      }
+      // This warp has read its TMEM rows: release the accumulator to the even CTA's MMA.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&acc_empty[acc]);
+        else mbar_arrive_cluster(acc_empty_c + acc * 8);
+      }
+      if constexpr (kStats > 0) {
+        if (row < M) {
+          float* ws = ea.row_ws;
+          const size_t plane = static_cast<size_t>(ea.num_n_tiles) * M;
+          ws[static_cast<size_t>(n_blk) * M + row] = st.a;
+          if constexpr (kStats == 2) ws[plane + static_cast<size_t>(n_blk) * M + row] = st.b;
+        }
+      }
+    }
+    if constexpr (kStore) {
+      if (ep_tid == 0) bulk_wait<0>();
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();  // neither CTA frees TMEM or exits while the pair still uses it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace akili

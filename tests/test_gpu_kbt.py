@@ -18,8 +18,10 @@ from akili_bench_b200.parity import assert_parity  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(16, 16, 16), (24, 40, 56), (128, 256, 64), (200, 264, 136), (136, 520, 1032)]
-ROW_SHAPES = [(16, 16, 16), (72, 1048, 200), (40, 4096, 128)]  # full-row epilogues spanning several tiles
+# M <= 128 runs the single-CTA kernel, larger M the CTA-pair kernel (256-row tiles).
+SHAPES = [(16, 16, 16), (24, 40, 56), (128, 256, 64), (200, 264, 136), (136, 520, 1032), (392, 776, 200),
+          (1000, 264, 72)]
+ROW_SHAPES = [(16, 16, 16), (72, 1048, 200), (40, 4096, 128), (264, 4104, 136)]  # full-row epilogues, many tiles
 
 
 def f16(rng, shape, scale=1.0, loc=0.0):
@@ -87,7 +89,8 @@ def test_kbt_gemm_layernorm(oracle, M, N, K):
                                                  1e-5, out_dtype=dt), ref, what="layernorm")
 
 
-@pytest.mark.parametrize("M,N,D", [(16, 16, 8), (24, 40, 16), (200, 264, 64), (72, 1048, 128), (40, 4096, 128)])
+@pytest.mark.parametrize("M,N,D", [(16, 16, 8), (24, 40, 16), (200, 264, 64), (72, 1048, 128), (40, 4096, 128),
+                                   (520, 1000, 128)])
 def test_kbt_attention_score(oracle, M, N, D):
     rng = np.random.default_rng(13 * M + N)
     q, k = f16(rng, (M, D)), f16(rng, (N, D))
