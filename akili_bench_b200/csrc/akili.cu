@@ -250,9 +250,10 @@ struct GemmJob {
   const float* ln_b = nullptr;
 };
 
+// Partial statistics: two slots (half tiles of BN/2 columns) per BN-column tile.
 size_t stats_bytes(const GemmJob& j) {
   const int bn = epi_bn(j.epi);
-  const size_t nt = (j.N + bn - 1) / bn;
+  const size_t nt = 2 * ((j.N + bn - 1) / bn);
   return static_cast<size_t>(epi_stats(j.epi)) * nt * j.M * sizeof(float);
 }
 
@@ -315,7 +316,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kGemmThreads);
+  cfg.blockDim = dim3(kPairThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -397,7 +398,7 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.M = static_cast<int>(M);
   ea.N = static_cast<int>(N);
   ea.K = static_cast<int>(K);
-  ea.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+  ea.num_n_tiles = static_cast<int>(2 * ((N + BN - 1) / BN));  // statistics slots: two per tile
 
   if (pair) return launch_gemm_pair<E, OutT, BK>(di, tmA, tmB0, tmB1, tmC, ea, st);
   const int smem = gemm_smem_bytes(kStore, sizeof(OutT));
@@ -487,7 +488,7 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
   if (rc) return rc;
   // 3. finalisers
   const int M = static_cast<int>(j.M), N = static_cast<int>(j.N);
-  const int nt = (N + epi_bn(j.epi) - 1) / epi_bn(j.epi);
+  const int nt = 2 * ((N + epi_bn(j.epi) - 1) / epi_bn(j.epi));  // statistics slots (half tiles)
   switch (j.epi) {
     case Epi::kRowSumHalf:
     case Epi::kRowSumBias:
@@ -509,10 +510,10 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
     case Epi::kLnPre:
       if (md.out_f32)
         layernorm_finalize_kernel<float><<<grid_for(di, M, 8, 8), 256, 0, st>>>(
-            static_cast<float*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi), j.eps);
+            static_cast<float*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi) / 2, j.eps);
       else
         layernorm_finalize_kernel<__half><<<grid_for(di, M, 8, 8), 256, 0, st>>>(
-            static_cast<__half*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi), j.eps);
+            static_cast<__half*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi) / 2, j.eps);
       return launch_status();
     case Epi::kSoftmaxPre:
       if (md.out_f32)

@@ -174,10 +174,30 @@ __device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
   }
 }
 
+// Warp-wide merge of per-tile LayerNorm partials (count, mean, M2) with Chan
+// et al.'s pairwise formula: lane t merges tiles t, t+32, ... then a
+// butterfly combines the lanes, so the partial loads are issued in parallel.
+__device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, float nb, float mb, float m2b) {
+  const float ntot = n + nb;
+  if (nb == 0.0f) return;
+  if (n == 0.0f) {
+    n = nb;
+    mean = mb;
+    m2 = m2b;
+    return;
+  }
+  const float delta = mb - mean;
+  mean += delta * (nb / ntot);
+  m2 += m2b + delta * delta * (n * nb / ntot);
+  n = ntot;
+}
+
 // In-place LayerNorm of the pre-normalised rows y = x.W + b written by the
 // GEMM epilogue.  Per-tile (mean, M2) partials over `tile_n` columns are
-// merged with Chan et al.'s pairwise formula; var = M2 / N (biased, as
+// (half tiles; a slot past the row's end is empty) merged with Chan et al.'s
+// pairwise formula; var = M2 / N (biased, as
 // benchmarks/kbt_gemm_layernorm/main.cpp:159-166); inv_std = 1/sqrtf(var+eps).
+// One warp per row, 16-byte accesses, four row chunks in flight per lane.
 template <typename T>
 __global__ void layernorm_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws,
                                           const float* __restrict__ ln_w, const float* __restrict__ ln_b, int M,
@@ -186,19 +206,20 @@ __global__ void layernorm_finalize_kernel(T* __restrict__ c, const float* __rest
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
     float n = 0.0f, mean = 0.0f, m2 = 0.0f;
-    for (int t = 0; t < ntiles; ++t) {
-      const float nt = static_cast<float>(min(tile_n, N - t * tile_n));
-      const float mt = ws[static_cast<size_t>(t) * M + row];
-      const float m2t = ws[static_cast<size_t>(ntiles + t) * M + row];
-      const float ntot = n + nt;
-      const float delta = mt - mean;
-      mean += delta * (nt / ntot);
-      m2 += m2t + delta * delta * (n * nt / ntot);
-      n = ntot;
+    for (int t = lane; t < ntiles; t += 32)
+      chan_merge(n, mean, m2, static_cast<float>(max(0, min(tile_n, N - t * tile_n))), ws[static_cast<size_t>(t) * M + row],
+                 ws[static_cast<size_t>(ntiles + t) * M + row]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float nb = __shfl_xor_sync(0xffffffffu, n, o);
+      const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
+      const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+      chan_merge(n, mean, m2, nb, mb, m2b);
     }
     const float var = m2 / static_cast<float>(N);
     const float inv_std = 1.0f / sqrtf(var + eps);
     T* cr = c + static_cast<size_t>(row) * N;
+#pragma unroll 4
     for (int j = lane * 8; j < N; j += 256) {
       float f[8];
       load8(cr + j, f);
@@ -215,6 +236,34 @@ __global__ void layernorm_finalize_kernel(T* __restrict__ c, const float* __rest
   }
 }
 
+// Merge of (max, sum of exp2) partials in the log2 domain; -inf max = empty.
+__device__ __forceinline__ void lse2_merge(float& m, float& l, float mb, float lb) {
+  if (mb == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = mb;
+    l = lb;
+    return;
+  }
+  const float mn = fmaxf(m, mb);
+  l = l * exp2f(m - mn) + lb * exp2f(mb - mn);
+  m = mn;
+}
+
+// Warp-wide merge of a row's per-tile (max, sumexp) partials.
+__device__ __forceinline__ void row_lse2(const float* __restrict__ ws, int M, int ntiles, int row, int lane, float& m,
+                                         float& l) {
+  m = -INFINITY;
+  l = 0.0f;
+  for (int t = lane; t < ntiles; t += 32)
+    lse2_merge(m, l, ws[static_cast<size_t>(t) * M + row], ws[static_cast<size_t>(ntiles + t) * M + row]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float mb = __shfl_xor_sync(0xffffffffu, m, o);
+    const float lb = __shfl_xor_sync(0xffffffffu, l, o);
+    lse2_merge(m, l, mb, lb);
+  }
+}
+
 // In-place softmax of the rows y written by the GEMM epilogue, from the
 // per-tile (max, sumexp) partials in the log2 domain:
 // out = exp2(y * log2 e - m2) * (1 / l).
@@ -224,16 +273,12 @@ __global__ void softmax_finalize_kernel(T* __restrict__ c, const float* __restri
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
-    float m = -INFINITY;
-    for (int t = 0; t < ntiles; ++t) m = fmaxf(m, ws[static_cast<size_t>(t) * M + row]);
-    float l = 0.0f;
-    for (int t = 0; t < ntiles; ++t) {
-      const float mt = ws[static_cast<size_t>(t) * M + row];
-      if (mt != -INFINITY) l += ws[static_cast<size_t>(ntiles + t) * M + row] * exp2f(mt - m);
-    }
+    float m, l;
+    row_lse2(ws, M, ntiles, row, lane, m, l);
     const float inv = 1.0f / l;
     constexpr float kLog2e = 1.4426950408889634f;
     T* cr = c + static_cast<size_t>(row) * N;
+#pragma unroll 4
     for (int j = lane * 8; j < N; j += 256) {
       float f[8];
       load8(cr + j, f);

@@ -229,6 +229,75 @@ __device__ __forceinline__ void stage_row(uint8_t* stage, int r, const float (&v
   }
 }
 
+// Epilogue of one half of a tile's output columns: 32-column chunks
+// [c_begin, c_end) read from TMEM by 128 threads (one per accumulator row,
+// TMEM base `tbase` already offset to this warp's lane quarter), the op
+// applied, and the result either staged through `staging` (two ping-pong
+// buffers) for TMA stores issued by `issuer`, or reduced to the row's
+// statistics, which are returned.  `bar_id` is the named barrier of these
+// 128 threads.
+template <Epi E, typename OutT>
+__device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUtensorMap* tmC, uint32_t tbase, int n0,
+                                                  int mrow0, int r, int c_begin, int c_end, uint8_t* staging,
+                                                  uint32_t bar_id, bool issuer, int& chunk_ctr) {
+  constexpr bool kDual = epi_dual(E);
+  constexpr bool kStore = epi_stores(E);
+  constexpr int kStats = epi_stats(E);
+  constexpr int kStageOut = kBM * 32 * sizeof(OutT);
+  RowState st;
+  st.a = (kStats == 2 && E != Epi::kLnPre) ? -INFINITY : 0.0f;
+  st.b = 0.0f;
+  st.n = 0.0f;
+  float v2[64];
+  float u2[kDual ? 64 : 1];
+  for (int c = c_begin; c < c_end; ++c) {
+    const bool odd = ((c - c_begin) & 1) != 0;
+    // TMEM is read 64 columns at a time: one load + wait per chunk pair.
+    if (!odd) {
+      tmem_ld64(tbase + c * 32, v2);
+      if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
+    }
+    float v[32];
+    float u[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      v[i] = odd ? v2[32 + i] : v2[i];
+      if constexpr (kDual) u[i] = odd ? u2[32 + i] : u2[i];
+    }
+    const int col0 = n0 + c * 32;
+    const int nvalid = min(32, ea.N - col0);
+    epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
+    if constexpr (kStore) {
+      uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
+      if (issuer) bulk_wait_read<1>();
+      named_bar_sync(bar_id, 128);
+      stage_row<OutT>(stg, r, v);
+      fence_async_shared();
+      named_bar_sync(bar_id, 128);
+      if (issuer) {
+        tma_store_2d(tmC, stg, col0, mrow0);
+        bulk_commit();
+      }
+      ++chunk_ctr;
+    }
+  }
+  return st;
+}
+
+// Per-row partial statistics of one half tile go to slot `slot` of the
+// [stat][slot][M] workspace (two slots per BN-column tile).
+template <Epi E>
+__device__ __forceinline__ void write_stats(const EpiArgs& ea, int slot, int row, const RowState& st) {
+  constexpr int kStats = epi_stats(E);
+  if constexpr (kStats > 0) {
+    if (row < ea.M) {
+      const size_t plane = static_cast<size_t>(ea.num_n_tiles) * ea.M;
+      ea.row_ws[static_cast<size_t>(slot) * ea.M + row] = st.a;
+      if constexpr (kStats == 2) ea.row_ws[plane + static_cast<size_t>(slot) * ea.M + row] = st.b;
+    }
+  }
+}
+
 template <Epi E, typename OutT, bool kBKMajor>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
@@ -403,52 +472,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = n_blk * BN;
       const int row = m_blk * kBM + r;
       const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-      RowState st;
-      st.a = (kStats == 2 && E != Epi::kLnPre) ? -INFINITY : 0.0f;
-      st.b = 0.0f;
-      st.n = 0.0f;
-      float v2[64];
-      float u2[kDual ? 64 : 1];
-      for (int c = 0; c < nchunks; ++c) {
-        // TMEM is read 64 columns at a time: one load + wait per chunk pair.
-        if ((c & 1) == 0) {
-          tmem_ld64(tbase + c * 32, v2);
-          if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
-        }
-        float v[32];
-        float u[32];
+      constexpr int HC = BN / 64;  // chunks per half tile
+      RowState st[2];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          v[i] = (c & 1) ? v2[32 + i] : v2[i];
-          if constexpr (kDual) u[i] = (c & 1) ? u2[32 + i] : u2[i];
-        }
-        const int col0 = n0 + c * 32;
-        const int nvalid = min(32, N - col0);
-        epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
-        if constexpr (kStore) {
-          uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
-          if (ep_tid == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);
-          stage_row<OutT>(stg, r, v);
-          fence_async_shared();
-          named_bar_sync(1, 128);
-          if (ep_tid == 0) {
-            tma_store_2d(&tmC, stg, col0, m_blk * kBM);
-            bulk_commit();
-          }
-          ++chunk_ctr;
-        }
-      }
+      for (int h = 0; h < 2; ++h)
+        st[h] = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, m_blk * kBM, r, h * HC, min((h + 1) * HC, nchunks),
+                                       staging, 1, ep_tid == 0, chunk_ctr);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
-      if constexpr (kStats > 0) {
-        if (row < M) {
-          float* ws = ea.row_ws;
-          const size_t plane = static_cast<size_t>(ea.num_n_tiles) * M;
-          ws[static_cast<size_t>(n_blk) * M + row] = st.a;
-          if constexpr (kStats == 2) ws[plane + static_cast<size_t>(n_blk) * M + row] = st.b;
-        }
-      }
+      write_stats<E>(ea, 2 * n_blk, row, st[0]);
+      write_stats<E>(ea, 2 * n_blk + 1, row, st[1]);
     }
     if constexpr (kStore) {
       if (ep_tid == 0) bulk_wait<0>();
@@ -479,18 +512,20 @@ namespace akili {
 // release an accumulator with a remote arrive on the even CTA's barrier.
 // Each CTA's epilogue handles its own 128 rows exactly as in gemm_kernel.
 // ---------------------------------------------------------------------------
-constexpr int kPairStages = 6;
+constexpr int kPairThreads = 320;  // TMA, MMA, 8 epilogue warps (two per TMEM lane quarter)
 constexpr int kPairStageBytes = kATileBytes + kBTileBytes / 2;  // 16 KB A + 16 KB half of B
+// Ring depth: 6 slots, 5 when the two epilogue groups stage fp32 output.
+__host__ __device__ constexpr int pair_stages(bool stores, int out_bytes) { return stores && out_bytes == 4 ? 5 : 6; }
 
 __host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes) {
-  int s = kPairStages * kPairStageBytes;
-  if (stores) s += 2 * kBM * 32 * out_bytes;
+  int s = pair_stages(stores, out_bytes) * kPairStageBytes;
+  if (stores) s += 2 * 2 * kBM * 32 * out_bytes;
   s += 256 + 1024;
   return s;
 }
 
 template <Epi E, typename OutT, bool kBKMajor>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                      const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmC,
                      const EpiArgs ea) {
@@ -501,12 +536,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int BNH = BN / 2;     // B columns (per operand) this CTA loads
   constexpr int kOutBytes = sizeof(OutT);
   constexpr int kStageOut = kBM * 32 * kOutBytes;
+  constexpr int kPairStages = pair_stages(kStore, kOutBytes);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint8_t* staging = ring + kPairStages * kPairStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + (kStore ? 2 * kStageOut : 0));
+  uint8_t* staging = ring + kPairStages * kPairStageBytes;  // [group][2 ping-pong buffers]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + (kStore ? 2 * 2 * kStageOut : 0));
   uint64_t* full = bars;                       // [stages], used in the even CTA
   uint64_t* empty = bars + kPairStages;        // [stages]
   uint64_t* acc_full = bars + 2 * kPairStages; // [2]
@@ -534,7 +570,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 8);  // one arrive per epilogue warp of both CTAs
+      mbar_init(&acc_empty[a], 16);  // one arrive per epilogue warp (8 per CTA) of both CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -644,10 +680,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ep_tid = threadIdx.x - 64;
+    // Two groups of four warps: group h takes output columns of half h of
+    // each tile, for all 128 rows (warp w reads TMEM lanes 32*(w%4)..).
+    const int grp = (static_cast<int>(warp) - 2) >> 2;
+    const int gtid = threadIdx.x - 64 - 128 * grp;
     const int wq = static_cast<int>(warp & 3);
     const int r = wq * 32 + static_cast<int>(lane);
+    const uint32_t bar_id = 1 + grp;
+    uint8_t* gstaging = staging + grp * 2 * kStageOut;
     const uint32_t acc_empty_c = mapa_shared(smem_u32(acc_empty), 0);
+    constexpr int HC = BN / 64;  // chunks per half tile
     int it = 0;
     int chunk_ctr = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
@@ -656,49 +698,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) *abort_flag = 1;
-      named_bar_sync(1, 128);
+      named_bar_sync(bar_id, 128);
       if (*abort_flag) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
       const int n0 = n_blk * BN;
       const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
-      const int row = mrow0 + r;
       const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-      RowState st;
-      st.a = (kStats == 2 && E != Epi::kLnPre) ? -INFINITY : 0.0f;
-      st.b = 0.0f;
-      st.n = 0.0f;
-      float v2[64];
-      float u2[kDual ? 64 : 1];
-      for (int c = 0; c < nchunks; ++c) {
-        if ((c & 1) == 0) {
-          tmem_ld64(tbase + c * 32, v2);
-          if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
-        }
-        float v[32];
-        float u[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          v[i] = (c & 1) ? v2[32 + i] : v2[i];
-          if constexpr (kDual) u[i] = (c & 1) ? u2[32 + i] : u2[i];
-        }
-        const int col0 = n0 + c * 32;
-        const int nvalid = min(32, N - col0);
-        epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
-        if constexpr (kStore) {
-          uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
-          if (ep_tid == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);
-          stage_row<OutT>(stg, r, v);
-          fence_async_shared();
-          named_bar_sync(1, 128);
-          if (ep_tid == 0) {
-            tma_store_2d(&tmC, stg, col0, mrow0);
-            bulk_commit();
-          }
-          ++chunk_ctr;
-        }
-      }
+      const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
+                                                 min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
+                                                 chunk_ctr);
       // This warp has read its TMEM rows: release the accumulator to the even CTA's MMA.
       tc_fence_before();
       __syncwarp();
@@ -706,17 +715,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (leader) mbar_arrive(&acc_empty[acc]);
         else mbar_arrive_cluster(acc_empty_c + acc * 8);
       }
-      if constexpr (kStats > 0) {
-        if (row < M) {
-          float* ws = ea.row_ws;
-          const size_t plane = static_cast<size_t>(ea.num_n_tiles) * M;
-          ws[static_cast<size_t>(n_blk) * M + row] = st.a;
-          if constexpr (kStats == 2) ws[plane + static_cast<size_t>(n_blk) * M + row] = st.b;
-        }
-      }
+      write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
     }
     if constexpr (kStore) {
-      if (ep_tid == 0) bulk_wait<0>();
+      if (gtid == 0) bulk_wait<0>();
     }
   }
 

@@ -230,7 +230,7 @@ int akili_kbt_gemm_layernorm_ex(const kbt_gemm_layernorm_arg_t* arg, const akili
  * partial statistics, lives in a fixed device array of
  * AKILI_NOALLOC_SCRATCH_BYTES inside the library (held by every GPU that
  * loads it until exit); a problem needing more, i.e.
- * 8 * M * ceil(N / 256) bytes > AKILI_NOALLOC_SCRATCH_BYTES, returns
+ * 16 * M * ceil(N / 256) bytes > AKILI_NOALLOC_SCRATCH_BYTES, returns
  * AKILI_E_SCRATCH_LIMIT.  The first call on a device looks up that array's
  * device address (once per device, with the device current); make that first
  * call before any stream capture.  All calls share the array: calls that

@@ -34,9 +34,9 @@ def _noalloc(arg, ex, stream=0):
 
 def test_noalloc_rejects_what_it_cannot_hold_without_touching_the_gpu():
     ex = abi.make_ex(abi.DTYPE_F16, abi.DTYPE_F16)
-    # 8 * M * ceil(N/256) bytes of partials must fit the fixed array
+    # 16 * M * ceil(N/256) bytes of partials must fit the fixed array
     big = _arg(65536, 8192, 64)
-    assert 8 * 65536 * 32 > abi.NOALLOC_SCRATCH_BYTES
+    assert 16 * 65536 * 32 > abi.NOALLOC_SCRATCH_BYTES
     assert _noalloc(big, ex) == abi.E_SCRATCH_LIMIT
     assert "no-alloc scratch" in abi.strerror(abi.E_SCRATCH_LIMIT)
     # fp32 operands would need converted copies, which the fixed scratch does not hold
