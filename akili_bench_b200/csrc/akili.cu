@@ -690,9 +690,18 @@ int job_silu_mul(const kbt_gemm_silu_mul_arg_t* a, GemmJob& j, bool chk = true) 
 // -------------------------------------------------------------- flash --
 struct FlashJob {
   uint32_t seq_len = 0, head_dim = 0;
+  uint32_t kernel_type = 1;  // 0: the reference's fp32 SIMT flash, 1: its fp16 tensor-core flash
   const void *Q = nullptr, *K = nullptr, *V = nullptr;
   void* O = nullptr;
 };
+
+// fp32 operands with the reference's SIMT kernel type (fp32 arithmetic,
+// benchmarks/flash/kernel.cpp:27-135) compute S in split precision, so
+// scores of the unscaled reference inputs keep fp32-level accuracy; head
+// dims up to 64 (the reference's SIMT path allows 16).
+bool flash_split(const FlashJob& j, const Mode& md) {
+  return md.in_f32 && j.kernel_type == 0 && j.head_dim <= 64;
+}
 
 int job_flash(const flash_arg_t* a, FlashJob& j, bool chk = true) {
   if (!a) return AKILI_E_NULL_ARG;
@@ -700,7 +709,7 @@ int job_flash(const flash_arg_t* a, FlashJob& j, bool chk = true) {
   if (a->head_dim > 128) return AKILI_E_UNSUPPORTED;
   int rc;
   if (chk && (rc = check_ptrs({a->Q_addr, a->K_addr, a->V_addr, a->O_addr}))) return rc;
-  j.seq_len = a->seq_len; j.head_dim = a->head_dim;
+  j.seq_len = a->seq_len; j.head_dim = a->head_dim; j.kernel_type = a->kernel_type;
   j.Q = P(a->Q_addr); j.K = P(a->K_addr); j.V = P(a->V_addr); j.O = W(a->O_addr);
   return AKILI_OK;
 }
@@ -709,7 +718,7 @@ size_t flash_scratch_bytes(const FlashJob& j, const Mode& md) {
   if (!md.in_f32) return 0;
   const size_t n = static_cast<size_t>(md.batch) * md.heads * j.seq_len * j.head_dim;
   Carve c;
-  c.need(n * 2); c.need(n * 2); c.need(n * 2);
+  for (int i = 0; i < (flash_split(j, md) ? 5 : 3); ++i) c.need(n * 2);
   return c.off;
 }
 
@@ -720,6 +729,8 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
   const size_t n = static_cast<size_t>(md.batch) * md.heads * j.seq_len * j.head_dim;
   const __half *q = static_cast<const __half*>(j.Q), *k = static_cast<const __half*>(j.K),
                *v = static_cast<const __half*>(j.V);
+  const __half *qlo = nullptr, *klo = nullptr;
+  const bool split = flash_split(j, md);
   if (md.in_f32) {
     char* base = nullptr;
     if ((rc = acquire_scratch(md, flash_scratch_bytes(j, md), st, &base))) return rc;
@@ -728,8 +739,19 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
     __half* cq = static_cast<__half*>(cv.take(n * 2));
     __half* ck = static_cast<__half*>(cv.take(n * 2));
     __half* cvv = static_cast<__half*>(cv.take(n * 2));
-    if ((rc = cast_to_f16(di, static_cast<const float*>(j.Q), cq, n, st))) return rc;
-    if ((rc = cast_to_f16(di, static_cast<const float*>(j.K), ck, n, st))) return rc;
+    if (split) {
+      __half* cql = static_cast<__half*>(cv.take(n * 2));
+      __half* ckl = static_cast<__half*>(cv.take(n * 2));
+      const int g = grid_for(di, n, 256, 8);
+      split_f32_to_f16x2_kernel<<<g, 256, 0, st>>>(static_cast<const float*>(j.Q), cq, cql, n);
+      if ((rc = launch_status())) return rc;
+      split_f32_to_f16x2_kernel<<<g, 256, 0, st>>>(static_cast<const float*>(j.K), ck, ckl, n);
+      if ((rc = launch_status())) return rc;
+      qlo = cql; klo = ckl;
+    } else {
+      if ((rc = cast_to_f16(di, static_cast<const float*>(j.Q), cq, n, st))) return rc;
+      if ((rc = cast_to_f16(di, static_cast<const float*>(j.K), ck, n, st))) return rc;
+    }
     if ((rc = cast_to_f16(di, static_cast<const float*>(j.V), cvv, n, st))) return rc;
     q = cq; k = ck; v = cvv;
   }
@@ -749,14 +771,21 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
   else
     ok = ok && map3d(&to, j.O, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 32, kFlashBM,
                      CU_TENSOR_MAP_SWIZZLE_64B, 2);
+  CUtensorMap tql = tq, tkl = tk;
+  if (split)
+    ok = ok && map3d(&tql, qlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 64, kFlashBM,
+                     CU_TENSOR_MAP_SWIZZLE_128B, 2) &&
+         map3d(&tkl, klo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, D, j.seq_len, bh, 64, kFlashBN,
+               CU_TENSOR_MAP_SWIZZLE_128B, 2);
   if (!ok) return AKILI_E_LAUNCH;
   FlashArgs fa;
   fa.seq_len = static_cast<int>(j.seq_len);
   fa.head_dim = static_cast<int>(D);
   fa.scale_log2 = md.scale * 1.4426950408889634f;
   dim3 grid((j.seq_len + kFlashBM * kFlashQTiles - 1) / (kFlashBM * kFlashQTiles), bh);
-  if (dpad == 64) rc = launch_flash<64>(grid, md.out_f32, tq, tk, tv, to, fa, st);
-  else rc = launch_flash<128>(grid, md.out_f32, tq, tk, tv, to, fa, st);
+  if (split) rc = launch_flash<64, true>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
+  else if (dpad == 64) rc = launch_flash<64, false>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
+  else rc = launch_flash<128, false>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
   if (rc == AKILI_OK) g_launches.fetch_add(1, std::memory_order_relaxed);
   return rc;
 }
@@ -765,7 +794,7 @@ cudaStream_t S(akili_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ------------------------------------------------- no-alloc LayerNorm scratch --
 // Fixed device scratch of akili_kbt_gemm_layernorm_noalloc: the per-(row,
-// 256-column tile) (mean, M2) partials its GEMM epilogue writes and its
+// 128-column half tile) (mean, M2) partials its GEMM epilogue writes and its
 // finaliser reads.  Every slot the finaliser reads is written earlier in the
 // same call, so nothing needs clearing between calls; concurrent calls race.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[AKILI_NOALLOC_SCRATCH_BYTES];

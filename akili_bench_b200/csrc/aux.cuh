@@ -32,6 +32,19 @@ __global__ void cast_f32_to_f16_kernel(const float* __restrict__ src, __half* __
     dst[i] = __float2half_rn(src[i]);
 }
 
+// x -> (hi, lo) = (fp16(x), fp16(x - fp16(x))): hi + lo carries ~22 bits of
+// x's mantissa, for the split-precision products of the fp32 flash mode.
+__global__ void split_f32_to_f16x2_kernel(const float* __restrict__ src, __half* __restrict__ hi,
+                                          __half* __restrict__ lo, size_t n) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+    const float x = src[i];
+    const __half h = __float2half_rn(x);
+    hi[i] = h;
+    lo[i] = __float2half_rn(x - __half2float(h));
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

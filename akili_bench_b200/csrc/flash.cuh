@@ -78,25 +78,29 @@ struct FlashArgs {
   float scale_log2;  // softmax scale * log2(e)
 };
 
-template <int DP>
+// kSplit: Q and K also carry their fp16 low parts (x - fp16(x)), doubling
+// their tiles; S is then Q_hi.K_hi + Q_hi.K_lo + Q_lo.K_hi in fp32.
+template <int DP, bool kSplit = false>
 struct FlashSmem {
-  static constexpr int kQ = kFlashBM * DP * 2;   // one Q tile
-  static constexpr int kKV = kFlashBN * DP * 2;  // one K or V block
+  static constexpr int kQ = kFlashBM * DP * 2;   // one Q tile (one part)
+  static constexpr int kKV = kFlashBN * DP * 2;  // one K or V block (one part)
+  static constexpr int kParts = kSplit ? 2 : 1;
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kFlashQTiles * kQ;
-  static constexpr int kVOff = kKOff + 2 * kKV;
+  static constexpr int kKOff = kQOff + kFlashQTiles * kQ * kParts;
+  static constexpr int kVOff = kKOff + 2 * kKV * kParts;
   static constexpr int kBarOff = kVOff + 2 * kKV;
   static constexpr int kBytes = kBarOff + 256 + 1024;
   // the output staging of both softmax groups reuses the drained K/V rings
   static_assert(2 * 2 * kFlashBM * 32 * 4 <= 4 * kKV, "staging must fit in the K/V rings");
 };
 
-template <int DP, typename OutT>
+template <int DP, typename OutT, bool kSplit>
 __global__ void __launch_bounds__(kFlashThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                     const __grid_constant__ CUtensorMap tmQlo, const __grid_constant__ CUtensorMap tmKlo,
                      const FlashArgs fa) {
-  using L = FlashSmem<DP>;
+  using L = FlashSmem<DP, kSplit>;
   constexpr int kChunks = DP / 64;  // 64-column swizzle chunks of Q/K/V
   constexpr int kStageOut = kFlashBM * 32 * sizeof(OutT);
   constexpr uint32_t kColO = 256;   // O_t at 256 + 128 t; S_t / P_t at 128 t
@@ -159,17 +163,23 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ loads
     if (lane == 0) {
-      mbar_expect_tx(q_full, kFlashQTiles * L::kQ);
+      mbar_expect_tx(q_full, kFlashQTiles * L::kQ * L::kParts);
       for (int t = 0; t < kFlashQTiles; ++t)
-        for (int q = 0; q < kChunks; ++q)
+        for (int q = 0; q < kChunks; ++q) {
           tma_load_3d(sQ + t * L::kQ + q * 16384, &tmQ, q_full, q * 64, m0 + t * kFlashBM, bh);
+          if constexpr (kSplit)
+            tma_load_3d(sQ + (kFlashQTiles + t) * L::kQ + q * 16384, &tmQlo, q_full, q * 64, m0 + t * kFlashBM, bh);
+        }
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, kSiteFlashFree)) break;
-        mbar_expect_tx(&k_full[st], L::kKV);
-        for (int q = 0; q < kChunks; ++q)
+        mbar_expect_tx(&k_full[st], L::kKV * L::kParts);
+        for (int q = 0; q < kChunks; ++q) {
           tma_load_3d(sK + st * L::kKV + q * 16384, &tmK, &k_full[st], q * 64, j * kFlashBN, bh);
+          if constexpr (kSplit)
+            tma_load_3d(sK + (2 + st) * L::kKV + q * 16384, &tmKlo, &k_full[st], q * 64, j * kFlashBN, bh);
+        }
         if (!mbar_wait(&v_empty[st], ph ^ 1, kSiteFlashFree)) break;
         mbar_expect_tx(&v_full[st], L::kKV);
         for (int q = 0; q < kChunks; ++q)
@@ -212,8 +222,14 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
 #pragma unroll
             for (int k = 0; k < DP / 16; ++k) {
               const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-              umma_f16_ss(tmem + t * 128, make_sdesc(q_addr + t * L::kQ + off, 16, 1024, kSw128),
-                          make_sdesc(k_addr + off, 16, 1024, kSw128), idesc_s, k != 0);
+              const uint64_t qh = make_sdesc(q_addr + t * L::kQ + off, 16, 1024, kSw128);
+              const uint64_t kh = make_sdesc(k_addr + off, 16, 1024, kSw128);
+              umma_f16_ss(tmem + t * 128, qh, kh, idesc_s, k != 0);
+              if constexpr (kSplit) {
+                umma_f16_ss(tmem + t * 128, qh, make_sdesc(k_addr + 2 * L::kKV + off, 16, 1024, kSw128), idesc_s, 1);
+                umma_f16_ss(tmem + t * 128, make_sdesc(q_addr + (kFlashQTiles + t) * L::kQ + off, 16, 1024, kSw128),
+                            kh, idesc_s, 1);
+              }
             }
             umma_commit(&s_full[t]);
           }
@@ -346,18 +362,19 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   }
 }
 
-template <int DP>
+template <int DP, bool kSplit>
 int launch_flash(dim3 grid, bool out_f32, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                 const CUtensorMap& to, const FlashArgs& fa, cudaStream_t st) {
-  const int smem = FlashSmem<DP>::kBytes;
-  auto k32 = flash_fwd_kernel<DP, float>;
-  auto k16 = flash_fwd_kernel<DP, __half>;
+                 const CUtensorMap& to, const CUtensorMap& tqlo, const CUtensorMap& tklo, const FlashArgs& fa,
+                 cudaStream_t st) {
+  const int smem = FlashSmem<DP, kSplit>::kBytes;
+  auto k32 = flash_fwd_kernel<DP, float, kSplit>;
+  auto k16 = flash_fwd_kernel<DP, __half, kSplit>;
   auto kern = out_f32 ? k32 : k16;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
     cudaGetLastError();
     return AKILI_E_LAUNCH;
   }
-  kern<<<grid, kFlashThreads, smem, st>>>(tq, tk, tv, to, fa);
+  kern<<<grid, kFlashThreads, smem, st>>>(tq, tk, tv, to, tqlo, tklo, fa);
   return cudaGetLastError() == cudaSuccess ? AKILI_OK : AKILI_E_LAUNCH;
 }
 

@@ -187,8 +187,12 @@ def kbt_gemm_silu_mul(x, wa, ba, wb, bb, out=None, out_dtype=None, stream=None):
     return c
 
 
-def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None):
-    """q/k/v [S, D] (one head, reference layout) or [B, H, S, D]."""
+def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None, kernel_type=1):
+    """q/k/v [S, D] (one head, reference layout) or [B, H, S, D].
+
+    kernel_type follows the reference's flash_arg_t: 1 = its fp16 tensor-core
+    flash (operands rounded to fp16), 0 = its fp32 SIMT flash (with fp32
+    inputs the scores are computed in split precision)."""
     if q.dim() == 2:
         B, H, (S, D) = 1, 1, q.shape
     else:
@@ -197,7 +201,7 @@ def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None):
     arg = abi.FlashArg()
     arg.grid_dim[0] = (S + 7) // 8
     arg.block_dim[0] = 8
-    arg.kernel_type = 1
+    arg.kernel_type = kernel_type
     arg.seq_len, arg.head_dim = S, D
     arg.block_size_r = arg.block_size_c = 8
     arg.Q_addr, arg.K_addr, arg.V_addr, arg.O_addr = _addr(q), _addr(k), _addr(v), _addr(o)

@@ -75,3 +75,19 @@ def test_flash_large_logits_are_stable(oracle):
     ref = oracle.flash(q, k, v, S, D, 1.0)
     got = ops.flash(dev(q, torch.float32), dev(k, torch.float32), dev(v, torch.float32)).cpu().numpy()
     assert_parity(got, ref, what="flash large logits")
+
+
+@pytest.mark.parametrize("S,D", [(256, 8), (128, 16), (300, 64)])
+def test_flash_fp32_simt_mode_matches_unrounded_gold(oracle, S, D):
+    """kernel_type 0 with fp32 inputs (the reference SIMT flash, fp32
+    arithmetic): split-precision scores track the fp32 gold on the reference
+    harness's own input range (uniform [-5, 5), no scale: logits in the
+    hundreds), where fp16-rounded scores would not."""
+    rng = np.random.default_rng(S * 3 + D)
+    q, k, v = (rng.random((S, D), dtype=np.float32) * 10 - 5 for _ in range(3))
+    ref = oracle.flash(q, k, v, S, D, 1.0)
+    got = ops.flash(dev(q, torch.float32), dev(k, torch.float32), dev(v, torch.float32), kernel_type=0).cpu().numpy()
+    assert ops.device_status() == 0
+    assert_parity(got, ref, what=f"flash fp32 simt S={S} D={D}")
+    # and the reference harness's own per-element bound (flash/main.cpp:37-49)
+    assert (np.abs(got - ref) <= 5e-2 + 1e-2 * np.abs(got)).all()

@@ -32,8 +32,8 @@ B200 = os.path.join(ROOT, "oracle", "_ref", "b200")
 # short K, where the harness check is meaningful.
 HARNESS_RUNS = {
     "kbt_sgemm": [[], ["-m24", "-n40", "-p16"], ["-m136", "-n264", "-p8"]],
-    "kbt_gemm_add_relu": [[], ["-m24", "-n40", "-p16"]],
-    "kbt_gemm_mul_leakyrelu": [[], ["-m40", "-n24", "-p16"]],
+    "kbt_gemm_add_relu": [[], ["-m24", "-n40", "-p8"]],
+    "kbt_gemm_mul_leakyrelu": [[], ["-m40", "-n24", "-p8"]],
     "kbt_gemm_div_sum_scale": [[], ["-m64", "-n1024", "-p64"]],
     "kbt_gemm_layernorm": [[], ["-m64", "-n1024", "-p64"]],
     "kbt_attention_score": [[], ["-m64", "-n640", "-d64"]],
@@ -42,7 +42,10 @@ HARNESS_RUNS = {
     "kbt_matmul_sum_max_avgpool": [[], ["-m64", "-n640", "-p32"]],
     "kbt_gemm_rmsnorm_swiglu": [[], ["-m64", "-n256", "-p128"]],
     "kbt_gemm_silu_mul": [[], ["-m64", "-n256", "-p128"]],
-    "flash": [["-n", "64", "-d", "8", "-t", "1"], ["-n", "128", "-d", "16", "-t", "0"]],
+    # -t 1: the reference's fp16 tensor-core flash; -t 0: its fp32 SIMT flash
+    # (split-precision scores here), judged by the harness's own tolerance.
+    "flash": [["-n", "64", "-d", "8", "-t", "1"], ["-n", "128", "-d", "16", "-t", "0"],
+              ["-n", "256", "-d", "8", "-t", "0"]],
 }
 
 
@@ -79,7 +82,13 @@ def test_golden_vectors_through_plain_entry(oracle, path):
     abi.check(bench, arg)
     torch.cuda.synchronize()
     got = out.cpu().numpy()
-    ref = oracle_eval(oracle, bench, arg, d, round_inputs=True)
+    # The fp32 SIMT flash mode (kernel_type 0) keeps fp32-level scores: it is
+    # held to the reference gold itself; every other path to the oracle on
+    # the fp16-rounded operands the device uses.
+    if bench == "flash" and arg.kernel_type == 0:
+        ref = d["expected"]
+    else:
+        ref = oracle_eval(oracle, bench, arg, d, round_inputs=True)
     rows = d["expected"].size != arg.M if bench != "flash" else True
     shape = (-1, arg.head_dim) if bench == "flash" else ((arg.M, -1) if rows else (-1,))
     assert_parity(got.reshape(shape), ref.reshape(shape), rows=rows, what=bench)
