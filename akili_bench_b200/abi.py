@@ -143,6 +143,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.akili_workspace_bytes.restype = C.c_int
     L.akili_device_status.argtypes = [C.POINTER(C.c_uint32), C.c_int]
     L.akili_device_status.restype = C.c_int
+    L.akili_selftest_wait_timeout.argtypes = [C.c_uint32, C.c_void_p]
+    L.akili_selftest_wait_timeout.restype = C.c_int
     L.akili_launch_count.argtypes = []
     L.akili_launch_count.restype = C.c_uint64
     L.akili_abi_version.argtypes = []

@@ -836,6 +836,21 @@ int entry(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
   return run_job(j, md, S(s));
 }
 
+static_assert((0x1000u | kSiteSelfTest) == AKILI_STATUS_SELFTEST, "status code of the self-test wait");
+
+// One CTA waits on an mbarrier that nothing arrives at, bounded by limit_ns:
+// the wait gives up, records kSiteSelfTest and the kernel returns.
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ alignas(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_for(&bar, 0, kSiteSelfTest, limit_ns);
+  __syncthreads();
+}
+
 }  // namespace
 
 // ===================================================================== ABI ==
@@ -966,6 +981,15 @@ int akili_device_status(uint32_t* status, int clear) {
     if (cudaMemcpyToSymbol(g_status, &z, sizeof(z)) != cudaSuccess) return AKILI_E_LAUNCH;
   }
   return v ? AKILI_E_DEVICE_TIMEOUT : AKILI_OK;
+}
+
+int akili_selftest_wait_timeout(uint32_t limit_us, akili_stream_t s) {
+  if (limit_us == 0 || limit_us > 1000000u) return AKILI_E_SHAPE;
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  selftest_wait_kernel<<<1, 32, 0, S(s)>>>(uint64_t(limit_us) * 1000ull);
+  return launch_status();
 }
 
 uint64_t akili_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }

@@ -35,6 +35,7 @@ enum WaitSite : uint32_t {
   kSiteFlashPV = 9,
   kSiteFlashFree = 10,
   kSiteDrain = 11,
+  kSiteSelfTest = 12,
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -77,8 +78,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with the given parity to complete.  Returns false (and
-// records `site` in g_status) if it has not completed within kWaitTimeoutNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
+// records `site` in g_status) if it has not completed within `limit_ns`.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint32_t site,
+                                              uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -86,11 +88,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(a, parity)) return true;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > limit_ns) {
       record_timeout(site);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
+  return mbar_wait_for(bar, parity, site, kWaitTimeoutNs);
 }
 
 // -------------------------------------------------------------------- TMA --

@@ -216,6 +216,17 @@ def launch_count() -> int:
     return int(abi.load().akili_launch_count())
 
 
+def selftest_wait_timeout(limit_us: int, stream=None) -> None:
+    """Launch a kernel whose one wait can never complete; it gives up after
+    limit_us and records STATUS_SELFTEST in the device status word."""
+    rc = abi.load().akili_selftest_wait_timeout(int(limit_us), C.c_void_p(_stream(stream)))
+    if rc != abi.OK:
+        raise abi.AkiliError("selftest_wait_timeout", rc)
+
+
+STATUS_SELFTEST = 0x100C
+
+
 def device_status(clear: bool = True) -> int:
     v = C.c_uint32(0)
     abi.load().akili_device_status(C.byref(v), 1 if clear else 0)

@@ -283,6 +283,14 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
  * that gave up.  Synchronises the device. `clear` != 0 resets it. */
 int akili_device_status(uint32_t* status, int clear);
 
+/* Self-test of device-side failure detection: launches one CTA that waits
+ * on an mbarrier nothing arrives at, with a limit of `limit_us` microseconds
+ * (1..1000000).  The wait gives up, records AKILI_STATUS_SELFTEST in the
+ * status word and the kernel returns; the context stays usable.  Returns
+ * AKILI_OK once launched; read the outcome with akili_device_status(). */
+#define AKILI_STATUS_SELFTEST 0x100Cu
+int akili_selftest_wait_timeout(uint32_t limit_us, akili_stream_t stream);
+
 /* Number of kernel launches this library has issued in this process
  * (all devices).  For launch accounting in benchmarks. */
 uint64_t akili_launch_count(void);
