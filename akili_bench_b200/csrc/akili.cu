@@ -24,6 +24,7 @@
 #include "aux.cuh"
 #include "flash.cuh"
 #include "gemm.cuh"
+#include "softmax_rows.cuh"
 
 using namespace akili;
 
@@ -250,8 +251,13 @@ struct GemmJob {
   const float* ln_b = nullptr;
 };
 
+// Row softmax of a short-K product runs fused end to end (softmax_rows_kernel):
+// no partial statistics, no finaliser.
+bool softmax_fused(const GemmJob& j) { return j.epi == Epi::kSoftmaxPre && j.K <= static_cast<uint32_t>(kSmMaxK); }
+
 // Partial statistics: two slots (half tiles of BN/2 columns) per BN-column tile.
 size_t stats_bytes(const GemmJob& j) {
+  if (softmax_fused(j)) return 0;
   const int bn = epi_bn(j.epi);
   const size_t nt = 2 * ((j.N + bn - 1) / bn);
   return static_cast<size_t>(epi_stats(j.epi)) * nt * j.M * sizeof(float);
@@ -423,6 +429,51 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   return launch_status();
 }
 
+constexpr int kSmemOptin = 232448;  // 227 KB of dynamic shared memory per CTA (sm_100)
+
+template <typename OutT, bool BK>
+int launch_softmax_rows(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaStream_t st) {
+  CUtensorMap tmA, tmB, tmC;
+  const uint64_t M = j.M, N = j.N, K = j.K;
+  bool ok = map2d(&tmA, jb.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, K * 2, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (BK)
+    ok = ok && map2d(&tmB, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, N, K * 2, 64, 256, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    ok = ok && map2d(&tmB, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, K, N * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  // store boxes: 32 rows x 128 bytes (64 fp16 or 32 fp32 columns), one per warp
+  if (sizeof(OutT) == 2)
+    ok = ok && map2d(&tmC, j.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, N, M, N * 2, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    ok = ok && map2d(&tmC, j.C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, N, M, N * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok) return AKILI_E_LAUNCH;
+  SoftmaxRowsArgs p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.c = j.s0 * 1.4426950408889634f;
+  p.L = softmax_rows_layout(p.K, sizeof(OutT), kSmemOptin);
+  if (p.L.stages < 2) return AKILI_E_UNSUPPORTED;
+  auto kern = softmax_rows_kernel<OutT, BK>;
+  static std::mutex mu;
+  static std::map<int, bool> attr_done;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (!attr_done[dev]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptin) != cudaSuccess) {
+        cudaGetLastError();
+        return AKILI_E_LAUNCH;
+      }
+      attr_done[dev] = true;
+    }
+  }
+  const int blocks = static_cast<int>((M + kBM - 1) / kBM);
+  const int grid = blocks < di.sms ? blocks : di.sms;
+  kern<<<grid, kSmThreads, p.L.total, st>>>(tmA, tmB, tmC, p);
+  return launch_status();
+}
+
 template <Epi E, bool BK = false>
 int launch_gemm_out(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, bool out_f32, cudaStream_t st) {
   if constexpr (!epi_stores(E)) {
@@ -470,6 +521,13 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
     if (epi_dual(j.epi) && (rc = cast_to_f16(di, static_cast<const float*>(j.B1), jb.castB1, nB, st))) return rc;
   }
   // 2. the fused GEMM
+  if (softmax_fused(j)) {
+    if (md.out_f32)
+      return j.b_kmajor ? launch_softmax_rows<float, true>(di, j, jb, st)
+                        : launch_softmax_rows<float, false>(di, j, jb, st);
+    return j.b_kmajor ? launch_softmax_rows<__half, true>(di, j, jb, st)
+                      : launch_softmax_rows<__half, false>(di, j, jb, st);
+  }
   switch (j.epi) {
     case Epi::kPlain: rc = launch_gemm_out<Epi::kPlain>(di, j, jb, md.out_f32, st); break;
     case Epi::kBiasRelu: rc = launch_gemm_out<Epi::kBiasRelu>(di, j, jb, md.out_f32, st); break;

@@ -40,29 +40,6 @@ constexpr int kFlashQTiles = 2;
 constexpr int kFlashThreads = 64 + 128 * kFlashQTiles;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-// 2^x on the FMA pipe, to take part of the softmax's exponentials off the
-// MUFU unit (its throughput equals the tensor core's per key block here).
-// x = n + f with n = round(x) by the 1.5*2^23 magic-number addition and
-// f in [-0.5, 0.5]; 2^f by a cubic fitted for this kernel (iterated
-// reweighted least squares on the relative error: max 7.5e-5, well below
-// fp16's 4.9e-4 rounding of P); 2^n added into the exponent field.  Inputs
-// are clamped at -126, where the result is already below fp16's range.
-__device__ __forceinline__ float exp2_fma(float x) {
-  constexpr float kMagic = 12582912.0f;
-  x = fmaxf(x, -126.0f);
-  const float t = x + kMagic;
-  const float f = x - (t - kMagic);
-  const float p = fmaf(fmaf(fmaf(0.055174145847558975f, f, 0.24261757731437683f), f, 0.6932610869407654f), f,
-                       0.9999275803565979f);
-  return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - __float_as_int(kMagic)) << 23));
-}
-// 2^x by the MUFU unit in one instruction; results below the normal range
-// flush to zero (-inf gives 0), which fp16 P could not represent anyway.
-__device__ __forceinline__ float ex2_mufu(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 // Of each group of kExpGroup consecutive score pairs, the last is exponentiated
 // by exp2_fma, the others by the MUFU's exp2; 0 keeps every exponential on the
 // MUFU, which measured fastest once the softmax loop was trimmed (C5: 911 vs

@@ -549,7 +549,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* acc_empty = acc_full + 2;          // [2], used in the even CTA
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);  // one per epilogue group
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -573,7 +573,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&acc_empty[a], 16);  // one arrive per epilogue warp (8 per CTA) of both CTAs
     }
     mbar_init(drain, 1);
-    *abort_flag = 0;
+    abort_flag[0] = 0;
+    abort_flag[1] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -697,9 +698,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       tile_coords(tile, num_m, num_n, m_blk, n_blk);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) *abort_flag = 1;
+      // Each group reads only its own flag, after its own barrier, so all of
+      // its threads leave together.
+      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[grp] = 1;
       named_bar_sync(bar_id, 128);
-      if (*abort_flag) break;
+      if (abort_flag[grp]) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
       const int n0 = n_blk * BN;

@@ -36,6 +36,7 @@ enum WaitSite : uint32_t {
   kSiteFlashFree = 10,
   kSiteDrain = 11,
   kSiteSelfTest = 12,
+  kSiteExchange = 13,
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -392,6 +393,41 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t M, uint32_t N, bo
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; }
+
+// 2^x by the MUFU unit in one instruction; results below the normal range
+// flush to zero (-inf gives 0).
+__device__ __forceinline__ float ex2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x on the FMA pipe, to take part of a softmax's exponentials off the MUFU
+// unit.  x = n + f with n = round(x) by the 1.5*2^23 magic-number addition
+// and f in [-0.5, 0.5]; 2^f by a degree-5 polynomial fitted for this library
+// (iteratively reweighted least squares on the relative error, toward the
+// minimax fit: max relative error 2.1e-7 evaluated in fp32, about 2 ulp);
+// 2^n added into the exponent field.  Inputs are clamped at -126; below
+// that the result is negligible against any row sum.
+__device__ __forceinline__ float exp2_fma(float x) {
+  constexpr float kMagic = 12582912.0f;
+  x = fmaxf(x, -126.0f);
+  const float t = x + kMagic;
+  const float f = x - (t - kMagic);
+  float p = fmaf(0.0013276375830173492f, f, 0.00967551488429308f);
+  p = fmaf(p, f, 0.05550713464617729f);
+  p = fmaf(p, f, 0.24022120237350464f);
+  p = fmaf(p, f, 0.6931469440460205f);
+  p = fmaf(p, f, 1.0000001192092896f);
+  return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - __float_as_int(kMagic)) << 23));
+}
+
+// 2^x for two fp16 values in one MUFU instruction (x packed as fp16x2).
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
 
 // Pack two floats into fp16x2 (round to nearest even).
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

@@ -48,6 +48,9 @@ FLASH_SHAPE = [8, 32, 4096, 128]  # batch, heads, seq, head_dim; --
 NCU_TRAFFIC = {
     # profiles/gemm_pair_kernel_kbt_gemm_add_relu_8192x4096x4096.md: 171.7 MB read + 49.7 MB written
     "kbt_gemm_add_relu": 221.4e6,
+    # profiles/softmax_rows_kernel_kbt_attention_score_16384x4096x128.md: 5.5 MB read + 74.5 MB written
+    # (part of the output is still in L2 when the kernel ends)
+    "kbt_attention_score": 80.0e6,
 }
 
 
@@ -155,7 +158,7 @@ def workloads(torch, ops):
     W["kbt_attention_score"] = Workload(
         "kbt_attention_score", {"M": Ma, "N": Na, "D": Da}, 2.0 * Ma * Na * Da, as_make,
         lambda d, out, st: ops.kbt_attention_score(d["q"], d["k"], out=out, stream=st), bound="hbm",
-        io_bytes=2.0 * (Ma * Da + Na * Da) + 2.0 * Ma * Na)
+        io_bytes=2.0 * (Ma * Da + Na * Da) + 2.0 * Ma * Na, kernel="softmax_rows_kernel")
 
     def sg_make(gen):
         return {"a": (torch.rand((128, 128), generator=gen.x, device="cuda") * 2 - 1).to(f16),

@@ -89,8 +89,10 @@ def test_kbt_gemm_layernorm(oracle, M, N, K):
                                                  1e-5, out_dtype=dt), ref, what="layernorm")
 
 
+# D <= 256 runs the fused two-sweep kernel (softmax_rows_kernel); larger D the
+# GEMM with stored scores plus the finaliser.
 @pytest.mark.parametrize("M,N,D", [(16, 16, 8), (24, 40, 16), (200, 264, 64), (72, 1048, 128), (40, 4096, 128),
-                                   (520, 1000, 128)])
+                                   (520, 1000, 128), (136, 264, 256), (72, 520, 264)])
 def test_kbt_attention_score(oracle, M, N, D):
     rng = np.random.default_rng(13 * M + N)
     q, k = f16(rng, (M, D)), f16(rng, (N, D))
@@ -98,7 +100,11 @@ def test_kbt_attention_score(oracle, M, N, D):
     both_forms(lambda dt: ops.kbt_attention_score(dev(q, dt), dev(k, dt), out_dtype=dt), ref, what="attn_score")
 
 
-@pytest.mark.parametrize("M,N,K", ROW_SHAPES + [(200, 264, 136)])
+# K <= 256 is fused (both sweeps recompute the product); (136, 520, 1032) and
+# (264, 1040, 320) take the stored-scores path; 19456 rows are 152 row blocks,
+# more than one per SM.
+@pytest.mark.parametrize("M,N,K", ROW_SHAPES + [(200, 264, 136), (136, 520, 1032), (264, 1040, 320),
+                                                (19456, 264, 64)])
 def test_kbt_matmul_softmax(oracle, M, N, K):
     rng = np.random.default_rng(17 * M + N)
     a, b = f16(rng, (M, K)), f16(rng, (K, N), K ** -0.5)
