@@ -91,8 +91,7 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* k_empty = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* rel = bars + 5;       // [2] end of key-block iteration j -> rel[j & 1]
   uint64_t* s_full = bars + 9;    // [2] per Q tile
   uint64_t* p_full = bars + 11;   // [2] per Q tile
   uint64_t* o_done = bars + 13;   // [2] per Q tile
@@ -112,8 +111,7 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&rel[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 128);
       mbar_init(&o_done[s], 1);
@@ -150,14 +148,16 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, kSiteFlashFree)) break;
+        // K_j reuses the slot of K_j-2, free once iteration j-2 of the MMA
+        // loop has completed; V_j the slot of V_j-2, read in iteration j-1.
+        if (j >= 2 && !mbar_wait(&rel[st], ph ^ 1, kSiteFlashFree)) break;
         mbar_expect_tx(&k_full[st], L::kKV * L::kParts);
         for (int q = 0; q < kChunks; ++q) {
           tma_load_3d(sK + st * L::kKV + q * 16384, &tmK, &k_full[st], q * 64, j * kFlashBN, bh);
           if constexpr (kSplit)
             tma_load_3d(sK + (2 + st) * L::kKV + q * 16384, &tmKlo, &k_full[st], q * 64, j * kFlashBN, bh);
         }
-        if (!mbar_wait(&v_empty[st], ph ^ 1, kSiteFlashFree)) break;
+        if (j >= 2 && !mbar_wait(&rel[(j - 1) & 1], ((j - 1) >> 1) & 1, kSiteFlashFree)) break;
         mbar_expect_tx(&v_full[st], L::kKV);
         for (int q = 0; q < kChunks; ++q)
           tma_load_3d(sV + st * L::kKV + q * 16384, &tmV, &v_full[st], q * 64, j * kFlashBN, bh);
@@ -171,49 +171,62 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     bool ok = true;
     if (lane == 0) {
       ok = mbar_wait(q_full, 0, kSiteFlashQ);
-      // O_t += P_t,jj . V_jj for both tiles, then release V_jj's slot.
-      auto issue_pv = [&](int jj, int t) -> bool {
-        if (!mbar_wait(&p_full[t], jj & 1, kSiteFlashP)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + (jj & 1) * L::kKV);
-#pragma unroll
-        for (int k = 0; k < kFlashBN / 16; ++k)
-          umma_f16_ts(tmem + kColO + t * 128, tmem + t * 128 + k * 8,
-                      make_sdesc(v_addr + k * 2048, 16384, 1024, kSw128), idesc_o, (jj | k) != 0);
-        return true;
-      };
-      const uint32_t q_addr = smem_u32(sQ);
+      // Shared-memory descriptors are built once; the start-address field is
+      // (address >> 4) in the low bits, so an operand at byte offset `off`
+      // from a base is base descriptor + (off >> 4).  One MMA here is only
+      // 64 tensor cycles and the MMA queue is shallow, so the issuing thread
+      // keeps its own work between MMAs small: an add per operand, one
+      // batched wait at the top of each iteration and three commits.
+      const uint64_t qd0 = make_sdesc(smem_u32(sQ), 16, 1024, kSw128);
+      const uint64_t kd0 = make_sdesc(smem_u32(sK), 16, 1024, kSw128);
+      const uint64_t vd0 = make_sdesc(smem_u32(sV), 16384, 1024, kSw128);
       for (int j = 0; j <= nkv && ok; ++j) {
         const int st = j & 1;
-        if (j < nkv) ok = mbar_wait(&k_full[st], (j >> 1) & 1, kSiteFlashKV);
-        if (ok && j >= 1) ok = mbar_wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1, kSiteFlashKV);
-        for (int t = 0; t < kFlashQTiles && ok; ++t) {
+        const int jj = j - 1;  // the block whose P.V this iteration issues
+        // K_j, V_j-1 and P_0,j-1 in one wait; P_1,j-1 before its P.V.
+        ok = mbar_wait3(j < nkv ? &k_full[st] : nullptr, (j >> 1) & 1, j >= 1 ? &v_full[jj & 1] : nullptr,
+                        (jj >> 1) & 1, j >= 1 ? &p_full[0] : nullptr, jj & 1, kSiteFlashKV);
+        const uint64_t kd = kd0 + static_cast<uint64_t>((st * L::kKV) >> 4);
+        const uint64_t vd = vd0 + static_cast<uint64_t>(((jj & 1) * L::kKV) >> 4);
+#pragma unroll
+        for (int t = 0; t < kFlashQTiles; ++t) {
+          if (!ok) break;
           if (j >= 1) {
-            ok = issue_pv(j - 1, t);
+            // O_t += P_t,j-1 . V_j-1
+            if (t > 0) ok = mbar_wait(&p_full[t], jj & 1, kSiteFlashP);
             if (!ok) break;
+            tc_fence_after();
+            const uint32_t o_tmem = tmem + kColO + t * 128;
+            const uint32_t p_tmem = tmem + t * 128;
+#pragma unroll
+            for (int k = 0; k < kFlashBN / 16; ++k)
+              umma_f16_ts(o_tmem, p_tmem + k * 8, vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_o,
+                          (jj | k) != 0);
             if (j == nkv) umma_commit(&o_done[t]);
           }
           if (j < nkv) {
+            // S_t,j = Q_t . K_j^T
             tc_fence_after();
-            const uint32_t k_addr = smem_u32(sK + st * L::kKV);
+            const uint64_t qd = qd0 + static_cast<uint64_t>((t * L::kQ) >> 4);
+            const uint32_t s_tmem = tmem + t * 128;
 #pragma unroll
             for (int k = 0; k < DP / 16; ++k) {
-              const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-              const uint64_t qh = make_sdesc(q_addr + t * L::kQ + off, 16, 1024, kSw128);
-              const uint64_t kh = make_sdesc(k_addr + off, 16, 1024, kSw128);
-              umma_f16_ss(tmem + t * 128, qh, kh, idesc_s, k != 0);
+              const uint64_t off = static_cast<uint64_t>(((k >> 2) * 16384 + (k & 3) * 32) >> 4);
+              const uint64_t qh = qd + off;
+              const uint64_t kh = kd + off;
+              umma_f16_ss(s_tmem, qh, kh, idesc_s, k != 0);
               if constexpr (kSplit) {
-                umma_f16_ss(tmem + t * 128, qh, make_sdesc(k_addr + 2 * L::kKV + off, 16, 1024, kSw128), idesc_s, 1);
-                umma_f16_ss(tmem + t * 128, make_sdesc(q_addr + (kFlashQTiles + t) * L::kQ + off, 16, 1024, kSw128),
-                            kh, idesc_s, 1);
+                umma_f16_ss(s_tmem, qh, kh + static_cast<uint64_t>((2 * L::kKV) >> 4), idesc_s, 1);
+                umma_f16_ss(s_tmem, qh + static_cast<uint64_t>((kFlashQTiles * L::kQ) >> 4), kh, idesc_s, 1);
               }
             }
             umma_commit(&s_full[t]);
           }
         }
         if (!ok) break;
-        if (j >= 1) umma_commit(&v_empty[(j - 1) & 1]);
-        if (j < nkv) umma_commit(&k_empty[st]);
+        // K_j (read by S_t,j) and V_j-1 (read by P_t,j-1 . V_j-1) are free once
+        // this iteration's MMAs complete.
+        umma_commit(&rel[st]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, kSiteDrain);

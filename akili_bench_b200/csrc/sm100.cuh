@@ -99,6 +99,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return mbar_wait_for(bar, parity, site, kWaitTimeoutNs);
 }
 
+// Wait for up to three barrier phases at once: the try_waits are issued back
+// to back so their latencies overlap (a barrier with bar == nullptr is skipped).
+__device__ __forceinline__ bool mbar_wait3(uint64_t* b0, uint32_t p0, uint64_t* b1, uint32_t p1, uint64_t* b2,
+                                           uint32_t p2, uint32_t site) {
+  const bool r0 = b0 == nullptr || mbar_try_wait(smem_u32(b0), p0);
+  const bool r1 = b1 == nullptr || mbar_try_wait(smem_u32(b1), p1);
+  const bool r2 = b2 == nullptr || mbar_try_wait(smem_u32(b2), p2);
+  if (r0 && r1 && r2) return true;
+  return (r0 || mbar_wait(b0, p0, site)) && (r1 || mbar_wait(b1, p1, site)) && (r2 || mbar_wait(b2, p2, site));
+}
+
 // -------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
