@@ -135,6 +135,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         fx = getattr(L, f"akili_{name}_ex")
         fx.argtypes = [C.POINTER(st), C.POINTER(AkiliEx), C.c_void_p]
         fx.restype = C.c_int
+    L.akili_flash_ml_ex.argtypes = [C.POINTER(FlashArg), C.POINTER(AkiliEx), C.c_uint64, C.c_uint64, C.c_void_p]
+    L.akili_flash_ml_ex.restype = C.c_int
     L.akili_kbt_gemm_layernorm_noalloc.argtypes = [C.POINTER(KbtGemmLayernormArg), C.POINTER(AkiliEx), C.c_void_p]
     L.akili_kbt_gemm_layernorm_noalloc.restype = C.c_int
     L.akili_strerror.argtypes = [C.c_int]
@@ -154,8 +156,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
 
 
 def make_ex(in_dtype=DTYPE_F16, out_dtype=DTYPE_F16, batch=0, heads=0, softmax_scale=0.0,
-            workspace=0, workspace_bytes=0) -> AkiliEx:
-    return AkiliEx(ABI_VERSION, in_dtype, out_dtype, batch, heads, softmax_scale, 0, 0, workspace,
+            workspace=0, workspace_bytes=0, causal=0) -> AkiliEx:
+    return AkiliEx(ABI_VERSION, in_dtype, out_dtype, batch, heads, softmax_scale, causal, 0, workspace,
                    workspace_bytes)
 
 

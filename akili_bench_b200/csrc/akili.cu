@@ -38,6 +38,7 @@ struct Mode {
   bool out_f32 = true;
   uint32_t batch = 1, heads = 1;
   float scale = 1.0f;
+  bool causal = false;  // flash only
   void* workspace = nullptr;
   uint64_t workspace_bytes = 0;
 };
@@ -47,7 +48,8 @@ int parse_ex(const akili_ex_t* ex, Mode* md) {
   if (!ex) return AKILI_OK;
   if (ex->abi_version != AKILI_ABI_VERSION) return AKILI_E_ABI;
   if (ex->in_dtype > AKILI_DTYPE_F16 || ex->out_dtype > AKILI_DTYPE_F16) return AKILI_E_DTYPE;
-  if (ex->causal != 0 || ex->flags != 0) return AKILI_E_UNSUPPORTED;
+  if (ex->causal > 1 || ex->flags != 0) return AKILI_E_UNSUPPORTED;
+  md->causal = ex->causal == 1;
   md->in_f32 = ex->in_dtype == AKILI_DTYPE_F32;
   md->out_f32 = ex->out_dtype == AKILI_DTYPE_F32;
   md->batch = ex->batch ? ex->batch : 1;
@@ -751,6 +753,8 @@ struct FlashJob {
   uint32_t kernel_type = 1;  // 0: the reference's fp32 SIMT flash, 1: its fp16 tensor-core flash
   const void *Q = nullptr, *K = nullptr, *V = nullptr;
   void* O = nullptr;
+  float* m_out = nullptr;  // optional row statistics (akili_flash_ml_ex)
+  float* l_out = nullptr;
 };
 
 // fp32 operands with the reference's SIMT kernel type (fp32 arithmetic,
@@ -840,6 +844,9 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
   fa.seq_len = static_cast<int>(j.seq_len);
   fa.head_dim = static_cast<int>(D);
   fa.scale_log2 = md.scale * 1.4426950408889634f;
+  fa.causal = md.causal ? 1 : 0;
+  fa.m_out = j.m_out;
+  fa.l_out = j.l_out;
   dim3 grid((j.seq_len + kFlashBM * kFlashQTiles - 1) / (kFlashBM * kFlashQTiles), bh);
   if (split) rc = launch_flash<64, true>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
   else if (dpad == 64) rc = launch_flash<64, false>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
@@ -887,6 +894,7 @@ int entry(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
   Mode md;
   int rc = parse_ex(ex, &md);
   if (rc) return rc;
+  if (md.causal) return AKILI_E_UNSUPPORTED;  // a mask has no meaning for the GEMM ops
   if (!a) return AKILI_E_NULL_ARG;
   GemmJob j;
   // An empty batch (M == 0) is a no-op; its buffers may legitimately be null.
@@ -944,7 +952,7 @@ int akili_kbt_gemm_layernorm_noalloc(const kbt_gemm_layernorm_arg_t* a, const ak
   int rc = parse_ex(ex, &md);
   if (rc) return rc;
   if (md.in_f32) return AKILI_E_DTYPE;
-  if (md.workspace) return AKILI_E_UNSUPPORTED;
+  if (md.workspace || md.causal) return AKILI_E_UNSUPPORTED;
   if (!a) return AKILI_E_NULL_ARG;
   GemmJob j;
   if ((rc = job_layernorm(a, j, a->M != 0))) return rc;
@@ -966,6 +974,20 @@ int akili_flash_ex(const flash_arg_t* a, const akili_ex_t* ex, akili_stream_t s)
   return run_flash(j, md, S(s));
 }
 int akili_flash(const flash_arg_t* a, akili_stream_t s) { return akili_flash_ex(a, nullptr, s); }
+
+int akili_flash_ml_ex(const flash_arg_t* a, const akili_ex_t* ex, uint64_t m_addr, uint64_t l_addr,
+                      akili_stream_t s) {
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  FlashJob j;
+  if ((rc = job_flash(a, j))) return rc;
+  if (!m_addr || !l_addr) return AKILI_E_NULL_ARG;
+  if ((m_addr | l_addr) % 4) return AKILI_E_ALIGN;
+  j.m_out = reinterpret_cast<float*>(static_cast<uintptr_t>(m_addr));
+  j.l_out = reinterpret_cast<float*>(static_cast<uintptr_t>(l_addr));
+  return run_flash(j, md, S(s));
+}
 
 const char* akili_strerror(int code) {
   switch (code) {

@@ -53,6 +53,9 @@ struct FlashArgs {
   int seq_len;
   int head_dim;
   float scale_log2;  // softmax scale * log2(e)
+  int causal;        // 1: query i sees keys j <= i only
+  float* m_out;      // optional [bh][seq_len]: row max of the scaled scores
+  float* l_out;      // optional [bh][seq_len]: sum_j exp(score_j - m)
 };
 
 // kSplit: Q and K also carry their fp16 low parts (x - fp16(x)), doubling
@@ -100,8 +103,12 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);  // [2]
 
   const int N = fa.seq_len;
-  const int nkv = (N + kFlashBN - 1) / kFlashBN;
   const int m0 = blockIdx.x * (kFlashBM * kFlashQTiles);
+  // Causal: this CTA's queries end at m0 + 255, so key blocks past that are
+  // never visited (benchmarks/cupbop_dao_flash/dao_flash_cupbop.cu:64-71 skips
+  // them the same way); keys after a row's own index are masked per row.
+  const int nkv_all = (N + kFlashBN - 1) / kFlashBN;
+  const int nkv = fa.causal ? min(nkv_all, (m0 + kFlashBM * kFlashQTiles + kFlashBN - 1) / kFlashBN) : nkv_all;
   const int bh = blockIdx.y;
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -244,7 +251,9 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     const uint32_t tO = tmem + lane_off + kColO + grp * 128;
     const float sl = fa.scale_log2;
     float m_use = -INFINITY;
+    float m_true = -INFINITY;  // the row's exact running max (m_use may lag it by the rescale threshold)
     float l = 0.0f;
+    const int qrow = m0 + grp * kFlashBM + r;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait(&s_full[grp], j & 1, kSiteFlashS)) abort_flag[grp] = 1;
@@ -259,7 +268,9 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       // the log2 domain (keys past the end are masked).
       float s[128];
       tmem_ld128(tS, s);
-      const int nvalid = N - kv0;  // >= 1
+      // keys of this block the row may see: all but those past the end and,
+      // when causal, those after the row's own index (may be <= 0)
+      const int nvalid = fa.causal ? min(N - kv0, qrow - kv0 + 1) : N - kv0;
       // Row max of the raw scores (the scale is positive, so it commutes with
       // max); keys past the end exist only in the last block and are set to
       // -inf there, so full blocks carry no per-element masking.
@@ -278,6 +289,7 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       }
       const float rmax = sl * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      m_true = fmaxf(m_true, rmax);
       const bool grow = rmax > m_use + kRescaleThreshold;
       const float m_new = grow ? rmax : m_use;
       const float alpha = grow ? exp2f(m_use - m_new) : 1.0f;  // 0 on the first block
@@ -313,6 +325,12 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       mbar_arrive(&p_full[grp]);
       l = l * alpha + rsum;
       m_use = m_new;
+    }
+    if (ok && fa.m_out != nullptr && qrow < N) {
+      // softmax statistics in the reference's natural-log form
+      const size_t o = static_cast<size_t>(bh) * N + qrow;
+      fa.m_out[o] = m_true * 0.6931471805599453f;
+      fa.l_out[o] = l * exp2f(m_use - m_true);
     }
     if (ok && nkv >= 1) {
       if (!mbar_wait(&o_done[grp], 0, kSiteFlashPV)) abort_flag[grp] = 1;

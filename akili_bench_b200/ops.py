@@ -187,12 +187,16 @@ def kbt_gemm_silu_mul(x, wa, ba, wb, bb, out=None, out_dtype=None, stream=None):
     return c
 
 
-def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None, kernel_type=1):
+def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None, kernel_type=1, causal=False,
+          return_stats=False):
     """q/k/v [S, D] (one head, reference layout) or [B, H, S, D].
 
     kernel_type follows the reference's flash_arg_t: 1 = its fp16 tensor-core
     flash (operands rounded to fp16), 0 = its fp32 SIMT flash (with fp32
-    inputs the scores are computed in split precision)."""
+    inputs the scores are computed in split precision).  causal=True masks
+    keys after each query (cupbop_dao_flash).  return_stats=True also returns
+    the per-row softmax statistics (m, l), fp32 shaped like q without its
+    last dimension: m = row max of the scaled scores, l = sum exp(score - m)."""
     if q.dim() == 2:
         B, H, (S, D) = 1, 1, q.shape
     else:
@@ -206,10 +210,18 @@ def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None, ke
     arg.block_size_r = arg.block_size_c = 8
     arg.Q_addr, arg.K_addr, arg.V_addr, arg.O_addr = _addr(q), _addr(k), _addr(v), _addr(o)
     extra = None
-    if B * H != 1 or softmax_scale is not None:
-        extra = {"batch": B, "heads": H, "softmax_scale": float(softmax_scale or 0.0)}
-    _launch("flash", arg, q, o, stream, ex_extra=extra)
-    return o
+    if B * H != 1 or softmax_scale is not None or causal:
+        extra = {"batch": B, "heads": H, "softmax_scale": float(softmax_scale or 0.0), "causal": int(causal)}
+    if not return_stats:
+        _launch("flash", arg, q, o, stream, ex_extra=extra)
+        return o
+    m = torch.empty(q.shape[:-1], device=q.device, dtype=torch.float32)
+    l = torch.empty(q.shape[:-1], device=q.device, dtype=torch.float32)
+    ex = abi.make_ex(_dt(q), _dt(o), **(extra or {}))
+    rc = abi.load().akili_flash_ml_ex(C.byref(arg), C.byref(ex), _addr(m), _addr(l), C.c_void_p(_stream(stream)))
+    if rc != abi.OK:
+        raise abi.AkiliError("flash_ml_ex", rc)
+    return o, m, l
 
 
 def launch_count() -> int:

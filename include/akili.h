@@ -54,7 +54,7 @@ typedef struct CUstream_st* akili_stream_t;
 #define AKILI_E_SHAPE            (-2)  /* a size is 0 (other than M) or not a multiple of 8 */
 #define AKILI_E_ALIGN            (-3)  /* a buffer address is not 16-byte aligned           */
 #define AKILI_E_DTYPE            (-4)  /* unsupported in_dtype / out_dtype                  */
-#define AKILI_E_UNSUPPORTED      (-5)  /* e.g. causal=1, head_dim > 128                     */
+#define AKILI_E_UNSUPPORTED      (-5)  /* e.g. causal=1 on a GEMM op, head_dim > 128        */
 #define AKILI_E_NO_DEVICE        (-6)  /* current device is not an sm_100 part              */
 #define AKILI_E_ALLOC            (-7)  /* internal scratch pool could not grow              */
 #define AKILI_E_LAUNCH           (-8)  /* a CUDA launch or tensor-map encode failed         */
@@ -185,7 +185,7 @@ typedef struct {
   uint32_t batch;           /* flash: batch size (0 means 1)                               */
   uint32_t heads;           /* flash: heads per batch entry (0 means 1)                    */
   float    softmax_scale;   /* flash: scale of Q.K^T, >= 0 (0 means 1: the unscaled reference) */
-  uint32_t causal;          /* reserved; must be 0                                         */
+  uint32_t causal;          /* flash: 1 masks key j > query i; must be 0 for the other ops */
   uint32_t flags;           /* reserved; must be 0                                         */
   uint64_t workspace;       /* optional device scratch; 0 means the internal pool          */
   uint64_t workspace_bytes; /* size of `workspace`                                         */
@@ -267,6 +267,17 @@ int akili_kbt_gemm_silu_mul_ex(const kbt_gemm_silu_mul_arg_t* arg, const akili_e
 /* flash/main.cpp:299-307, device entry flash_kernel_entry flash/kernel.cpp:344-417 */
 int akili_flash(const flash_arg_t* arg, akili_stream_t stream);
 int akili_flash_ex(const flash_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
+/* Flash forward that also writes each query row's softmax statistics, as
+ * the reference's flash kernels keep them in their l and m buffers
+ * (benchmarks/cupbop_fmha/fmha_cupbop.cu:42,115-116 and
+ * benchmarks/cupbop_dao_flash/dao_flash_cupbop.cu:38,124-125):
+ *   m[bh][i] = max_j score_ij,  l[bh][i] = sum_j exp(score_ij - m[bh][i]),
+ * score = softmax_scale * Q_i.K_j over the keys the row sees (all, or j <= i
+ * with ex->causal = 1).  m_addr and l_addr are device fp32 arrays of
+ * batch*heads*seq_len entries, 4-byte aligned; logsumexp = m + log(l). */
+int akili_flash_ml_ex(const flash_arg_t* arg, const akili_ex_t* ex, uint64_t m_addr, uint64_t l_addr,
+                      akili_stream_t stream);
 
 /* ---- runtime helpers (no counterpart in the reference beyond RT_CHECK) --- */
 

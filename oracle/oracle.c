@@ -273,6 +273,45 @@ void oracle_flash(float* out, const float* q, const float* k, const float* v, ui
   free(probs);
 }
 
+/* benchmarks/cupbop_dao_flash/dao_flash_cupbop.cu:135-168 (attention_cpu
+ * with its causal mask: key j > query i scores -1e30f), per query row, with
+ * the scale as a parameter.  When m_out / l_out are non-null the row's
+ * softmax statistics are written as the reference kernel keeps them
+ * (dao_flash_cupbop.cu:111-125, fmha_cupbop.cu:115-116): m = the row maximum
+ * of the scaled scores, l = sum_j exp(score_j - m) (masked keys add 0). */
+void oracle_flash_causal(float* out, float* m_out, float* l_out, const float* q, const float* k, const float* v,
+                         uint32_t seq_len, uint32_t d, float scale, uint32_t causal, uint32_t row0, uint32_t row1) {
+  uint32_t N = seq_len;
+  float* scores = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    float max_s = -1e30f;
+    for (uint32_t j = 0; j < N; ++j) {
+      if (causal && j > i) {
+        scores[j] = -1e30f;
+      } else {
+        float sum = 0.0f;
+        for (uint32_t kk = 0; kk < d; ++kk) sum += q[(uint64_t)i * d + kk] * k[(uint64_t)j * d + kk];
+        scores[j] = sum * scale;
+      }
+      if (scores[j] > max_s) max_s = scores[j];
+    }
+    float sum_exp = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      scores[j] = expf(scores[j] - max_s);
+      sum_exp += scores[j];
+    }
+    if (m_out) m_out[i] = max_s;
+    if (l_out) l_out[i] = sum_exp;
+    for (uint32_t j = 0; j < N; ++j) scores[j] /= sum_exp;
+    for (uint32_t kk = 0; kk < d; ++kk) {
+      float val = 0.0f;
+      for (uint32_t j = 0; j < N; ++j) val += scores[j] * v[(uint64_t)j * d + kk];
+      out[(uint64_t)i * d + kk] = val;
+    }
+  }
+  free(scores);
+}
+
 /* IEEE binary16 round-to-nearest-even, as the reference's f2h (`(__fp16)x`,
  * benchmarks/kbt_sgemm/kernel.cpp:13-18) and CUDA's __float2half_rn do.
  * Written from the format definition: 1 sign, 5 exponent (bias 15),

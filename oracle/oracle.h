@@ -62,6 +62,8 @@ void oracle_kbt_gemm_silu_mul(const float* a, const float* wa, const float* ba, 
  * product; 1.0f reproduces the reference (which has no scale). */
 void oracle_flash(float* out, const float* q, const float* k, const float* v, uint32_t seq_len,
                   uint32_t d, float scale, uint32_t row0, uint32_t row1);
+void oracle_flash_causal(float* out, float* m_out, float* l_out, const float* q, const float* k, const float* v,
+                         uint32_t seq_len, uint32_t d, float scale, uint32_t causal, uint32_t row0, uint32_t row1);
 
 /* Helpers used by tests to reproduce the device's operand rounding. */
 float oracle_round_f16(float x);                 /* fp32 -> nearest-even fp16 -> fp32 */

@@ -34,6 +34,7 @@ _SIGS = {
     "oracle_kbt_gemm_rmsnorm_swiglu": [_f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _u32, _u32],
     "oracle_kbt_gemm_silu_mul": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_flash": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _f, _u32, _u32],
+    "oracle_flash_causal": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _f, _u32, _u32, _u32],
     "oracle_round_f16_array": [_f32p, C.c_uint64],
 }
 
@@ -183,3 +184,16 @@ def flash(q, k, v, seq_len, d, scale=1.0, row0=0, row1=None, threads=1, out=None
     o = _out((seq_len, d), out)
     _rows(lib().oracle_flash, (_p(o), _p(q), _p(k), _p(v)), (seq_len, d, scale), row0, row1, threads)
     return o
+
+
+def flash_causal(q, k, v, seq_len, d, scale=1.0, causal=True, row0=0, row1=None, threads=1):
+    """One head with the optional causal mask; returns (o, m, l): o [seq_len x d]
+    and the per-row softmax statistics m, l [seq_len] (rows outside
+    [row0, row1) are zero)."""
+    row1 = seq_len if row1 is None else row1
+    o = _out((seq_len, d), None)
+    m = np.zeros(seq_len, np.float32)
+    l = np.zeros(seq_len, np.float32)
+    _rows(lib().oracle_flash_causal, (_p(o), _p(m), _p(l), _p(q), _p(k), _p(v)),
+          (seq_len, d, scale, 1 if causal else 0), row0, row1, threads)
+    return o, m, l

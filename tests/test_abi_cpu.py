@@ -26,7 +26,7 @@ def exported(lib: str) -> set[str]:
 
 def test_libakili_exports_every_declared_entry():
     names = declared("akili.h", "akili_")
-    assert len(names) == 24 + 1 + 6  # ops, the no-alloc LayerNorm, runtime helpers
+    assert len(names) == 24 + 1 + 1 + 6  # ops, flash statistics, the no-alloc LayerNorm, runtime helpers
     missing = names - exported(abi.LIB_PATH)
     assert not missing, missing
     L = abi.load()
@@ -99,6 +99,13 @@ def test_validation_codes_before_any_cuda_call():
     assert abi.call("flash", f) == abi.E_UNSUPPORTED
     f.head_dim = 12
     assert abi.call("flash", f) == abi.E_SHAPE
+    # causal is a flash option (0 or 1); the statistics entry needs both buffers
+    f.head_dim = 64
+    ex = abi.make_ex(causal=2)
+    assert abi.call("flash", f, ex) == abi.E_UNSUPPORTED
+    ex = abi.make_ex(causal=1)
+    assert L.akili_flash_ml_ex(C.byref(f), C.byref(ex), 0, 0x5000, None) == abi.E_NULL_ARG
+    assert L.akili_flash_ml_ex(C.byref(f), C.byref(ex), 0x5002, 0x6000, None) == abi.E_ALIGN
 
 
 def test_valid_args_without_a_gpu_report_no_device():

@@ -91,3 +91,56 @@ def test_flash_fp32_simt_mode_matches_unrounded_gold(oracle, S, D):
     assert_parity(got, ref, what=f"flash fp32 simt S={S} D={D}")
     # and the reference harness's own per-element bound (flash/main.cpp:37-49)
     assert (np.abs(got - ref) <= 5e-2 + 1e-2 * np.abs(got)).all()
+
+
+def _heads(oracle, q, k, v, scale, causal):
+    B, H, S, D = q.shape
+    o = np.zeros_like(q)
+    m = np.zeros((B, H, S), np.float32)
+    l = np.zeros((B, H, S), np.float32)
+    for b in range(B):
+        for h in range(H):
+            o[b, h], m[b, h], l[b, h] = oracle.flash_causal(q[b, h].copy(), k[b, h].copy(), v[b, h].copy(), S, D,
+                                                            scale, causal=causal)
+    return o, m, l
+
+
+# S values that are not multiples of the 256-query CTA tile or the 128-key
+# block exercise the diagonal and the tails together.
+@pytest.mark.parametrize("B,H,S,D", [(1, 2, 256, 128), (2, 1, 300, 64), (1, 1, 520, 128), (1, 3, 136, 8),
+                                     (1, 1, 1024, 128)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_causal_and_row_statistics(oracle, B, H, S, D, causal):
+    """cupbop_dao_flash semantics (key j > query i masked) and the m/l row
+    statistics of its kernel, against the oracle on the same fp16 operands."""
+    rng = np.random.default_rng(B * 100 + S + D + causal)
+    q, k, v = f16(rng, (B, H, S, D)), f16(rng, (B, H, S, D)), f16(rng, (B, H, S, D))
+    scale = D ** -0.5
+    ref_o, ref_m, ref_l = _heads(oracle, q, k, v, scale, causal)
+    got_o, got_m, got_l = ops.flash(dev(q, torch.float16), dev(k, torch.float16), dev(v, torch.float16),
+                                    softmax_scale=scale, out_dtype=torch.float32, causal=causal, return_stats=True)
+    assert ops.device_status() == 0
+    got_o = got_o.cpu().numpy()
+    for b in range(B):
+        for h in range(H):
+            assert_parity(got_o[b, h], ref_o[b, h], what=f"flash causal={causal} b={b} h={h}")
+    np.testing.assert_allclose(got_m.cpu().numpy(), ref_m, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(got_l.cpu().numpy(), ref_l, rtol=2e-3)
+    if causal:  # the first query sees only the first key
+        np.testing.assert_allclose(got_o[:, :, 0], v[:, :, 0], rtol=0, atol=1e-6)
+        np.testing.assert_allclose(got_l.cpu().numpy()[:, :, 0], 1.0, rtol=1e-6)
+
+
+def test_flash_causal_fp32_reference_semantics(oracle):
+    """fp32 buffers with the fp32 SIMT kernel type (split-precision scores),
+    unscaled, one head, causal: held to the unrounded fp32 oracle."""
+    S, D = 200, 16
+    rng = np.random.default_rng(11)
+    q, k, v = (rng.standard_normal((S, D), dtype=np.float32) for _ in range(3))
+    ref_o, ref_m, ref_l = oracle.flash_causal(q, k, v, S, D, 1.0, causal=True)
+    got_o, got_m, got_l = ops.flash(dev(q, torch.float32), dev(k, torch.float32), dev(v, torch.float32),
+                                    kernel_type=0, causal=True, return_stats=True)
+    assert ops.device_status() == 0
+    assert_parity(got_o.cpu().numpy(), ref_o, what="flash causal fp32")
+    np.testing.assert_allclose(got_m.cpu().numpy(), ref_m, rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(got_l.cpu().numpy(), ref_l, rtol=2e-3)

@@ -104,3 +104,25 @@ def test_exact_pin_negative_controls(bench):
     assert "FAILED!" in out and "PASSED!" not in out
     rc, out = _pin(bench, argv, AKILI_HOST_DEVICE="oracle_ulp")
     assert "Found 1 errors!" in out and "FAILED!" in out
+
+
+@pytest.mark.parametrize("S,D", [(1, 8), (37, 16), (130, 64)])
+def test_causal_flash_oracle_known_answers(oracle, S, D):
+    """dao_flash causal semantics: row 0 attends to key 0 only (O = V[0]); the
+    last row sees every key (equals the non-causal row); without the mask the
+    function is the plain flash oracle.  m/l are the row max and sum of exp."""
+    rng = np.random.default_rng(S * 7 + D)
+    q, k, v = (rng.standard_normal((S, D), dtype=np.float32) for _ in range(3))
+    scale = D ** -0.5
+    o_c, m_c, l_c = oracle.flash_causal(q, k, v, S, D, scale, causal=True)
+    o_n, m_n, l_n = oracle.flash_causal(q, k, v, S, D, scale, causal=False)
+    assert np.array_equal(o_n, oracle.flash(q, k, v, S, D, scale))
+    assert np.array_equal(o_c[0], v[0])
+    assert np.array_equal(o_c[-1], o_n[-1]) and m_c[-1] == m_n[-1] and l_c[-1] == l_n[-1]
+    s64 = (q.astype(np.float64) @ k.astype(np.float64).T) * scale
+    mask = np.triu(np.ones((S, S), bool), 1)
+    s64c = np.where(mask, -np.inf, s64)
+    np.testing.assert_allclose(m_c, s64c.max(1), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(l_c, np.exp(s64c - s64c.max(1, keepdims=True)).sum(1), rtol=1e-4)
+    p = np.exp(s64c - s64c.max(1, keepdims=True))
+    np.testing.assert_allclose(o_c, (p / p.sum(1, keepdims=True)) @ v, rtol=1e-4, atol=1e-5)
