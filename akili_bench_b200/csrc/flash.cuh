@@ -103,7 +103,10 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);  // [2]
 
   const int N = fa.seq_len;
-  const int m0 = blockIdx.x * (kFlashBM * kFlashQTiles);
+  // Causal: the CTA of query tile pair x visits 2x + 2 key blocks, so the
+  // pairs are handed out last first (the longest CTAs start earliest).
+  const int pair = fa.causal ? static_cast<int>(gridDim.x - 1 - blockIdx.x) : static_cast<int>(blockIdx.x);
+  const int m0 = pair * (kFlashBM * kFlashQTiles);
   // Causal: this CTA's queries end at m0 + 255, so key blocks past that are
   // never visited (benchmarks/cupbop_dao_flash/dao_flash_cupbop.cu:64-71 skips
   // them the same way); keys after a row's own index are masked per row.
