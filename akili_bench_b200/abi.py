@@ -100,6 +100,55 @@ class AkiliEx(C.Structure):  # include/akili.h akili_ex_t
                 ("workspace", _u64), ("workspace_bytes", _u64)]
 
 
+# ---- kb2_* structs (benchmarks/kb2_<bench>/common.h): no launch fields ----
+_MNK = [("M", _u32), ("N", _u32), ("K", _u32)]
+
+
+class Kb2GemmAddReluArg(C.Structure):  # benchmarks/kb2_gemm_add_relu/common.h
+    _fields_ = _MNK + [("a_addr", _u64), ("w_addr", _u64), ("bias_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2GemmMulLeakyreluArg(C.Structure):  # benchmarks/kb2_gemm_mul_leakyrelu/common.h
+    _fields_ = _MNK + [("multiplier", _f), ("negative_slope", _f), ("a_addr", _u64), ("w_addr", _u64),
+                       ("bias_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2GemmDivSumScaleArg(C.Structure):  # benchmarks/kb2_gemm_div_sum_scale/common.h
+    _fields_ = _MNK + [("scaling_factor", _f), ("a_addr", _u64), ("w_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2GemmLayernormArg(C.Structure):  # benchmarks/kb2_gemm_layernorm/common.h
+    _fields_ = _MNK + [("eps", _f), ("a_addr", _u64), ("w_addr", _u64), ("bias_addr", _u64), ("ln_w_addr", _u64),
+                       ("ln_b_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2AttentionScoreArg(C.Structure):  # benchmarks/kb2_attention_score/common.h
+    _fields_ = [("M", _u32), ("N", _u32), ("D", _u32), ("q_addr", _u64), ("k_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2MatmulSoftmaxArg(C.Structure):  # benchmarks/kb2_matmul_softmax/common.h
+    _fields_ = _MNK + [("a_addr", _u64), ("b_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2MatmulScaleResidaddClampArg(C.Structure):  # benchmarks/kb2_matmul_scale_residadd_clamp/common.h
+    _fields_ = _MNK + [("scale_factor", _f), ("clamp_min", _f), ("clamp_max", _f), ("a_addr", _u64),
+                       ("w_addr", _u64), ("bias_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2MatmulSumMaxAvgpoolArg(C.Structure):  # benchmarks/kb2_matmul_sum_max_avgpool/common.h
+    _fields_ = _MNK + [("a_addr", _u64), ("w_addr", _u64), ("bias_addr", _u64), ("c_addr", _u64)]
+
+
+class Kb2GemmRmsnormSwigluArg(C.Structure):  # benchmarks/kb2_gemm_rmsnorm_swiglu/common.h
+    _fields_ = _MNK + [("eps", _f), ("x_addr", _u64), ("rms_w_addr", _u64), ("wg_addr", _u64), ("wu_addr", _u64),
+                       ("c_addr", _u64)]
+
+
+class Kb2GemmSiluMulArg(C.Structure):  # benchmarks/kb2_gemm_silu_mul/common.h
+    _fields_ = _MNK + [("a_addr", _u64), ("wa_addr", _u64), ("ba_addr", _u64), ("wb_addr", _u64), ("bb_addr", _u64),
+                       ("c_addr", _u64)]
+
+
 # name -> (struct, buffer fields in harness upload order + outputs, sizeof in the reference)
 OPS = {
     "kbt_sgemm": (KbtSgemmArg, 64),
@@ -114,6 +163,16 @@ OPS = {
     "kbt_gemm_rmsnorm_swiglu": (KbtGemmRmsnormSwigluArg, 96),
     "kbt_gemm_silu_mul": (KbtGemmSiluMulArg, 96),
     "flash": (FlashArg, 64),
+    "kb2_gemm_add_relu": (Kb2GemmAddReluArg, 48),
+    "kb2_gemm_mul_leakyrelu": (Kb2GemmMulLeakyreluArg, 56),
+    "kb2_gemm_div_sum_scale": (Kb2GemmDivSumScaleArg, 40),
+    "kb2_gemm_layernorm": (Kb2GemmLayernormArg, 64),
+    "kb2_attention_score": (Kb2AttentionScoreArg, 40),
+    "kb2_matmul_softmax": (Kb2MatmulSoftmaxArg, 40),
+    "kb2_matmul_scale_residadd_clamp": (Kb2MatmulScaleResidaddClampArg, 56),
+    "kb2_matmul_sum_max_avgpool": (Kb2MatmulSumMaxAvgpoolArg, 48),
+    "kb2_gemm_rmsnorm_swiglu": (Kb2GemmRmsnormSwigluArg, 56),
+    "kb2_gemm_silu_mul": (Kb2GemmSiluMulArg, 64),
 }
 
 _LIB = None

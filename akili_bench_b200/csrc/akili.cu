@@ -228,10 +228,17 @@ int cast_to_f16(const DevInfo& di, const float* src, __half* dst, size_t n, cuda
   return launch_status();
 }
 
+// x = hi + lo with hi = fp16(x), lo = fp16(x - hi) (the split operands).
+int split_to_f16x2(const DevInfo& di, const float* src, __half* hi, __half* lo, size_t n, cudaStream_t st) {
+  split_f32_to_f16x2_kernel<<<grid_for(di, n, 256, 8), 256, 0, st>>>(src, hi, lo, n);
+  return launch_status();
+}
+
 // ------------------------------------------------------------ GEMM jobs --
 struct GemmJob {
   Epi epi = Epi::kPlain;
   bool b_kmajor = false;
+  bool split = false;  // fp32 operands as fp16 hi + lo parts (the kb2_* family)
   uint32_t M = 0, N = 0, K = 0;
   const void* A = nullptr;   // [M x K] (in dtype)
   const void* B0 = nullptr;  // [K x N] or, when b_kmajor, [N x K]
@@ -255,7 +262,9 @@ struct GemmJob {
 
 // Row softmax of a short-K product runs fused end to end (softmax_rows_kernel):
 // no partial statistics, no finaliser.
-bool softmax_fused(const GemmJob& j) { return j.epi == Epi::kSoftmaxPre && j.K <= static_cast<uint32_t>(kSmMaxK); }
+bool softmax_fused(const GemmJob& j) {
+  return j.epi == Epi::kSoftmaxPre && !j.split && j.K <= static_cast<uint32_t>(kSmMaxK);
+}
 
 // Partial statistics: two slots (half tiles of BN/2 columns) per BN-column tile.
 size_t stats_bytes(const GemmJob& j) {
@@ -273,6 +282,10 @@ struct JobBuffers {
   __half* castA = nullptr;
   __half* castB0 = nullptr;
   __half* castB1 = nullptr;
+  // split mode: the lo parts
+  __half* Alo = nullptr;
+  __half* B0lo = nullptr;
+  __half* B1lo = nullptr;
   float* stats = nullptr;
 };
 
@@ -285,18 +298,22 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
     if (j.xhat_hint) jb->castA = static_cast<__half*>(j.xhat_hint);
     else jb->castA = static_cast<__half*>(grab(nA * 2));
     jb->A = jb->castA;
+    if (j.split) jb->Alo = static_cast<__half*>(grab(nA * 2));
   } else if (md.in_f32) {
     jb->castA = static_cast<__half*>(grab(nA * 2));
     jb->A = jb->castA;
+    if (j.split) jb->Alo = static_cast<__half*>(grab(nA * 2));
   } else {
     jb->A = static_cast<const __half*>(j.A);
   }
   if (md.in_f32) {
     jb->castB0 = static_cast<__half*>(grab(nB * 2));
     jb->B0 = jb->castB0;
+    if (j.split) jb->B0lo = static_cast<__half*>(grab(nB * 2));
     if (dual) {
       jb->castB1 = static_cast<__half*>(grab(nB * 2));
       jb->B1 = jb->castB1;
+      if (j.split) jb->B1lo = static_cast<__half*>(grab(nB * 2));
     }
   } else {
     jb->B0 = static_cast<const __half*>(j.B0);
@@ -362,15 +379,16 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
   return launch_status();
 }
 
-template <Epi E, typename OutT, bool BK>
+template <Epi E, typename OutT, bool BK, bool kSplit = false>
 int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaStream_t st) {
   constexpr bool kStore = epi_stores(E);
   constexpr int BN = epi_bn(E);
   CUtensorMap tmA, tmB0, tmB1, tmC;
   const uint64_t M = j.M, N = j.N, K = j.K;
   bool ok = map2d(&tmA, jb.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, K * 2, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
-  // CTA pairs (two SMs per 256-row tile) whenever M fills more than one 128-row block.
-  const bool pair = M > static_cast<uint64_t>(kBM);
+  // CTA pairs (two SMs per 256-row tile) whenever M fills more than one 128-row
+  // block; the split (fp32) mode runs on the single-CTA kernel only.
+  const bool pair = !kSplit && M > static_cast<uint64_t>(kBM);
   if (BK) {
     ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, N, K * 2, 64, pair ? BN / 2 : BN,
                      CU_TENSOR_MAP_SWIZZLE_128B);
@@ -409,7 +427,18 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.num_n_tiles = static_cast<int>(2 * ((N + BN - 1) / BN));  // statistics slots: two per tile
 
   if (pair) return launch_gemm_pair<E, OutT, BK>(di, tmA, tmB0, tmB1, tmC, ea, st);
-  const int smem = gemm_smem_bytes(kStore, sizeof(OutT));
+  // the lo parts of the split mode: the same boxes over the lo copies
+  CUtensorMap tmAlo = tmA, tmB0lo = tmB0, tmB1lo = tmB1;
+  if constexpr (kSplit) {
+    constexpr auto kF16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    constexpr auto kSw = CU_TENSOR_MAP_SWIZZLE_128B;
+    ok = map2d(&tmAlo, jb.Alo, kF16, K, M, K * 2, 64, kBM, kSw);
+    if (BK) ok = ok && map2d(&tmB0lo, jb.B0lo, kF16, K, N, K * 2, 64, BN, kSw);
+    else ok = ok && map2d(&tmB0lo, jb.B0lo, kF16, N, K, N * 2, 64, 64, kSw);
+    if (epi_dual(E)) ok = ok && map2d(&tmB1lo, jb.B1lo, kF16, N, K, N * 2, 64, 64, kSw);
+    if (!ok) return AKILI_E_LAUNCH;
+  }
+  const int smem = gemm_smem_bytes(kStore, sizeof(OutT), kSplit);
   static std::mutex mu;
   static std::map<int, bool> attr_done;
   {
@@ -417,7 +446,7 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> g(mu);
     if (!attr_done[dev]) {
-      if (cudaFuncSetAttribute(gemm_kernel<E, OutT, BK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      if (cudaFuncSetAttribute(gemm_kernel<E, OutT, BK, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
           cudaSuccess) {
         cudaGetLastError();
         return AKILI_E_LAUNCH;
@@ -427,7 +456,8 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   }
   const int tiles = static_cast<int>(((M + kBM - 1) / kBM) * ((N + BN - 1) / BN));
   const int grid = tiles < di.sms ? tiles : di.sms;
-  gemm_kernel<E, OutT, BK><<<grid, kGemmThreads, smem, st>>>(tmA, tmB0, tmB1, tmC, ea);
+  gemm_kernel<E, OutT, BK, kSplit><<<grid, kGemmThreads, smem, st>>>(tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo,
+                                                                     ea);
   return launch_status();
 }
 
@@ -478,6 +508,7 @@ int launch_softmax_rows(const DevInfo& di, const GemmJob& j, const JobBuffers& j
 
 template <Epi E, bool BK = false>
 int launch_gemm_out(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, bool out_f32, cudaStream_t st) {
+  if (j.split) return launch_gemm<E, float, BK, true>(di, j, jb, st);  // the kb2_* family: fp32 out
   if constexpr (!epi_stores(E)) {
     return launch_gemm<E, float, BK>(di, j, jb, st);
   } else {
@@ -510,17 +541,27 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
     const int grid = grid_for(di, j.M, rows_per_block, 8);
     if (md.in_f32)
       rmsnorm_prepass_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(j.A), j.rms_w, jb.castA,
-                                                          static_cast<int>(j.M), static_cast<int>(j.K), j.eps);
+                                                          jb.Alo, static_cast<int>(j.M), static_cast<int>(j.K),
+                                                          j.eps);
     else
       rmsnorm_prepass_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(j.A), j.rms_w, jb.castA,
-                                                           static_cast<int>(j.M), static_cast<int>(j.K), j.eps);
+                                                           nullptr, static_cast<int>(j.M), static_cast<int>(j.K),
+                                                           j.eps);
     if ((rc = launch_status())) return rc;
   } else if (md.in_f32) {
-    if ((rc = cast_to_f16(di, static_cast<const float*>(j.A), jb.castA, nA, st))) return rc;
+    if (j.split) rc = split_to_f16x2(di, static_cast<const float*>(j.A), jb.castA, jb.Alo, nA, st);
+    else rc = cast_to_f16(di, static_cast<const float*>(j.A), jb.castA, nA, st);
+    if (rc) return rc;
   }
   if (md.in_f32) {
-    if ((rc = cast_to_f16(di, static_cast<const float*>(j.B0), jb.castB0, nB, st))) return rc;
-    if (epi_dual(j.epi) && (rc = cast_to_f16(di, static_cast<const float*>(j.B1), jb.castB1, nB, st))) return rc;
+    if (j.split) rc = split_to_f16x2(di, static_cast<const float*>(j.B0), jb.castB0, jb.B0lo, nB, st);
+    else rc = cast_to_f16(di, static_cast<const float*>(j.B0), jb.castB0, nB, st);
+    if (rc) return rc;
+    if (epi_dual(j.epi)) {
+      if (j.split) rc = split_to_f16x2(di, static_cast<const float*>(j.B1), jb.castB1, jb.B1lo, nB, st);
+      else rc = cast_to_f16(di, static_cast<const float*>(j.B1), jb.castB1, nB, st);
+      if (rc) return rc;
+    }
   }
   // 2. the fused GEMM
   if (softmax_fused(j)) {
@@ -747,6 +788,129 @@ int job_silu_mul(const kbt_gemm_silu_mul_arg_t* a, GemmJob& j, bool chk = true) 
   return AKILI_OK;
 }
 
+// ----------------------------------------------------- kb2_* job builders --
+// The fp32 SIMT family (benchmarks/kb2_<bench>/kernel.cpp): the same fused
+// ops with fp32 operands kept to fp32 accuracy through the split mode.
+int job_kb2_add_relu(const kb2_gemm_add_relu_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kBiasRelu; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  return AKILI_OK;
+}
+
+int job_kb2_mul_leakyrelu(const kb2_gemm_mul_leakyrelu_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kBiasMulLeaky; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.s0 = a->multiplier; j.s1 = a->negative_slope;
+  return AKILI_OK;
+}
+
+int job_kb2_div_sum_scale(const kb2_gemm_div_sum_scale_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kRowSumHalf; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.C = W(a->c_addr);
+  j.final_scale = a->scaling_factor;
+  return AKILI_OK;
+}
+
+int job_kb2_layernorm(const kb2_gemm_layernorm_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->ln_w_addr, a->ln_b_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kLnPre; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.ln_w = F(a->ln_w_addr); j.ln_b = F(a->ln_b_addr); j.eps = a->eps;
+  return AKILI_OK;
+}
+
+int job_kb2_attention_score(const kb2_attention_score_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->D))) return rc;
+  if (chk && (rc = check_ptrs({a->q_addr, a->k_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kSoftmaxPre; j.split = true;
+  j.b_kmajor = true;
+  j.M = a->M; j.N = a->N; j.K = a->D;
+  j.A = P(a->q_addr); j.B0 = P(a->k_addr); j.C = W(a->c_addr);
+  j.s0 = 1.0f / sqrtf(static_cast<float>(a->D));  // kb2_attention_score/main.cpp verify loop
+  return AKILI_OK;
+}
+
+int job_kb2_matmul_softmax(const kb2_matmul_softmax_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->b_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kSoftmaxPre; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->b_addr); j.C = W(a->c_addr);
+  j.s0 = 1.0f;
+  return AKILI_OK;
+}
+
+int job_kb2_clamp(const kb2_matmul_scale_residadd_clamp_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kLseClamp; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.s0 = a->scale_factor; j.s1 = a->clamp_min; j.s2 = a->clamp_max;
+  return AKILI_OK;
+}
+
+int job_kb2_sum_max_avgpool(const kb2_matmul_sum_max_avgpool_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->w_addr, a->bias_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kRowSumBias; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->w_addr); j.vec0 = F(a->bias_addr); j.C = W(a->c_addr);
+  j.final_scale = 1.0f;
+  return AKILI_OK;
+}
+
+int job_kb2_rmsnorm_swiglu(const kb2_gemm_rmsnorm_swiglu_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->x_addr, a->rms_w_addr, a->wg_addr, a->wu_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kSwiglu; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->x_addr); j.B0 = P(a->wg_addr); j.B1 = P(a->wu_addr); j.C = W(a->c_addr);
+  j.rmsnorm = true; j.rms_w = F(a->rms_w_addr); j.eps = a->eps;
+  return AKILI_OK;
+}
+
+int job_kb2_silu_mul(const kb2_gemm_silu_mul_arg_t* a, GemmJob& j, bool chk = true) {
+  if (!a) return AKILI_E_NULL_ARG;
+  int rc;
+  if ((rc = check_m(a->M)) || (rc = check_dims(a->N, a->K))) return rc;
+  if (chk && (rc = check_ptrs({a->a_addr, a->wa_addr, a->ba_addr, a->wb_addr, a->bb_addr, a->c_addr}))) return rc;
+  j.epi = Epi::kSiluMulBias; j.split = true;
+  j.M = a->M; j.N = a->N; j.K = a->K;
+  j.A = P(a->a_addr); j.B0 = P(a->wa_addr); j.B1 = P(a->wb_addr); j.C = W(a->c_addr);
+  j.vec0 = F(a->ba_addr); j.vec1 = F(a->bb_addr);
+  return AKILI_OK;
+}
+
 // -------------------------------------------------------------- flash --
 struct FlashJob {
   uint32_t seq_len = 0, head_dim = 0;
@@ -917,6 +1081,20 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
   __syncthreads();
 }
 
+// kb2_* entries: fp32 in, fp32 out; an akili_ex_t may only add a workspace.
+template <class Arg, int (*Build)(const Arg*, GemmJob&, bool)>
+int entry_kb2(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  if (!md.in_f32 || !md.out_f32) return AKILI_E_DTYPE;
+  if (md.causal || md.batch != 1 || md.heads != 1) return AKILI_E_UNSUPPORTED;
+  if (!a) return AKILI_E_NULL_ARG;
+  GemmJob j;
+  if ((rc = Build(a, j, a->M != 0))) return rc;
+  return run_job(j, md, S(s));
+}
+
 }  // namespace
 
 // ===================================================================== ABI ==
@@ -941,6 +1119,24 @@ AKILI_GEMM_ENTRY(kbt_matmul_sum_max_avgpool, kbt_matmul_sum_max_avgpool_arg_t, j
 AKILI_GEMM_ENTRY(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t, job_rmsnorm_swiglu)
 AKILI_GEMM_ENTRY(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t, job_silu_mul)
 #undef AKILI_GEMM_ENTRY
+
+#define AKILI_KB2_ENTRY(name, build)                                                                \
+  int akili_##name(const name##_arg_t* a, akili_stream_t s) { return entry_kb2<name##_arg_t, build>(a, nullptr, s); } \
+  int akili_##name##_ex(const name##_arg_t* a, const akili_ex_t* ex, akili_stream_t s) {          \
+    if (!ex) return AKILI_E_NULL_ARG;                                                              \
+    return entry_kb2<name##_arg_t, build>(a, ex, s);                                               \
+  }
+AKILI_KB2_ENTRY(kb2_gemm_add_relu, job_kb2_add_relu)
+AKILI_KB2_ENTRY(kb2_gemm_mul_leakyrelu, job_kb2_mul_leakyrelu)
+AKILI_KB2_ENTRY(kb2_gemm_div_sum_scale, job_kb2_div_sum_scale)
+AKILI_KB2_ENTRY(kb2_gemm_layernorm, job_kb2_layernorm)
+AKILI_KB2_ENTRY(kb2_attention_score, job_kb2_attention_score)
+AKILI_KB2_ENTRY(kb2_matmul_softmax, job_kb2_matmul_softmax)
+AKILI_KB2_ENTRY(kb2_matmul_scale_residadd_clamp, job_kb2_clamp)
+AKILI_KB2_ENTRY(kb2_matmul_sum_max_avgpool, job_kb2_sum_max_avgpool)
+AKILI_KB2_ENTRY(kb2_gemm_rmsnorm_swiglu, job_kb2_rmsnorm_swiglu)
+AKILI_KB2_ENTRY(kb2_gemm_silu_mul, job_kb2_silu_mul)
+#undef AKILI_KB2_ENTRY
 
 // kbt_gemm_layernorm with its scratch in g_noalloc_scratch: no cudaMalloc,
 // cudaFree or other device allocation on any path (fp16 operands need no
@@ -1024,6 +1220,16 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
     return AKILI_OK;           \
   }
   AKILI_WS(kbt_sgemm, kbt_sgemm_arg_t, job_sgemm)
+  AKILI_WS(kb2_gemm_add_relu, kb2_gemm_add_relu_arg_t, job_kb2_add_relu)
+  AKILI_WS(kb2_gemm_mul_leakyrelu, kb2_gemm_mul_leakyrelu_arg_t, job_kb2_mul_leakyrelu)
+  AKILI_WS(kb2_gemm_div_sum_scale, kb2_gemm_div_sum_scale_arg_t, job_kb2_div_sum_scale)
+  AKILI_WS(kb2_gemm_layernorm, kb2_gemm_layernorm_arg_t, job_kb2_layernorm)
+  AKILI_WS(kb2_attention_score, kb2_attention_score_arg_t, job_kb2_attention_score)
+  AKILI_WS(kb2_matmul_softmax, kb2_matmul_softmax_arg_t, job_kb2_matmul_softmax)
+  AKILI_WS(kb2_matmul_scale_residadd_clamp, kb2_matmul_scale_residadd_clamp_arg_t, job_kb2_clamp)
+  AKILI_WS(kb2_matmul_sum_max_avgpool, kb2_matmul_sum_max_avgpool_arg_t, job_kb2_sum_max_avgpool)
+  AKILI_WS(kb2_gemm_rmsnorm_swiglu, kb2_gemm_rmsnorm_swiglu_arg_t, job_kb2_rmsnorm_swiglu)
+  AKILI_WS(kb2_gemm_silu_mul, kb2_gemm_silu_mul_arg_t, job_kb2_silu_mul)
   AKILI_WS(kbt_gemm_add_relu, kbt_gemm_add_relu_arg_t, job_add_relu)
   AKILI_WS(kbt_gemm_mul_leakyrelu, kbt_gemm_mul_leakyrelu_arg_t, job_mul_leakyrelu)
   AKILI_WS(kbt_gemm_div_sum_scale, kbt_gemm_div_sum_scale_arg_t, job_div_sum_scale)

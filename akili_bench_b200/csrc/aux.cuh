@@ -54,9 +54,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 // x_hat[i, k] = fp16( x[i,k] * (1 / sqrtf(sum_k x^2 / K + eps)) * w[k] )
 // (benchmarks/kbt_gemm_rmsnorm_swiglu/kernel.cpp:95-105, with the f2h of its
 // GEMM load, kernel.cpp:48, applied at the store).  One warp per row; K % 8 == 0.
+// With xlo non-null (the fp32 kb2 form, benchmarks/kb2_gemm_rmsnorm_swiglu/
+// main.cpp verify loop: x_hat stays fp32) x_hat is written as fp16 hi + lo
+// parts instead, hi = fp16(x_hat), lo = fp16(x_hat - hi).
 template <typename InT>
 __global__ void rmsnorm_prepass_kernel(const InT* __restrict__ x, const float* __restrict__ w,
-                                       __half* __restrict__ xhat, int M, int K, float eps) {
+                                       __half* __restrict__ xhat, __half* __restrict__ xlo, int M, int K,
+                                       float eps) {
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
@@ -105,12 +109,31 @@ __global__ void rmsnorm_prepass_kernel(const InT* __restrict__ x, const float* _
       const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + k));
       const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + k) + 1);
       const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = f[i] * inv_rms * ww[i];
       uint4 q;
-      q.x = pack_half2(f[0] * inv_rms * ww[0], f[1] * inv_rms * ww[1]);
-      q.y = pack_half2(f[2] * inv_rms * ww[2], f[3] * inv_rms * ww[3]);
-      q.z = pack_half2(f[4] * inv_rms * ww[4], f[5] * inv_rms * ww[5]);
-      q.w = pack_half2(f[6] * inv_rms * ww[6], f[7] * inv_rms * ww[7]);
+      q.x = pack_half2(h[0], h[1]);
+      q.y = pack_half2(h[2], h[3]);
+      q.z = pack_half2(h[4], h[5]);
+      q.w = pack_half2(h[6], h[7]);
       *reinterpret_cast<uint4*>(out + k) = q;
+      if (xlo != nullptr) {
+        const __half2* hh = reinterpret_cast<const __half2*>(&q);
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 t = __half22float2(hh[i]);
+          r[2 * i] = h[2 * i] - t.x;
+          r[2 * i + 1] = h[2 * i + 1] - t.y;
+        }
+        uint4 lq;
+        lq.x = pack_half2(r[0], r[1]);
+        lq.y = pack_half2(r[2], r[3]);
+        lq.z = pack_half2(r[4], r[5]);
+        lq.w = pack_half2(r[6], r[7]);
+        *reinterpret_cast<uint4*>(xlo + static_cast<size_t>(row) * K + k) = lq;
+      }
     }
   }
 }

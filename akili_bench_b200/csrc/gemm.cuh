@@ -70,8 +70,13 @@ struct EpiArgs {
   int num_n_tiles;
 };
 
-__host__ __device__ inline int gemm_smem_bytes(bool stores, int out_bytes) {
-  int s = kStages * kStageBytes;
+// Split mode (fp32 operands as fp16 hi + lo parts, the kb2_* family): a
+// stage holds [A_hi][B_hi][A_lo][B_lo], twice the bytes, so the ring is two deep.
+__host__ __device__ constexpr int gemm_stages(bool split) { return split ? 2 : kStages; }
+__host__ __device__ constexpr int gemm_stage_bytes(bool split) { return split ? 2 * kStageBytes : kStageBytes; }
+
+__host__ __device__ inline int gemm_smem_bytes(bool stores, int out_bytes, bool split = false) {
+  int s = gemm_stages(split) * gemm_stage_bytes(split);
   if (stores) s += 2 * kBM * 32 * out_bytes;
   s += 256;   // barriers + TMEM address
   s += 1024;  // alignment slack
@@ -172,7 +177,9 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
       if constexpr (E == Epi::kSoftmaxPre) {
         y = round_out<OutT>(v[j] * ea.s0);
       } else {
-        const float scaled = v[j] * ea.s0;
+        // kb2_matmul_scale_residadd_clamp adds a bias first (vec0); kbt has none
+        const float b = (ea.vec0 != nullptr && j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+        const float scaled = (v[j] + b) * ea.s0;
         float t = scaled + scaled;
         if (t < ea.s1) t = ea.s1;
         if (t > ea.s2) t = ea.s2;
@@ -298,11 +305,17 @@ __device__ __forceinline__ void write_stats(const EpiArgs& ea, int slot, int row
   }
 }
 
-template <Epi E, typename OutT, bool kBKMajor>
+// kSplit: A and B arrive as fp16 hi and lo parts (tmAlo, tmB0lo, tmB1lo;
+// unused otherwise) and every K-step issues A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
+// into the fp32 accumulator: fp32 operands at about 2^-21 relative error.
+template <Epi E, typename OutT, bool kBKMajor, bool kSplit = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                 const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmC,
-                const EpiArgs ea) {
+                const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmB0lo,
+                const __grid_constant__ CUtensorMap tmB1lo, const EpiArgs ea) {
+  constexpr int kSt = gemm_stages(kSplit);
+  constexpr int kSB = gemm_stage_bytes(kSplit);
   constexpr bool kDual = epi_dual(E);
   constexpr bool kStore = epi_stores(E);
   constexpr int kStats = epi_stats(E);
@@ -313,11 +326,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint8_t* staging = ring + kStages * kStageBytes;
+  uint8_t* staging = ring + kSt * kSB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(staging + (kStore ? 2 * kStageOut : 0));
   uint64_t* full = bars;
-  uint64_t* empty = bars + kStages;
-  uint64_t* acc_full = bars + 2 * kStages;
+  uint64_t* empty = bars + kSt;
+  uint64_t* acc_full = bars + 2 * kSt;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
@@ -332,7 +345,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t lane = lane_id();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kSt; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -370,27 +383,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {
           ok = mbar_wait(&empty[stage], phase ^ 1, kSiteProducerEmpty);
           if (ok) {
-            uint8_t* sa = ring + stage * kStageBytes;
-            uint8_t* sb = sa + kATileBytes;
-            mbar_expect_tx(&full[stage], kStageBytes);
-            tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
-            if constexpr (kBKMajor) {
-              tma_load_2d(sb, &tmB0, &full[stage], kb * kBK, n_blk * BN);
-            } else if constexpr (kDual) {
-              tma_load_2d(sb, &tmB0, &full[stage], n_blk * BN, kb * kBK);
-              tma_load_2d(sb + 8192, &tmB0, &full[stage], n_blk * BN + 64, kb * kBK);
-              tma_load_2d(sb + 16384, &tmB1, &full[stage], n_blk * BN, kb * kBK);
-              tma_load_2d(sb + 24576, &tmB1, &full[stage], n_blk * BN + 64, kb * kBK);
-            } else {
+            uint8_t* sa = ring + stage * kSB;
+            mbar_expect_tx(&full[stage], kSB);
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                tma_load_2d(sb + q * 8192, &tmB0, &full[stage], n_blk * BN + q * 64, kb * kBK);
+            for (int part = 0; part < (kSplit ? 2 : 1); ++part) {
+              // part 0: hi parts (or the fp16 operands), part 1: lo parts
+              uint8_t* pa = sa + part * kStageBytes;
+              uint8_t* sb = pa + kATileBytes;
+              const CUtensorMap* mA = part ? &tmAlo : &tmA;
+              const CUtensorMap* mB0 = part ? &tmB0lo : &tmB0;
+              const CUtensorMap* mB1 = part ? &tmB1lo : &tmB1;
+              tma_load_2d(pa, mA, &full[stage], kb * kBK, m_blk * kBM);
+              if constexpr (kBKMajor) {
+                tma_load_2d(sb, mB0, &full[stage], kb * kBK, n_blk * BN);
+              } else if constexpr (kDual) {
+                tma_load_2d(sb, mB0, &full[stage], n_blk * BN, kb * kBK);
+                tma_load_2d(sb + 8192, mB0, &full[stage], n_blk * BN + 64, kb * kBK);
+                tma_load_2d(sb + 16384, mB1, &full[stage], n_blk * BN, kb * kBK);
+                tma_load_2d(sb + 24576, mB1, &full[stage], n_blk * BN + 64, kb * kBK);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  tma_load_2d(sb + q * 8192, mB0, &full[stage], n_blk * BN + q * 64, kb * kBK);
+              }
             }
           }
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
-        if (++stage == kStages) {
+        if (++stage == kSt) {
           stage = 0;
           phase ^= 1;
         }
@@ -418,26 +439,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!ok) break;
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t sa = smem_u32(ring + stage * kStageBytes);
+          const uint32_t sa = smem_u32(ring + stage * kSB);
           const uint32_t sb = sa + kATileBytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
             const uint32_t accum = (kb | k) != 0;
-            if constexpr (kBKMajor) {
-              umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
-            } else if constexpr (kDual) {
-              umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
-              umma_f16_ss(d_tmem + 128, ad, make_sdesc(sb + 16384 + k * 2048, 8192, 1024, kSw128), idesc,
-                          accum);
-            } else {
-              umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+            // B descriptors of the hi part at byte offset `o` from sb (the lo
+            // part sits kStageBytes further on, as does A's)
+            auto bdesc = [&](uint32_t o) -> uint64_t {
+              return kBKMajor ? make_sdesc(sb + o + k * 32, 16, 1024, kSw128)
+                              : make_sdesc(sb + o + k * 2048, 8192, 1024, kSw128);
+            };
+            constexpr int kOps = kDual ? 2 : 1;
+#pragma unroll
+            for (int op = 0; op < kOps; ++op) {
+              const uint32_t d = d_tmem + op * 128;
+              const uint64_t bd = bdesc(op * 16384);
+              umma_f16_ss(d, ad, bd, idesc, accum);
+              if constexpr (kSplit) {
+                umma_f16_ss(d, ad, bdesc(kStageBytes + op * 16384), idesc, 1);
+                umma_f16_ss(d, make_sdesc(sa + kStageBytes + k * 32, 16, 1024, kSw128), bd, idesc, 1);
+              }
             }
           }
           umma_commit(&empty[stage]);
         }
         __syncwarp();
-        if (++stage == kStages) {
+        if (++stage == kSt) {
           stage = 0;
           phase ^= 1;
         }

@@ -80,6 +80,16 @@ int dispatch(const std::string& op, const void* a) {
   AKILI_DISPATCH(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t)
   AKILI_DISPATCH(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t)
   AKILI_DISPATCH(flash, flash_arg_t)
+  AKILI_DISPATCH(kb2_gemm_add_relu, kb2_gemm_add_relu_arg_t)
+  AKILI_DISPATCH(kb2_gemm_mul_leakyrelu, kb2_gemm_mul_leakyrelu_arg_t)
+  AKILI_DISPATCH(kb2_gemm_div_sum_scale, kb2_gemm_div_sum_scale_arg_t)
+  AKILI_DISPATCH(kb2_gemm_layernorm, kb2_gemm_layernorm_arg_t)
+  AKILI_DISPATCH(kb2_attention_score, kb2_attention_score_arg_t)
+  AKILI_DISPATCH(kb2_matmul_softmax, kb2_matmul_softmax_arg_t)
+  AKILI_DISPATCH(kb2_matmul_scale_residadd_clamp, kb2_matmul_scale_residadd_clamp_arg_t)
+  AKILI_DISPATCH(kb2_matmul_sum_max_avgpool, kb2_matmul_sum_max_avgpool_arg_t)
+  AKILI_DISPATCH(kb2_gemm_rmsnorm_swiglu, kb2_gemm_rmsnorm_swiglu_arg_t)
+  AKILI_DISPATCH(kb2_gemm_silu_mul, kb2_gemm_silu_mul_arg_t)
 #undef AKILI_DISPATCH
   std::fprintf(stderr, "akili vortex shim: no akili op named '%s'\n", op.c_str());
   return AKILI_E_UNSUPPORTED;

@@ -177,6 +177,59 @@ typedef struct {
   uint64_t Q_addr, K_addr, V_addr, O_addr;
 } flash_arg_t;
 
+/* ---- the kb2_* SIMT family: fp32 operands, fp32 arithmetic --------------
+ * benchmarks/kb2_<bench>/common.h: the same ops without the Vortex launch
+ * fields.  Their plain entries keep fp32 semantics (no fp16 rounding of the
+ * operands): the GEMM runs on the tensor cores with each operand split into
+ * two fp16 parts, x = hi + lo, and S = A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
+ * accumulated in fp32 (relative error about 2^-21 per product; operands
+ * must lie within fp16's range, |x| < 65504). */
+typedef struct {                 /* kb2_gemm_add_relu/common.h:4-12 */
+  uint32_t M, N, K;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kb2_gemm_add_relu_arg_t;
+typedef struct {                 /* kb2_gemm_mul_leakyrelu/common.h */
+  uint32_t M, N, K;
+  float multiplier, negative_slope;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kb2_gemm_mul_leakyrelu_arg_t;
+typedef struct {                 /* kb2_gemm_div_sum_scale/common.h */
+  uint32_t M, N, K;
+  float scaling_factor;
+  uint64_t a_addr, w_addr, c_addr;
+} kb2_gemm_div_sum_scale_arg_t;
+typedef struct {                 /* kb2_gemm_layernorm/common.h */
+  uint32_t M, N, K;
+  float eps;
+  uint64_t a_addr, w_addr, bias_addr, ln_w_addr, ln_b_addr, c_addr;
+} kb2_gemm_layernorm_arg_t;
+typedef struct {                 /* kb2_attention_score/common.h */
+  uint32_t M, N, D;
+  uint64_t q_addr, k_addr, c_addr;
+} kb2_attention_score_arg_t;
+typedef struct {                 /* kb2_matmul_softmax/common.h */
+  uint32_t M, N, K;
+  uint64_t a_addr, b_addr, c_addr;
+} kb2_matmul_softmax_arg_t;
+typedef struct {                 /* kb2_matmul_scale_residadd_clamp/common.h (adds a bias) */
+  uint32_t M, N, K;
+  float scale_factor, clamp_min, clamp_max;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kb2_matmul_scale_residadd_clamp_arg_t;
+typedef struct {                 /* kb2_matmul_sum_max_avgpool/common.h */
+  uint32_t M, N, K;
+  uint64_t a_addr, w_addr, bias_addr, c_addr;
+} kb2_matmul_sum_max_avgpool_arg_t;
+typedef struct {                 /* kb2_gemm_rmsnorm_swiglu/common.h (no scratch fields) */
+  uint32_t M, N, K;
+  float eps;
+  uint64_t x_addr, rms_w_addr, wg_addr, wu_addr, c_addr;
+} kb2_gemm_rmsnorm_swiglu_arg_t;
+typedef struct {                 /* kb2_gemm_silu_mul/common.h */
+  uint32_t M, N, K;
+  uint64_t a_addr, wa_addr, ba_addr, wb_addr, bb_addr, c_addr;
+} kb2_gemm_silu_mul_arg_t;
+
 /* ---- extension block for the fp16 / batched forms ------------------------ */
 typedef struct {
   uint32_t abi_version;     /* must be AKILI_ABI_VERSION                                  */
@@ -279,6 +332,41 @@ int akili_flash_ex(const flash_arg_t* arg, const akili_ex_t* ex, akili_stream_t 
 int akili_flash_ml_ex(const flash_arg_t* arg, const akili_ex_t* ex, uint64_t m_addr, uint64_t l_addr,
                       akili_stream_t stream);
 
+/* kb2_* entries: each replaces the vx_upload_bytes + vx_start +
+ * vx_ready_wait sequence of benchmarks/kb2_<bench>/main.cpp.  fp32 buffers,
+ * fp32 results (see the kb2 structs above); the `_ex` form takes an
+ * akili_ex_t only for its workspace (dtype fields must be F32, causal 0). */
+/* benchmarks/kb2_gemm_add_relu/main.cpp:104-108 */
+int akili_kb2_gemm_add_relu(const kb2_gemm_add_relu_arg_t* arg, akili_stream_t stream);
+int akili_kb2_gemm_add_relu_ex(const kb2_gemm_add_relu_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_gemm_mul_leakyrelu/main.cpp:110-114 */
+int akili_kb2_gemm_mul_leakyrelu(const kb2_gemm_mul_leakyrelu_arg_t* arg, akili_stream_t stream);
+int akili_kb2_gemm_mul_leakyrelu_ex(const kb2_gemm_mul_leakyrelu_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_gemm_div_sum_scale/main.cpp:100-104 */
+int akili_kb2_gemm_div_sum_scale(const kb2_gemm_div_sum_scale_arg_t* arg, akili_stream_t stream);
+int akili_kb2_gemm_div_sum_scale_ex(const kb2_gemm_div_sum_scale_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_gemm_layernorm/main.cpp:121-125 */
+int akili_kb2_gemm_layernorm(const kb2_gemm_layernorm_arg_t* arg, akili_stream_t stream);
+int akili_kb2_gemm_layernorm_ex(const kb2_gemm_layernorm_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_attention_score/main.cpp:96-100 */
+int akili_kb2_attention_score(const kb2_attention_score_arg_t* arg, akili_stream_t stream);
+int akili_kb2_attention_score_ex(const kb2_attention_score_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_matmul_softmax/main.cpp:96-100 */
+int akili_kb2_matmul_softmax(const kb2_matmul_softmax_arg_t* arg, akili_stream_t stream);
+int akili_kb2_matmul_softmax_ex(const kb2_matmul_softmax_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_matmul_scale_residadd_clamp/main.cpp:112-116 */
+int akili_kb2_matmul_scale_residadd_clamp(const kb2_matmul_scale_residadd_clamp_arg_t* arg, akili_stream_t stream);
+int akili_kb2_matmul_scale_residadd_clamp_ex(const kb2_matmul_scale_residadd_clamp_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_matmul_sum_max_avgpool/main.cpp:104-108 */
+int akili_kb2_matmul_sum_max_avgpool(const kb2_matmul_sum_max_avgpool_arg_t* arg, akili_stream_t stream);
+int akili_kb2_matmul_sum_max_avgpool_ex(const kb2_matmul_sum_max_avgpool_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_gemm_rmsnorm_swiglu/main.cpp:115-119 */
+int akili_kb2_gemm_rmsnorm_swiglu(const kb2_gemm_rmsnorm_swiglu_arg_t* arg, akili_stream_t stream);
+int akili_kb2_gemm_rmsnorm_swiglu_ex(const kb2_gemm_rmsnorm_swiglu_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+/* benchmarks/kb2_gemm_silu_mul/main.cpp:118-122 */
+int akili_kb2_gemm_silu_mul(const kb2_gemm_silu_mul_arg_t* arg, akili_stream_t stream);
+int akili_kb2_gemm_silu_mul_ex(const kb2_gemm_silu_mul_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
+
 /* ---- runtime helpers (no counterpart in the reference beyond RT_CHECK) --- */
 
 /* Human-readable text for an AKILI_E_* code (static storage). */
@@ -329,6 +417,22 @@ AKILI_CHECK_LAYOUT(kbt_gemm_rmsnorm_swiglu_arg_t, 96);
 AKILI_CHECK_LAYOUT(kbt_gemm_silu_mul_arg_t, 96);
 AKILI_CHECK_LAYOUT(flash_arg_t, 64);
 AKILI_CHECK_LAYOUT(akili_ex_t, 48);
+AKILI_CHECK_LAYOUT(kb2_gemm_add_relu_arg_t, 48);
+AKILI_CHECK_LAYOUT(kb2_gemm_mul_leakyrelu_arg_t, 56);
+AKILI_CHECK_LAYOUT(kb2_gemm_div_sum_scale_arg_t, 40);
+AKILI_CHECK_LAYOUT(kb2_gemm_layernorm_arg_t, 64);
+AKILI_CHECK_LAYOUT(kb2_attention_score_arg_t, 40);
+AKILI_CHECK_LAYOUT(kb2_matmul_softmax_arg_t, 40);
+AKILI_CHECK_LAYOUT(kb2_matmul_scale_residadd_clamp_arg_t, 56);
+AKILI_CHECK_LAYOUT(kb2_matmul_sum_max_avgpool_arg_t, 48);
+AKILI_CHECK_LAYOUT(kb2_gemm_rmsnorm_swiglu_arg_t, 56);
+AKILI_CHECK_LAYOUT(kb2_gemm_silu_mul_arg_t, 64);
+static_assert(offsetof(kb2_gemm_add_relu_arg_t, a_addr) == 16 && offsetof(kb2_gemm_add_relu_arg_t, c_addr) == 40,
+              "kb2_gemm_add_relu offsets");
+static_assert(offsetof(kb2_matmul_scale_residadd_clamp_arg_t, clamp_max) == 20 &&
+              offsetof(kb2_matmul_scale_residadd_clamp_arg_t, a_addr) == 24, "kb2 clamp offsets");
+static_assert(offsetof(kb2_gemm_layernorm_arg_t, eps) == 12 && offsetof(kb2_gemm_layernorm_arg_t, c_addr) == 56,
+              "kb2_gemm_layernorm offsets");
 static_assert(offsetof(kbt_sgemm_arg_t, M) == 24 && offsetof(kbt_sgemm_arg_t, a_addr) == 40 &&
               offsetof(kbt_sgemm_arg_t, c_addr) == 56, "kbt_sgemm offsets");
 static_assert(offsetof(kbt_gemm_mul_leakyrelu_arg_t, multiplier) == 36 &&

@@ -44,6 +44,16 @@ BENCHES = [
     "kbt_gemm_rmsnorm_swiglu",
     "kbt_gemm_silu_mul",
     "flash",
+    "kb2_gemm_add_relu",
+    "kb2_gemm_mul_leakyrelu",
+    "kb2_gemm_div_sum_scale",
+    "kb2_gemm_layernorm",
+    "kb2_attention_score",
+    "kb2_matmul_softmax",
+    "kb2_matmul_scale_residadd_clamp",
+    "kb2_matmul_sum_max_avgpool",
+    "kb2_gemm_rmsnorm_swiglu",
+    "kb2_gemm_silu_mul",
 ]
 
 # The reference's host compile flags (common/common.mk:63,69-71).

@@ -312,6 +312,212 @@ void oracle_flash_causal(float* out, float* m_out, float* l_out, const float* q,
   free(scores);
 }
 
+/* ---- the kb2_* family: fp32 gold loops of benchmarks/kb2_<bench>/main.cpp,
+ * restated in their loop order (the bias starts the dot product). ---- */
+
+/* kb2_gemm_add_relu/main.cpp:113-121 (verify loop) */
+void oracle_kb2_gemm_add_relu(const float* a, const float* w, const float* bias, float* c, uint32_t M,
+                              uint32_t N, uint32_t K, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum = bias[j];
+      for (uint32_t k = 0; k < K; ++k) sum += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      c[(uint64_t)i * N + j] = (sum > 0.0f) ? sum : 0.0f;
+    }
+}
+
+/* kb2_gemm_mul_leakyrelu/main.cpp (verify loop) */
+void oracle_kb2_gemm_mul_leakyrelu(const float* a, const float* w, const float* bias, float* c, uint32_t M,
+                                   uint32_t N, uint32_t K, float multiplier, float negative_slope, uint32_t row0,
+                                   uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float sum = bias[j];
+      for (uint32_t k = 0; k < K; ++k) sum += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      sum *= multiplier;
+      c[(uint64_t)i * N + j] = (sum >= 0.0f) ? sum : sum * negative_slope;
+    }
+}
+
+/* kb2_gemm_div_sum_scale/main.cpp (verify loop): out[i] = scaling * sum_j (dot * 0.5) */
+void oracle_kb2_gemm_div_sum_scale(const float* a, const float* w, float* c, uint32_t M, uint32_t N, uint32_t K,
+                                   float scaling_factor, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float total = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = 0.0f;
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      total += dot * 0.5f;
+    }
+    c[i] = total * scaling_factor;
+  }
+}
+
+/* kb2_gemm_layernorm/main.cpp (verify loop): bias-first dot, then the
+ * two-pass biased LayerNorm of the row */
+void oracle_kb2_gemm_layernorm(const float* a, const float* w, const float* bias, const float* ln_w,
+                               const float* ln_b, float* c, uint32_t M, uint32_t N, uint32_t K, float eps,
+                               uint32_t row0, uint32_t row1) {
+  (void)M;
+  float* vals = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = bias[j];
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      vals[j] = dot;
+    }
+    float sum = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) sum += vals[j];
+    float mean = sum / (float)N;
+    float var = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      float diff = vals[j] - mean;
+      var += diff * diff;
+    }
+    var /= (float)N;
+    float inv_std = 1.0f / sqrtf(var + eps);
+    for (uint32_t j = 0; j < N; ++j) {
+      float normalized = (vals[j] - mean) * inv_std;
+      c[(uint64_t)i * N + j] = normalized * ln_w[j] + ln_b[j];
+    }
+  }
+  free(vals);
+}
+
+/* softmax of one row as the kb2 verify loops compute it: max from element 0,
+ * sum of expf(x - max), then expf(x - max) / sum recomputed per element */
+static void kb2_softmax_row(const float* x, float* out, uint32_t N) {
+  float max_val = x[0];
+  for (uint32_t j = 1; j < N; ++j)
+    if (x[j] > max_val) max_val = x[j];
+  float sum_exp = 0.0f;
+  for (uint32_t j = 0; j < N; ++j) sum_exp += expf(x[j] - max_val);
+  for (uint32_t j = 0; j < N; ++j) out[j] = expf(x[j] - max_val) / sum_exp;
+}
+
+/* kb2_attention_score/main.cpp (verify loop): softmax_j(Q_i . K_j * (1/sqrt(D))) */
+void oracle_kb2_attention_score(const float* q, const float* k, float* c, uint32_t M, uint32_t N, uint32_t D,
+                                uint32_t row0, uint32_t row1) {
+  (void)M;
+  float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  float* scores = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = 0.0f;
+      for (uint32_t d = 0; d < D; ++d) dot += q[(uint64_t)i * D + d] * k[(uint64_t)j * D + d];
+      scores[j] = dot * inv_sqrt_d;
+    }
+    kb2_softmax_row(scores, c + (uint64_t)i * N, N);
+  }
+  free(scores);
+}
+
+/* kb2_matmul_softmax/main.cpp (verify loop): softmax_j(A_i . B_:j), no scale */
+void oracle_kb2_matmul_softmax(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                               uint32_t row0, uint32_t row1) {
+  (void)M;
+  float* vals = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = 0.0f;
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * b[(uint64_t)k * N + j];
+      vals[j] = dot;
+    }
+    kb2_softmax_row(vals, c + (uint64_t)i * N, N);
+  }
+  free(vals);
+}
+
+/* kb2_matmul_scale_residadd_clamp/main.cpp (verify loop): t = clamp(2 *
+ * (bias + dot) * scale); lse = max + logf(sum expf(t - max)); out = lse *
+ * (lse * tanhf(logf(1 + expf(lse)))) */
+void oracle_kb2_matmul_scale_residadd_clamp(const float* a, const float* w, const float* bias, float* c,
+                                            uint32_t M, uint32_t N, uint32_t K, float scale_factor,
+                                            float clamp_min, float clamp_max, uint32_t row0, uint32_t row1) {
+  (void)M;
+  float* vals = (float*)malloc(sizeof(float) * (N ? N : 1));
+  for (uint32_t i = row0; i < row1; ++i) {
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = bias[j];
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      dot *= scale_factor;
+      dot += dot;
+      if (dot < clamp_min) dot = clamp_min;
+      if (dot > clamp_max) dot = clamp_max;
+      vals[j] = dot;
+    }
+    float max_val = vals[0];
+    for (uint32_t j = 1; j < N; ++j)
+      if (vals[j] > max_val) max_val = vals[j];
+    float sum_exp = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) sum_exp += expf(vals[j] - max_val);
+    float lse = max_val + logf(sum_exp);
+    float mish_lse = lse * tanhf(logf(1.0f + expf(lse)));
+    c[i] = lse * mish_lse;
+  }
+  free(vals);
+}
+
+/* kb2_matmul_sum_max_avgpool/main.cpp (verify loop): out[i] = sum_j (bias + dot) */
+void oracle_kb2_matmul_sum_max_avgpool(const float* a, const float* w, const float* bias, float* c, uint32_t M,
+                                       uint32_t N, uint32_t K, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float total = 0.0f;
+    for (uint32_t j = 0; j < N; ++j) {
+      float dot = bias[j];
+      for (uint32_t k = 0; k < K; ++k) dot += a[(uint64_t)i * K + k] * w[(uint64_t)k * N + j];
+      total += dot;
+    }
+    c[i] = total;
+  }
+}
+
+/* kb2_gemm_rmsnorm_swiglu/main.cpp (verify loop): r = 1/sqrtf(sum x^2 / K +
+ * eps); h_k = x_k * r * w_k in fp32; gate, up = h . Wg, h . Wu; out =
+ * gate / (1 + expf(-gate)) * up */
+void oracle_kb2_gemm_rmsnorm_swiglu(const float* x, const float* rms_w, const float* wg, const float* wu, float* c,
+                                    uint32_t M, uint32_t N, uint32_t K, float eps, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i) {
+    float ss = 0.0f;
+    for (uint32_t k = 0; k < K; ++k) {
+      float v = x[(uint64_t)i * K + k];
+      ss += v * v;
+    }
+    float inv_rms = 1.0f / sqrtf(ss / (float)K + eps);
+    for (uint32_t j = 0; j < N; ++j) {
+      float gate = 0.0f, up = 0.0f;
+      for (uint32_t k = 0; k < K; ++k) {
+        float h = x[(uint64_t)i * K + k] * inv_rms * rms_w[k];
+        gate += h * wg[(uint64_t)k * N + j];
+        up += h * wu[(uint64_t)k * N + j];
+      }
+      float silu_gate = gate / (1.0f + expf(-gate));
+      c[(uint64_t)i * N + j] = silu_gate * up;
+    }
+  }
+}
+
+/* kb2_gemm_silu_mul/main.cpp (verify loop): gate = ba + a.Wa, up = bb + a.Wb
+ * (bias first); out = gate / (1 + expf(-gate)) * up */
+void oracle_kb2_gemm_silu_mul(const float* a, const float* wa, const float* ba, const float* wb, const float* bb,
+                              float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t i = row0; i < row1; ++i)
+    for (uint32_t j = 0; j < N; ++j) {
+      float gate = ba[j];
+      for (uint32_t k = 0; k < K; ++k) gate += a[(uint64_t)i * K + k] * wa[(uint64_t)k * N + j];
+      float up = bb[j];
+      for (uint32_t k = 0; k < K; ++k) up += a[(uint64_t)i * K + k] * wb[(uint64_t)k * N + j];
+      float silu_gate = gate / (1.0f + expf(-gate));
+      c[(uint64_t)i * N + j] = silu_gate * up;
+    }
+}
+
 /* IEEE binary16 round-to-nearest-even, as the reference's f2h (`(__fp16)x`,
  * benchmarks/kbt_sgemm/kernel.cpp:13-18) and CUDA's __float2half_rn do.
  * Written from the format definition: 1 sign, 5 exponent (bias 15),

@@ -64,6 +64,29 @@ void oracle_flash(float* out, const float* q, const float* k, const float* v, ui
                   uint32_t d, float scale, uint32_t row0, uint32_t row1);
 void oracle_flash_causal(float* out, float* m_out, float* l_out, const float* q, const float* k, const float* v,
                          uint32_t seq_len, uint32_t d, float scale, uint32_t causal, uint32_t row0, uint32_t row1);
+void oracle_kb2_gemm_add_relu(const float* a, const float* w, const float* bias, float* c, uint32_t M,
+                              uint32_t N, uint32_t K, uint32_t row0, uint32_t row1);
+void oracle_kb2_gemm_mul_leakyrelu(const float* a, const float* w, const float* bias, float* c, uint32_t M,
+                                   uint32_t N, uint32_t K, float multiplier, float negative_slope, uint32_t row0,
+                                   uint32_t row1);
+void oracle_kb2_gemm_div_sum_scale(const float* a, const float* w, float* c, uint32_t M, uint32_t N, uint32_t K,
+                                   float scaling_factor, uint32_t row0, uint32_t row1);
+void oracle_kb2_gemm_layernorm(const float* a, const float* w, const float* bias, const float* ln_w,
+                               const float* ln_b, float* c, uint32_t M, uint32_t N, uint32_t K, float eps,
+                               uint32_t row0, uint32_t row1);
+void oracle_kb2_attention_score(const float* q, const float* k, float* c, uint32_t M, uint32_t N, uint32_t D,
+                                uint32_t row0, uint32_t row1);
+void oracle_kb2_matmul_softmax(const float* a, const float* b, float* c, uint32_t M, uint32_t N, uint32_t K,
+                               uint32_t row0, uint32_t row1);
+void oracle_kb2_matmul_scale_residadd_clamp(const float* a, const float* w, const float* bias, float* c,
+                                            uint32_t M, uint32_t N, uint32_t K, float scale_factor,
+                                            float clamp_min, float clamp_max, uint32_t row0, uint32_t row1);
+void oracle_kb2_matmul_sum_max_avgpool(const float* a, const float* w, const float* bias, float* c, uint32_t M,
+                                       uint32_t N, uint32_t K, uint32_t row0, uint32_t row1);
+void oracle_kb2_gemm_rmsnorm_swiglu(const float* x, const float* rms_w, const float* wg, const float* wu, float* c,
+                                    uint32_t M, uint32_t N, uint32_t K, float eps, uint32_t row0, uint32_t row1);
+void oracle_kb2_gemm_silu_mul(const float* a, const float* wa, const float* ba, const float* wb, const float* bb,
+                              float* c, uint32_t M, uint32_t N, uint32_t K, uint32_t row0, uint32_t row1);
 
 /* Helpers used by tests to reproduce the device's operand rounding. */
 float oracle_round_f16(float x);                 /* fp32 -> nearest-even fp16 -> fp32 */

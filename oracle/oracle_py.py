@@ -35,6 +35,17 @@ _SIGS = {
     "oracle_kbt_gemm_silu_mul": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_flash": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _f, _u32, _u32],
     "oracle_flash_causal": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _f, _u32, _u32, _u32],
+    "oracle_kb2_gemm_add_relu": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
+    "oracle_kb2_gemm_mul_leakyrelu": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _f, _u32, _u32],
+    "oracle_kb2_gemm_div_sum_scale": [_f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _u32, _u32],
+    "oracle_kb2_gemm_layernorm": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _u32, _u32],
+    "oracle_kb2_attention_score": [_f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
+    "oracle_kb2_matmul_softmax": [_f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
+    "oracle_kb2_matmul_scale_residadd_clamp": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _f, _f, _u32,
+                                               _u32],
+    "oracle_kb2_matmul_sum_max_avgpool": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
+    "oracle_kb2_gemm_rmsnorm_swiglu": [_f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _u32, _u32],
+    "oracle_kb2_gemm_silu_mul": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_round_f16_array": [_f32p, C.c_uint64],
 }
 
@@ -197,3 +208,84 @@ def flash_causal(q, k, v, seq_len, d, scale=1.0, causal=True, row0=0, row1=None,
     _rows(lib().oracle_flash_causal, (_p(o), _p(m), _p(l), _p(q), _p(k), _p(v)),
           (seq_len, d, scale, 1 if causal else 0), row0, row1, threads)
     return o, m, l
+
+
+# ---- the kb2_* family (fp32 gold loops, bias-first dot products) ----
+
+def kb2_gemm_add_relu(a, w, bias, M, N, K, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_gemm_add_relu, (_p(a), _p(w), _p(bias), _p(c)), (M, N, K), row0, row1, threads)
+    return c
+
+
+def kb2_gemm_mul_leakyrelu(a, w, bias, M, N, K, multiplier=1.5, negative_slope=0.01, row0=0, row1=None,
+                           threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_gemm_mul_leakyrelu, (_p(a), _p(w), _p(bias), _p(c)),
+          (M, N, K, multiplier, negative_slope), row0, row1, threads)
+    return c
+
+
+def kb2_gemm_div_sum_scale(a, w, M, N, K, scaling_factor=2.0, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros(M, np.float32)
+    _rows(lib().oracle_kb2_gemm_div_sum_scale, (_p(a), _p(w), _p(c)), (M, N, K, scaling_factor), row0, row1,
+          threads)
+    return c
+
+
+def kb2_gemm_layernorm(a, w, bias, ln_w, ln_b, M, N, K, eps=1e-5, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_gemm_layernorm, (_p(a), _p(w), _p(bias), _p(ln_w), _p(ln_b), _p(c)), (M, N, K, eps),
+          row0, row1, threads)
+    return c
+
+
+def kb2_attention_score(q, k, M, N, D, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_attention_score, (_p(q), _p(k), _p(c)), (M, N, D), row0, row1, threads)
+    return c
+
+
+def kb2_matmul_softmax(a, b, M, N, K, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_matmul_softmax, (_p(a), _p(b), _p(c)), (M, N, K), row0, row1, threads)
+    return c
+
+
+def kb2_matmul_scale_residadd_clamp(a, w, bias, M, N, K, scale_factor=2.0, clamp_min=-10.0, clamp_max=10.0,
+                                    row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros(M, np.float32)
+    _rows(lib().oracle_kb2_matmul_scale_residadd_clamp, (_p(a), _p(w), _p(bias), _p(c)),
+          (M, N, K, scale_factor, clamp_min, clamp_max), row0, row1, threads)
+    return c
+
+
+def kb2_matmul_sum_max_avgpool(a, w, bias, M, N, K, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros(M, np.float32)
+    _rows(lib().oracle_kb2_matmul_sum_max_avgpool, (_p(a), _p(w), _p(bias), _p(c)), (M, N, K), row0, row1,
+          threads)
+    return c
+
+
+def kb2_gemm_rmsnorm_swiglu(x, rms_w, wg, wu, M, N, K, eps=1e-5, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_gemm_rmsnorm_swiglu, (_p(x), _p(rms_w), _p(wg), _p(wu), _p(c)), (M, N, K, eps), row0,
+          row1, threads)
+    return c
+
+
+def kb2_gemm_silu_mul(a, wa, ba, wb, bb, M, N, K, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_kb2_gemm_silu_mul, (_p(a), _p(wa), _p(ba), _p(wb), _p(bb), _p(c)), (M, N, K), row0, row1,
+          threads)
+    return c

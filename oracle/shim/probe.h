@@ -5,7 +5,8 @@
  *
  * In the reference harnesses `fabsf` / `std::fabs` appear only in the verify
  * loops (diff = fabsf(actual - expected), rel = diff / fabsf(expected), and
- * flash's Comparator::compare).  Redirecting them gives two modes, chosen by
+ * flash's Comparator::compare), and integer `std::abs` only in the kb2 ulp
+ * checks (std::abs(actual_bits - expected_bits)); both are redirected.  Redirecting them gives two modes, chosen by
  * the AKILI_PROBE environment variable:
  *
  *   exact   |x| is reported as 0 when x == 0 and as 1e30 otherwise, so every
@@ -34,11 +35,17 @@
 #include <vector>
 
 float akili_probe_fabsf(float x);
+int akili_probe_iabs(int x);
 
 #define fabsf akili_probe_fabsf
 namespace std {
 inline float akili_probe_fabs(float x) { return ::akili_probe_fabsf(x); }
 }  // namespace std
 #define fabs akili_probe_fabs
+/* The kb2 harnesses compare results in ulps: std::abs(fa.i - fb.i). */
+namespace std {
+inline int akili_probe_abs(int x) { return ::akili_probe_iabs(x); }
+}  // namespace std
+#define abs akili_probe_abs
 
 #endif

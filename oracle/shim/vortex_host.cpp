@@ -108,6 +108,44 @@ int run_oracle() {
     auto a = as<kbt_gemm_silu_mul_arg_t>(g_args);
     oracle_kbt_gemm_silu_mul(fp(a->a_addr), fp(a->wa_addr), fp(a->ba_addr), fp(a->wb_addr),
                              fp(a->bb_addr), fp(a->c_addr), a->M, a->N, a->K, 0, a->M);
+  } else if (op == "kb2_gemm_add_relu") {
+    auto a = as<kb2_gemm_add_relu_arg_t>(g_args);
+    oracle_kb2_gemm_add_relu(fp(a->a_addr), fp(a->w_addr), fp(a->bias_addr), fp(a->c_addr), a->M, a->N, a->K, 0,
+                             a->M);
+  } else if (op == "kb2_gemm_mul_leakyrelu") {
+    auto a = as<kb2_gemm_mul_leakyrelu_arg_t>(g_args);
+    oracle_kb2_gemm_mul_leakyrelu(fp(a->a_addr), fp(a->w_addr), fp(a->bias_addr), fp(a->c_addr), a->M, a->N, a->K,
+                                  a->multiplier, a->negative_slope, 0, a->M);
+  } else if (op == "kb2_gemm_div_sum_scale") {
+    auto a = as<kb2_gemm_div_sum_scale_arg_t>(g_args);
+    oracle_kb2_gemm_div_sum_scale(fp(a->a_addr), fp(a->w_addr), fp(a->c_addr), a->M, a->N, a->K,
+                                  a->scaling_factor, 0, a->M);
+  } else if (op == "kb2_gemm_layernorm") {
+    auto a = as<kb2_gemm_layernorm_arg_t>(g_args);
+    oracle_kb2_gemm_layernorm(fp(a->a_addr), fp(a->w_addr), fp(a->bias_addr), fp(a->ln_w_addr), fp(a->ln_b_addr),
+                              fp(a->c_addr), a->M, a->N, a->K, a->eps, 0, a->M);
+  } else if (op == "kb2_attention_score") {
+    auto a = as<kb2_attention_score_arg_t>(g_args);
+    oracle_kb2_attention_score(fp(a->q_addr), fp(a->k_addr), fp(a->c_addr), a->M, a->N, a->D, 0, a->M);
+  } else if (op == "kb2_matmul_softmax") {
+    auto a = as<kb2_matmul_softmax_arg_t>(g_args);
+    oracle_kb2_matmul_softmax(fp(a->a_addr), fp(a->b_addr), fp(a->c_addr), a->M, a->N, a->K, 0, a->M);
+  } else if (op == "kb2_matmul_scale_residadd_clamp") {
+    auto a = as<kb2_matmul_scale_residadd_clamp_arg_t>(g_args);
+    oracle_kb2_matmul_scale_residadd_clamp(fp(a->a_addr), fp(a->w_addr), fp(a->bias_addr), fp(a->c_addr), a->M,
+                                           a->N, a->K, a->scale_factor, a->clamp_min, a->clamp_max, 0, a->M);
+  } else if (op == "kb2_matmul_sum_max_avgpool") {
+    auto a = as<kb2_matmul_sum_max_avgpool_arg_t>(g_args);
+    oracle_kb2_matmul_sum_max_avgpool(fp(a->a_addr), fp(a->w_addr), fp(a->bias_addr), fp(a->c_addr), a->M, a->N,
+                                      a->K, 0, a->M);
+  } else if (op == "kb2_gemm_rmsnorm_swiglu") {
+    auto a = as<kb2_gemm_rmsnorm_swiglu_arg_t>(g_args);
+    oracle_kb2_gemm_rmsnorm_swiglu(fp(a->x_addr), fp(a->rms_w_addr), fp(a->wg_addr), fp(a->wu_addr),
+                                   fp(a->c_addr), a->M, a->N, a->K, a->eps, 0, a->M);
+  } else if (op == "kb2_gemm_silu_mul") {
+    auto a = as<kb2_gemm_silu_mul_arg_t>(g_args);
+    oracle_kb2_gemm_silu_mul(fp(a->a_addr), fp(a->wa_addr), fp(a->ba_addr), fp(a->wb_addr), fp(a->bb_addr),
+                             fp(a->c_addr), a->M, a->N, a->K, 0, a->M);
   } else if (op == "flash") {
     auto a = as<flash_arg_t>(g_args);
     oracle_flash(fp(a->O_addr), fp(a->Q_addr), fp(a->K_addr), fp(a->V_addr), a->seq_len,
@@ -139,6 +177,29 @@ extern "C++" float akili_probe_fabsf(float x) {
     std::fflush(rec);
   }
   return __builtin_fabsf(x);
+}
+
+/* Integer abs of the kb2 harnesses' ulp check, std::abs(actual_bits -
+ * expected_bits) (see probe.h): exact mode reports any non-zero difference as
+ * far beyond every tolerance; record mode appends the argument (as int32) to
+ * the same file as the fabs probe. */
+extern "C++" int akili_probe_iabs(int x) {
+  static int mode = -1;
+  static FILE* rec = nullptr;
+  if (mode < 0) {
+    const char* m = std::getenv("AKILI_PROBE");
+    mode = !m ? 0 : (std::strcmp(m, "exact") == 0 ? 1 : (std::strcmp(m, "record") == 0 ? 2 : 0));
+    if (mode == 2) {
+      const char* f = std::getenv("AKILI_PROBE_FILE");
+      rec = f ? std::fopen(f, "ab") : nullptr;
+    }
+  }
+  if (mode == 1) return x == 0 ? 0 : 0x7fffffff;
+  if (mode == 2 && rec) {
+    std::fwrite(&x, 4, 1, rec);
+    std::fflush(rec);
+  }
+  return x < 0 ? -x : x;
 }
 
 /* ---- runtime API ------------------------------------------------------- */

@@ -46,6 +46,16 @@ INPUTS = {
     "kbt_gemm_rmsnorm_swiglu": ["x", "rms_w", "wg", "wu"],
     "kbt_gemm_silu_mul": ["a", "wa", "ba", "wb", "bb"],
     "flash": ["Q", "K", "V", "O_init"],
+    "kb2_gemm_add_relu": ["a", "w", "bias"],
+    "kb2_gemm_mul_leakyrelu": ["a", "w", "bias"],
+    "kb2_gemm_div_sum_scale": ["a", "w"],
+    "kb2_gemm_layernorm": ["a", "w", "bias", "ln_w", "ln_b"],
+    "kb2_attention_score": ["q", "k"],
+    "kb2_matmul_softmax": ["a", "b"],
+    "kb2_matmul_scale_residadd_clamp": ["a", "w", "bias"],
+    "kb2_matmul_sum_max_avgpool": ["a", "w", "bias"],
+    "kb2_gemm_rmsnorm_swiglu": ["x", "rms_w", "wg", "wu"],
+    "kb2_gemm_silu_mul": ["a", "wa", "ba", "wb", "bb"],
 }
 
 # Verify-loop shape: ("rel", thr) = diff, fabsf(expected), and a third call
@@ -56,11 +66,18 @@ PATTERN = {
     "kbt_gemm_mul_leakyrelu": ("rel", np.float32(1e-6)),
     "kbt_gemm_div_sum_scale": ("rel", np.float32(1e-6)),
     "flash": ("flash", None),
+    # kb2 relative checks: fabsf(expected) first, then one more call per element
+    **{b: ("first", None) for b in ["kb2_gemm_add_relu", "kb2_gemm_mul_leakyrelu", "kb2_gemm_div_sum_scale",
+                                    "kb2_gemm_layernorm", "kb2_gemm_rmsnorm_swiglu", "kb2_gemm_silu_mul"]},
+    # kb2 ulp checks: std::abs(actual_bits - expected_bits), one int per element
+    **{b: ("ulp", None) for b in ["kb2_attention_score", "kb2_matmul_softmax", "kb2_matmul_scale_residadd_clamp",
+                                  "kb2_matmul_sum_max_avgpool"]},
 }
 
 CASES = {
     "kbt_sgemm": {"default": [], "m24n40p56": ["-m24", "-n40", "-p56"], "m8n136p72": ["-m8", "-n136", "-p72"]},
     "kbt_attention_score": {"default": [], "m24n40d16": ["-m24", "-n40", "-d16"], "m32n64d64": ["-m32", "-n64", "-d64"]},
+    "kb2_attention_score": {"default": [], "m24n40d16": ["-m24", "-n40", "-d16"], "m32n64d64": ["-m32", "-n64", "-d64"]},
     "flash": {"n64d8tcu": ["-n", "64", "-d", "8", "-t", "1"], "n128d16simt": ["-n", "128", "-d", "16", "-t", "0"],
               "n16d8tcu": ["-n", "16", "-d", "8", "-t", "1"]},
 }
@@ -71,6 +88,10 @@ def parse_expected(bench: str, rec: np.ndarray) -> np.ndarray:
     kind, thr = PATTERN.get(bench, ("abs", None))
     if kind == "abs":
         return -rec
+    if kind == "first":
+        return rec[0::2].copy()
+    if kind == "ulp":  # recorded int32 x = 0 - expected_bits
+        return (-rec.view(np.int32)).astype(np.int32).view(np.float32)
     out = []
     i = 0
     if kind == "flash":
@@ -109,7 +130,10 @@ def run_case(bench: str, tag: str, argv: list[str]) -> str:
 
 
 def main() -> int:
+    only = sys.argv[1:]  # optional: bench names (or prefixes) to (re)generate
     for bench in INPUTS:
+        if only and not any(bench.startswith(o) for o in only):
+            continue
         cases = CASES.get(bench, GEMM_DEFAULT_CASES)
         for tag, argv in cases.items():
             p = run_case(bench, tag, argv)

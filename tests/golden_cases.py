@@ -40,7 +40,9 @@ def oracle_eval(oracle, bench: str, arg, d: dict, round_inputs: bool = False) ->
         n, dd = arg.seq_len, arg.head_dim
         return oracle.flash(g["Q"], g["K"], g["V"], n, dd, 1.0).ravel()
     M, N = arg.M, arg.N
-    K = arg.D if bench == "kbt_attention_score" else arg.K
+    K = arg.D if bench in ("kbt_attention_score", "kb2_attention_score") else arg.K
+    if bench.startswith("kb2_"):
+        return _kb2_eval(oracle, bench, arg, g, M, N, K).ravel()
     if bench == "kbt_sgemm":
         out = oracle.kbt_sgemm(g["a"], g["b"], M, N, K)
     elif bench == "kbt_gemm_add_relu":
@@ -68,3 +70,28 @@ def oracle_eval(oracle, bench: str, arg, d: dict, round_inputs: bool = False) ->
     else:
         raise KeyError(bench)
     return out.ravel()
+
+
+def _kb2_eval(oracle, bench, arg, g, M, N, K):
+    if bench == "kb2_gemm_add_relu":
+        return oracle.kb2_gemm_add_relu(g["a"], g["w"], g["bias"], M, N, K)
+    if bench == "kb2_gemm_mul_leakyrelu":
+        return oracle.kb2_gemm_mul_leakyrelu(g["a"], g["w"], g["bias"], M, N, K, arg.multiplier, arg.negative_slope)
+    if bench == "kb2_gemm_div_sum_scale":
+        return oracle.kb2_gemm_div_sum_scale(g["a"], g["w"], M, N, K, arg.scaling_factor)
+    if bench == "kb2_gemm_layernorm":
+        return oracle.kb2_gemm_layernorm(g["a"], g["w"], g["bias"], g["ln_w"], g["ln_b"], M, N, K, arg.eps)
+    if bench == "kb2_attention_score":
+        return oracle.kb2_attention_score(g["q"], g["k"], M, N, K)
+    if bench == "kb2_matmul_softmax":
+        return oracle.kb2_matmul_softmax(g["a"], g["b"], M, N, K)
+    if bench == "kb2_matmul_scale_residadd_clamp":
+        return oracle.kb2_matmul_scale_residadd_clamp(g["a"], g["w"], g["bias"], M, N, K, arg.scale_factor,
+                                                      arg.clamp_min, arg.clamp_max)
+    if bench == "kb2_matmul_sum_max_avgpool":
+        return oracle.kb2_matmul_sum_max_avgpool(g["a"], g["w"], g["bias"], M, N, K)
+    if bench == "kb2_gemm_rmsnorm_swiglu":
+        return oracle.kb2_gemm_rmsnorm_swiglu(g["x"], g["rms_w"], g["wg"], g["wu"], M, N, K, arg.eps)
+    if bench == "kb2_gemm_silu_mul":
+        return oracle.kb2_gemm_silu_mul(g["a"], g["wa"], g["ba"], g["wb"], g["bb"], M, N, K)
+    raise KeyError(bench)

@@ -46,6 +46,17 @@ HARNESS_RUNS = {
     # (split-precision scores here), judged by the harness's own tolerance.
     "flash": [["-n", "64", "-d", "8", "-t", "1"], ["-n", "128", "-d", "16", "-t", "0"],
               ["-n", "256", "-d", "8", "-t", "0"]],
+    # the fp32 kb2 family: relative 1e-3 per element, or 20 ulps (FLOAT_ULP)
+    "kb2_gemm_add_relu": [[], ["-m24", "-n40", "-p56"]],
+    "kb2_gemm_mul_leakyrelu": [[], ["-m40", "-n24", "-p72"]],
+    "kb2_gemm_div_sum_scale": [[], ["-m64", "-n264", "-p64"]],
+    "kb2_gemm_layernorm": [[], ["-m64", "-n264", "-p64"]],
+    "kb2_attention_score": [[], ["-m64", "-n136", "-d64"]],
+    "kb2_matmul_softmax": [[], ["-m64", "-n136", "-p32"]],
+    "kb2_matmul_scale_residadd_clamp": [[], ["-m64", "-n136", "-p32"]],
+    "kb2_matmul_sum_max_avgpool": [[], ["-m64", "-n136", "-p32"]],
+    "kb2_gemm_rmsnorm_swiglu": [[], ["-m64", "-n256", "-p128"]],
+    "kb2_gemm_silu_mul": [[], ["-m64", "-n256", "-p128"]],
 }
 
 
@@ -59,7 +70,8 @@ def test_reference_harness_passes_on_b200(bench, argv):
     assert "PASSED!" in r.stdout, r.stdout[-1500:] + r.stderr[-1500:]
 
 
-@pytest.mark.parametrize("path", case_files(), ids=lambda p: os.path.basename(p)[:-4])
+@pytest.mark.parametrize("path", [p for p in case_files() if not os.path.basename(p).startswith("kb2_")],
+                         ids=lambda p: os.path.basename(p)[:-4])
 def test_golden_vectors_through_plain_entry(oracle, path):
     """Golden inputs (fp32, the harness's own rand() values) through akili_<bench>
     with reference semantics; compared with the oracle on the same operands

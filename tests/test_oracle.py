@@ -24,10 +24,13 @@ BENCHES = ["kbt_sgemm", "kbt_gemm_add_relu", "kbt_gemm_mul_leakyrelu", "kbt_gemm
            "kbt_gemm_layernorm", "kbt_attention_score", "kbt_matmul_softmax",
            "kbt_matmul_scale_residadd_clamp", "kbt_matmul_sum_max_avgpool", "kbt_gemm_rmsnorm_swiglu",
            "kbt_gemm_silu_mul", "flash"]
+KB2 = ["kb2_gemm_add_relu", "kb2_gemm_mul_leakyrelu", "kb2_gemm_div_sum_scale", "kb2_gemm_layernorm",
+       "kb2_attention_score", "kb2_matmul_softmax", "kb2_matmul_scale_residadd_clamp",
+       "kb2_matmul_sum_max_avgpool", "kb2_gemm_rmsnorm_swiglu", "kb2_gemm_silu_mul"]
 
 
 def test_every_bench_has_golden_cases():
-    for b in BENCHES:
+    for b in BENCHES + KB2:
         assert len(case_files(b)) >= 3, b
 
 
@@ -80,11 +83,11 @@ def _pin(bench, argv, **env):
     return r.returncode, r.stdout
 
 
-@pytest.mark.parametrize("bench", [b for b in BENCHES if b != "flash"])
+@pytest.mark.parametrize("bench", [b for b in BENCHES if b != "flash"] + KB2)
 @pytest.mark.parametrize("size", list(PIN_SIZES))
 def test_reference_harness_exact_pin(bench, size):
     argv = PIN_SIZES[size]
-    if bench == "kbt_attention_score":
+    if bench in ("kbt_attention_score", "kb2_attention_score"):
         argv = [a.replace("-p", "-d") for a in argv]
     rc, out = _pin(bench, argv)
     assert rc == 0 and "PASSED!" in out, out[-400:]
@@ -96,7 +99,8 @@ def test_reference_flash_harness_exact_pin(argv):
     assert rc == 0 and "PASSED!" in out, out[-400:]
 
 
-@pytest.mark.parametrize("bench", ["kbt_gemm_add_relu", "kbt_gemm_layernorm", "flash"])
+@pytest.mark.parametrize("bench", ["kbt_gemm_add_relu", "kbt_gemm_layernorm", "flash", "kb2_gemm_add_relu",
+                                   "kb2_matmul_softmax"])
 def test_exact_pin_negative_controls(bench):
     argv = ["-n", "64", "-d", "8", "-t", "1"] if bench == "flash" else []
     # (the harness returns its error count, which can wrap to exit status 0: read the text)
