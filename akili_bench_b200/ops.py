@@ -224,6 +224,17 @@ def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None, ke
     return o, m, l
 
 
+def kb2_gemm_add_relu(a, w, bias, out=None, stream=None):
+    """The fp32 kb2 form: a [M, K], w [K, N], bias [N], out [M, N], all fp32
+    (fp32 accuracy through the split-precision GEMM)."""
+    M, K = a.shape
+    N = w.shape[1]
+    c = out if out is not None else torch.empty((M, N), device=a.device, dtype=torch.float32)
+    arg = abi.Kb2GemmAddReluArg(M, N, K, _addr(a), _addr(w), _addr(bias), _addr(c))
+    abi.check("kb2_gemm_add_relu", arg, None, _stream(stream))
+    return c
+
+
 def launch_count() -> int:
     return int(abi.load().akili_launch_count())
 

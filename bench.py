@@ -151,6 +151,15 @@ def workloads(torch, ops):
         "kbt_gemm_silu_mul", {"M": M3, "N": N4, "K": K2}, 4.0 * M3 * N4 * K2, gemm_inputs(M3, N4, K2, 0.02, True),
         lambda d, out, st: ops.kbt_gemm_silu_mul(d["x"], d["w"], d["b"], d["w2"], d["b2"], out=out, stream=st))
 
+    # kb2: the fp32 SIMT family's add_relu at the C2 shape, fp32 in and out
+    def kb2_make(gen):
+        return {"x": _rand(torch, gen.x, (M2, K2)), "w": _rand(torch, gen.w, (K2, N2), K2 ** -0.5),
+                "b": _rand(torch, gen.w, (N2,), 0.1)}
+    W["kb2_gemm_add_relu"] = Workload(
+        "kb2_gemm_add_relu", {"M": M2, "N": N2, "K": K2, "precision": "fp32 (split fp16 hi+lo)"},
+        2.0 * M2 * N2 * K2, kb2_make, lambda d, out, st: ops.kb2_gemm_add_relu(d["x"], d["w"], d["b"], out=out,
+                                                                               stream=st))
+
     Ma, Na, Da = 16384, 4096, 128
 
     def as_make(gen):
