@@ -100,6 +100,11 @@ class AkiliEx(C.Structure):  # include/akili.h akili_ex_t
                 ("workspace", _u64), ("workspace_bytes", _u64)]
 
 
+class AttentionArg(C.Structure):  # benchmarks/attention/common.h:8-19
+    _fields_ = [("grid_dim", _u32 * 2), ("N", _u32), ("d", _u32), ("Q_addr", _u64), ("K_addr", _u64),
+                ("S_addr", _u64), ("P_addr", _u64), ("V_addr", _u64), ("O_addr", _u64), ("kernel_id", _u32)]
+
+
 # ---- kb2_* structs (benchmarks/kb2_<bench>/common.h): no launch fields ----
 _MNK = [("M", _u32), ("N", _u32), ("K", _u32)]
 
@@ -194,6 +199,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         fx = getattr(L, f"akili_{name}_ex")
         fx.argtypes = [C.POINTER(st), C.POINTER(AkiliEx), C.c_void_p]
         fx.restype = C.c_int
+    L.akili_attention.argtypes = [C.POINTER(AttentionArg), C.c_void_p]
+    L.akili_attention.restype = C.c_int
     L.akili_flash_ml_ex.argtypes = [C.POINTER(FlashArg), C.POINTER(AkiliEx), C.c_uint64, C.c_uint64, C.c_void_p]
     L.akili_flash_ml_ex.restype = C.c_int
     L.akili_kbt_gemm_layernorm_noalloc.argtypes = [C.POINTER(KbtGemmLayernormArg), C.POINTER(AkiliEx), C.c_void_p]

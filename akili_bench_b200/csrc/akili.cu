@@ -21,6 +21,7 @@
 #include <utility>
 
 #include "../../include/akili.h"
+#include "attention_unfused.cuh"
 #include "aux.cuh"
 #include "flash.cuh"
 #include "gemm.cuh"
@@ -1170,6 +1171,33 @@ int akili_flash_ex(const flash_arg_t* a, const akili_ex_t* ex, akili_stream_t s)
   return run_flash(j, md, S(s));
 }
 int akili_flash(const flash_arg_t* a, akili_stream_t s) { return akili_flash_ex(a, nullptr, s); }
+
+int akili_attention(const attention_arg_t* a, akili_stream_t s) {
+  if (!a) return AKILI_E_NULL_ARG;
+  if (a->N == 0 || a->d == 0) return AKILI_E_SHAPE;
+  if (a->kernel_id > 2) return AKILI_E_UNSUPPORTED;
+  int rc;
+  if (a->kernel_id == 0) rc = check_ptrs({a->Q_addr, a->K_addr, a->S_addr});
+  else if (a->kernel_id == 1) rc = check_ptrs({a->S_addr, a->P_addr});
+  else rc = check_ptrs({a->P_addr, a->V_addr, a->O_addr});
+  if (rc) return rc;
+  DevInfo di;
+  if ((rc = device_info(&di))) return rc;
+  const int N = static_cast<int>(a->N), d = static_cast<int>(a->d);
+  auto fp = [](uint64_t v) { return reinterpret_cast<float*>(static_cast<uintptr_t>(v)); };
+  cudaStream_t st = S(s);
+  if (a->kernel_id == 1) {
+    attention_softmax_kernel<<<grid_for(di, N, 8, 8), 256, 0, st>>>(fp(a->S_addr), fp(a->P_addr), N, N);
+  } else {
+    const int M = N, Nc = a->kernel_id == 0 ? N : d, K = a->kernel_id == 0 ? d : N;
+    const float* A = fp(a->kernel_id == 0 ? a->Q_addr : a->P_addr);
+    const float* B = fp(a->kernel_id == 0 ? a->K_addr : a->V_addr);
+    float* C = fp(a->kernel_id == 0 ? a->S_addr : a->O_addr);
+    dim3 grid((Nc + kAtTile - 1) / kAtTile, (M + kAtTile - 1) / kAtTile);
+    attention_matmul_kernel<<<grid, dim3(kAtTile, 8), 0, st>>>(A, B, C, M, Nc, K);
+  }
+  return launch_status();
+}
 
 int akili_flash_ml_ex(const flash_arg_t* a, const akili_ex_t* ex, uint64_t m_addr, uint64_t l_addr,
                       akili_stream_t s) {

@@ -80,6 +80,7 @@ int dispatch(const std::string& op, const void* a) {
   AKILI_DISPATCH(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t)
   AKILI_DISPATCH(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t)
   AKILI_DISPATCH(flash, flash_arg_t)
+  AKILI_DISPATCH(attention, attention_arg_t)
   AKILI_DISPATCH(kb2_gemm_add_relu, kb2_gemm_add_relu_arg_t)
   AKILI_DISPATCH(kb2_gemm_mul_leakyrelu, kb2_gemm_mul_leakyrelu_arg_t)
   AKILI_DISPATCH(kb2_gemm_div_sum_scale, kb2_gemm_div_sum_scale_arg_t)
@@ -219,5 +220,7 @@ int vx_check_occupancy(vx_device_h, uint32_t, uint32_t* max_localmem) {
   if (max_localmem) *max_localmem = 227 * 1024;
   return 0;
 }
+
+int vx_dump_perf(vx_device_h, FILE*) { return 0; }
 
 }  // extern "C"

@@ -177,6 +177,17 @@ typedef struct {
   uint64_t Q_addr, K_addr, V_addr, O_addr;
 } flash_arg_t;
 
+/* benchmarks/attention/common.h: the unfused three-kernel attention (fp32,
+ * one head); kernel_id selects 0: S = Q.K (K stored d x N), 1: P =
+ * softmax(S) by rows, 2: O = P.V. */
+typedef struct {
+  uint32_t grid_dim[2];
+  uint32_t N;
+  uint32_t d;
+  uint64_t Q_addr, K_addr, S_addr, P_addr, V_addr, O_addr;
+  uint32_t kernel_id;
+} attention_arg_t;
+
 /* ---- the kb2_* SIMT family: fp32 operands, fp32 arithmetic --------------
  * benchmarks/kb2_<bench>/common.h: the same ops without the Vortex launch
  * fields.  Their plain entries keep fp32 semantics (no fp16 rounding of the
@@ -332,6 +343,11 @@ int akili_flash_ex(const flash_arg_t* arg, const akili_ex_t* ex, akili_stream_t 
 int akili_flash_ml_ex(const flash_arg_t* arg, const akili_ex_t* ex, uint64_t m_addr, uint64_t l_addr,
                       akili_stream_t stream);
 
+/* benchmarks/attention/main.cpp:218, :288, :378: each of the
+ * three vx_start launches, chosen by arg->kernel_id, on fp32 buffers with
+ * fp32 CUDA-core arithmetic (S and O summed in the reference's order). */
+int akili_attention(const attention_arg_t* arg, akili_stream_t stream);
+
 /* kb2_* entries: each replaces the vx_upload_bytes + vx_start +
  * vx_ready_wait sequence of benchmarks/kb2_<bench>/main.cpp.  fp32 buffers,
  * fp32 results (see the kb2 structs above); the `_ex` form takes an
@@ -417,6 +433,10 @@ AKILI_CHECK_LAYOUT(kbt_gemm_rmsnorm_swiglu_arg_t, 96);
 AKILI_CHECK_LAYOUT(kbt_gemm_silu_mul_arg_t, 96);
 AKILI_CHECK_LAYOUT(flash_arg_t, 64);
 AKILI_CHECK_LAYOUT(akili_ex_t, 48);
+AKILI_CHECK_LAYOUT(attention_arg_t, 72);
+static_assert(offsetof(attention_arg_t, N) == 8 && offsetof(attention_arg_t, Q_addr) == 16 &&
+              offsetof(attention_arg_t, O_addr) == 56 && offsetof(attention_arg_t, kernel_id) == 64,
+              "attention offsets");
 AKILI_CHECK_LAYOUT(kb2_gemm_add_relu_arg_t, 48);
 AKILI_CHECK_LAYOUT(kb2_gemm_mul_leakyrelu_arg_t, 56);
 AKILI_CHECK_LAYOUT(kb2_gemm_div_sum_scale_arg_t, 40);

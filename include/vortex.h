@@ -17,6 +17,7 @@
 
 #include <stddef.h>
 #include <stdint.h>
+#include <stdio.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -63,6 +64,11 @@ int vx_upload_kernel_file(vx_device_h hdevice, const char* filename, vx_buffer_h
 int vx_upload_bytes(vx_device_h hdevice, const void* content, uint64_t size, vx_buffer_h* hbuffer);
 
 int vx_check_occupancy(vx_device_h hdevice, uint32_t group_size, uint32_t* max_localmem);
+
+/* Performance-counter dump (benchmarks/attention/main.cpp:248 calls it after
+ * each launch).  The B200 backend has no Vortex counters: it writes nothing
+ * and returns 0. */
+int vx_dump_perf(vx_device_h hdevice, FILE* stream);
 
 #ifdef __cplusplus
 }

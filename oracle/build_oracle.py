@@ -44,6 +44,7 @@ BENCHES = [
     "kbt_gemm_rmsnorm_swiglu",
     "kbt_gemm_silu_mul",
     "flash",
+    "attention",
     "kb2_gemm_add_relu",
     "kb2_gemm_mul_leakyrelu",
     "kb2_gemm_div_sum_scale",

@@ -518,6 +518,39 @@ void oracle_kb2_gemm_silu_mul(const float* a, const float* wa, const float* ba, 
     }
 }
 
+/* ---- benchmarks/attention: the unfused three-kernel attention (fp32) ---- */
+
+/* attention/main.cpp:55-65 (matmul_cpu): out[M x N] = A[M x K] . B[K x N],
+ * each element summed over k in order. */
+void oracle_attention_matmul(float* out, const float* A, const float* B, uint32_t M, uint32_t N, uint32_t K,
+                             uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t row = row0; row < row1; ++row)
+    for (uint32_t col = 0; col < N; ++col) {
+      float sum = 0.0f;
+      for (uint32_t e = 0; e < K; ++e) sum += A[(uint64_t)row * K + e] * B[(uint64_t)e * N + col];
+      out[(uint64_t)row * N + col] = sum;
+    }
+}
+
+/* attention/main.cpp:67-81 (softmax_cpu): per row, max from element 0
+ * (std::max), out = expf(x - max), then out /= sum in order. */
+void oracle_attention_softmax(float* out, const float* A, uint32_t M, uint32_t N, uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t row = row0; row < row1; ++row) {
+    const float* a = A + (uint64_t)row * N;
+    float* o = out + (uint64_t)row * N;
+    float max_val = a[0];
+    for (uint32_t col = 1; col < N; ++col) max_val = (max_val < a[col]) ? a[col] : max_val;
+    float exp_sum = 0.0f;
+    for (uint32_t col = 0; col < N; ++col) {
+      o[col] = expf(a[col] - max_val);
+      exp_sum += o[col];
+    }
+    for (uint32_t col = 0; col < N; ++col) o[col] /= exp_sum;
+  }
+}
+
 /* IEEE binary16 round-to-nearest-even, as the reference's f2h (`(__fp16)x`,
  * benchmarks/kbt_sgemm/kernel.cpp:13-18) and CUDA's __float2half_rn do.
  * Written from the format definition: 1 sign, 5 exponent (bias 15),

@@ -46,6 +46,8 @@ _SIGS = {
     "oracle_kb2_matmul_sum_max_avgpool": [_f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_kb2_gemm_rmsnorm_swiglu": [_f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _f, _u32, _u32],
     "oracle_kb2_gemm_silu_mul": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
+    "oracle_attention_matmul": [_f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
+    "oracle_attention_softmax": [_f32p, _f32p, _u32, _u32, _u32, _u32],
     "oracle_round_f16_array": [_f32p, C.c_uint64],
 }
 
@@ -288,4 +290,20 @@ def kb2_gemm_silu_mul(a, wa, ba, wb, bb, M, N, K, row0=0, row1=None, threads=1):
     c = np.zeros((M, N), np.float32)
     _rows(lib().oracle_kb2_gemm_silu_mul, (_p(a), _p(wa), _p(ba), _p(wb), _p(bb), _p(c)), (M, N, K), row0, row1,
           threads)
+    return c
+
+
+# ---- benchmarks/attention (unfused, fp32) ----
+
+def attention_matmul(a, b, M, N, K, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_attention_matmul, (_p(c), _p(a), _p(b)), (M, N, K), row0, row1, threads)
+    return c
+
+
+def attention_softmax(a, M, N, row0=0, row1=None, threads=1):
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_attention_softmax, (_p(c), _p(a)), (M, N), row0, row1, threads)
     return c

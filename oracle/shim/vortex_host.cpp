@@ -146,6 +146,14 @@ int run_oracle() {
     auto a = as<kb2_gemm_silu_mul_arg_t>(g_args);
     oracle_kb2_gemm_silu_mul(fp(a->a_addr), fp(a->wa_addr), fp(a->ba_addr), fp(a->wb_addr), fp(a->bb_addr),
                              fp(a->c_addr), a->M, a->N, a->K, 0, a->M);
+  } else if (op == "attention") {
+    auto a = as<attention_arg_t>(g_args);
+    if (a->kernel_id == 0)
+      oracle_attention_matmul(fp(a->S_addr), fp(a->Q_addr), fp(a->K_addr), a->N, a->N, a->d, 0, a->N);
+    else if (a->kernel_id == 1)
+      oracle_attention_softmax(fp(a->P_addr), fp(a->S_addr), a->N, a->N, 0, a->N);
+    else
+      oracle_attention_matmul(fp(a->O_addr), fp(a->P_addr), fp(a->V_addr), a->N, a->d, a->N, 0, a->N);
   } else if (op == "flash") {
     auto a = as<flash_arg_t>(g_args);
     oracle_flash(fp(a->O_addr), fp(a->Q_addr), fp(a->K_addr), fp(a->V_addr), a->seq_len,
@@ -273,9 +281,16 @@ int vx_start(vx_device_h, vx_buffer_h, vx_buffer_h) {
   int rc = run_oracle();
   if (rc == 0 && m && std::strcmp(m, "oracle_ulp") == 0) {
     /* negative control: move the first output element by one ulp */
-    uint64_t out = (g_op == "flash") ? as<flash_arg_t>(g_args)->O_addr
-                                     : *reinterpret_cast<const uint64_t*>(g_args.data() + g_args.size() - 8 *
-                                           (g_op == "kbt_matmul_scale_residadd_clamp" ? 2 : 1));
+    uint64_t out;
+    if (g_op == "flash") {
+      out = as<flash_arg_t>(g_args)->O_addr;
+    } else if (g_op == "attention") {
+      auto a = as<attention_arg_t>(g_args);
+      out = a->kernel_id == 0 ? a->S_addr : (a->kernel_id == 1 ? a->P_addr : a->O_addr);
+    } else {
+      out = *reinterpret_cast<const uint64_t*>(g_args.data() + g_args.size() -
+                                               8 * (g_op == "kbt_matmul_scale_residadd_clamp" ? 2 : 1));
+    }
     float* c = fp(out);
     c[0] = std::nextafter(c[0], INFINITY);
   }
@@ -286,5 +301,7 @@ int vx_check_occupancy(vx_device_h, uint32_t, uint32_t* max_localmem) {
   *max_localmem = 16384;
   return 0;
 }
+
+int vx_dump_perf(vx_device_h, FILE*) { return 0; }
 
 }  // extern "C"

@@ -130,3 +130,14 @@ def test_causal_flash_oracle_known_answers(oracle, S, D):
     np.testing.assert_allclose(l_c, np.exp(s64c - s64c.max(1, keepdims=True)).sum(1), rtol=1e-4)
     p = np.exp(s64c - s64c.max(1, keepdims=True))
     np.testing.assert_allclose(o_c, (p / p.sum(1, keepdims=True)) @ v, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("argv", [[], ["-n", "128", "-d", "16"], ["-n", "200", "-d", "24"]],
+                         ids=lambda a: "".join(a).replace("-", "_") or "default")
+def test_reference_attention_harness_exact_pin(argv):
+    """benchmarks/attention: all three stages exact.  Its harness resets the
+    error count before the last stage, so no stage may print an error line."""
+    rc, out = _pin("attention", argv)
+    assert "PASSED!" in out and "*** error" not in out, out[-400:]
+    rc, out = _pin("attention", argv, AKILI_HOST_DEVICE="oracle_ulp")
+    assert out.count("*** error") == 3  # one moved element per stage
