@@ -41,9 +41,10 @@ constexpr int kFlashThreads = 64 + 128 * kFlashQTiles;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Of each group of kExpGroup consecutive score pairs, the last is exponentiated
-// by exp2_fma, the others by the MUFU's exp2; 0 keeps every exponential on the
-// MUFU, which measured fastest once the softmax loop was trimmed (C5: 911 vs
-// 882 TFLOP/s with one pair in four on the FMA pipe).
+// on the FMA pipe (exp2_fma3_pair), the others by the MUFU's exp2; 0 keeps every
+// exponential on the MUFU, which measured fastest once the softmax loop used
+// packed fp32x2 arithmetic (C5: 0.587 TFLOP/s per MHz against 0.559, 0.564
+// and 0.537 with one pair in 4, 3 and 2 on the FMA pipe).
 #ifndef AKILI_FLASH_EXP_GROUP
 #define AKILI_FLASH_EXP_GROUP 0
 #endif
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&rel[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 128);
+      mbar_init(&p_full[s], 4);  // one arrive per softmax warp
       mbar_init(&o_done[s], 1);
     }
     mbar_init(drain, 1);
@@ -282,7 +283,7 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
       if (nvalid >= kFlashBN) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) mx[i & 7] = fmaxf(mx[i & 7], s[i]);
+        for (int i = 0; i < 64; ++i) mx[i & 7] = fmax3(mx[i & 7], s[2 * i], s[2 * i + 1]);
       } else {
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
@@ -306,26 +307,41 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
           tmem_st32(tO + c * 32, o);
         }
       }
-      // P = exp2(s * sl - m) as packed fp16 into the first 64 columns of S
-      // (one FFMA + one exponential per score; one store).
-      const float nm = -m_new;
-      float sm[8];
+      // P = exp2(s * sl - m) as packed fp16 into the first 64 columns of S:
+      // per score pair one packed FFMA, two exponentials (MUFU, or the FMA
+      // pipe for one pair in kExpGroup), one packed add into the row sum and
+      // one pack; one TMEM store.
+      const uint64_t sl2 = f2_pack(sl, sl);
+      const uint64_t nm2 = f2_pack(-m_new, -m_new);
+      uint64_t sm2[4];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) sm[a] = 0.0f;
+      for (int a = 0; a < 4; ++a) sm2[a] = 0ull;
       uint32_t pk[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const bool fma_pipe = kExpGroup > 0 && (i % (kExpGroup > 0 ? kExpGroup : 1)) == kExpGroup - 1;
-        const float x0 = fmaf(s[2 * i], sl, nm), x1 = fmaf(s[2 * i + 1], sl, nm);
-        const float p0 = fma_pipe ? exp2_fma(x0) : ex2_mufu(x0);
-        const float p1 = fma_pipe ? exp2_fma(x1) : ex2_mufu(x1);
-        sm[i & 7] += p0 + p1;
+        float x0, x1, p0, p1;
+        f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2, nm2), x0, x1);
+        if (fma_pipe) {
+          exp2_fma3_pair(x0, x1, p0, p1);
+        } else {
+          p0 = ex2_mufu(x0);
+          p1 = ex2_mufu(x1);
+        }
+        sm2[i & 3] = f2_add(sm2[i & 3], f2_pack(p0, p1));
         pk[i] = pack_half2(p0, p1);
       }
       tmem_st64(tS, pk);
-      const float rsum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+      float sv[8];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) f2_unpack(sm2[a], sv[2 * a], sv[2 * a + 1]);
+      const float rsum = ((sv[0] + sv[1]) + (sv[2] + sv[3])) + ((sv[4] + sv[5]) + (sv[6] + sv[7]));
+      // P of this warp's 32 rows is in TMEM (tcgen05.st waited): one arrive
+      // per warp; 128 per-thread arrives on one mbarrier serialise for
+      // hundreds of cycles on the path from softmax to the P.V MMA.
       tc_fence_before();
-      mbar_arrive(&p_full[grp]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[grp]);
       l = l * alpha + rsum;
       m_use = m_new;
     }

@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 4);  // one arrive per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -508,7 +508,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         st[h] = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, m_blk * kBM, r, h * HC, min((h + 1) * HC, nchunks),
                                        staging, 1, ep_tid == 0, chunk_ctr);
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
       write_stats<E>(ea, 2 * n_blk, row, st[0]);
       write_stats<E>(ea, 2 * n_blk + 1, row, st[1]);
     }

@@ -433,6 +433,59 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - __float_as_int(kMagic)) << 23));
 }
 
+// ---- packed fp32x2 arithmetic (sm_100): two lanes of work per instruction ----
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x0, 2^x1 on the FMA pipe with packed fp32x2 steps: the magic-number split
+// of exp2_fma and a cubic for 2^f on [-0.5, 0.5] (fitted for this library by
+// iteratively reweighted least squares on the relative error: max 7.5e-5,
+// below the 4.9e-4 of fp16), for values that are rounded to fp16 next.
+// Inputs are clamped at -127.
+__device__ __forceinline__ void exp2_fma3_pair(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.0f;
+  const uint64_t x = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
+  const uint64_t magic = f2_pack(kMagic, kMagic);
+  const uint64_t t = f2_add(x, magic);
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));
+  uint64_t p = f2_fma(f2_pack(0.055174145847558975f, 0.055174145847558975f), f,
+                      f2_pack(0.24261757731437683f, 0.24261757731437683f));
+  p = f2_fma(p, f, f2_pack(0.6932610869407654f, 0.6932610869407654f));
+  p = f2_fma(p, f, f2_pack(0.9999275803565979f, 0.9999275803565979f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - __float_as_int(kMagic)) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - __float_as_int(kMagic)) << 23));
+}
+
 // 2^x for two fp16 values in one MUFU instruction (x packed as fp16x2).
 __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
   uint32_t y;
