@@ -3,28 +3,30 @@
 //
 //   O[bh, i, :] = sum_j softmax_j(scale * Q[bh,i,:].K[bh,j,:]) V[bh, j, :]
 //
-// One CTA per (256 queries = two 128-row Q tiles, batch*head), 320 threads:
-//   warp 0      TMA: both Q tiles once, then K_j and V_j (128 keys each)
-//               into two-deep K and V rings.
-//   warp 1      TMEM owner and MMA issuer.  Per key block j and Q tile t:
-//                 O_t += P_t,j-1 . V_j-1   (A = P from TMEM, B = V, MN-major)
-//                 S_t,j  = Q_t . K_j^T     (into the columns P_t,j-1 occupied)
-//               Issued in that order on one thread, the MMAs run in order, so
-//               S may overwrite P once the P.V that reads it is ahead of it.
-//   warps 2..5  softmax of Q tile 0; warps 6..9 softmax of Q tile 1 (one
-//               thread per query row).  While one tile's softmax runs, the
-//               tensor core works on the other tile.  Per block: read S_t,j
-//               from TMEM (scores never leave the chip), take the row max in
-//               the log2 domain, write P = exp2(scale*log2e*s - m) as packed
-//               fp16 back into the first 64 columns of S_t, and rescale O_t
-//               in TMEM only when the running max grows by more than 2^8
-//               (the stale max cancels in O / l).  S_t,j being complete
-//               implies O_t += P_t,j-1 V_j-1 is complete, so the rescale
-//               never races the accumulation.
-// Finally each softmax group divides its O rows by l, stages them through
-// swizzled shared memory (the drained K ring) and TMA-stores them.  Head dims
-// up to 64 use a 64-column tile, up to 128 a 128-column tile; TMA zero-fills
-// the padding and the key tail; keys >= seq_len are masked to -inf.
+// One CTA per (256 queries = two 128-row Q tiles, batch*head), 576 threads:
+//   warp 0       TMA: both Q tiles once, then K_j and V_j (128 keys each)
+//                into two-deep K and V rings.
+//   warp 1       TMEM owner and MMA issuer.  Per key block j and Q tile t:
+//                  O_t += P_t,j-1 . V_j-1   (A = P from TMEM, B = V, MN-major)
+//                  S_t,j  = Q_t . K_j^T     (into the columns P_t,j-1 occupied)
+//                Issued in that order on one thread, the MMAs run in order, so
+//                S may overwrite P once the P.V that reads it is ahead of it.
+//   warps 2..9   softmax of Q tile 0, warps 10..17 of Q tile 1: two threads
+//                per query row, each taking 64 of the block's 128 scores.
+//                While one tile's softmax runs, the tensor core works on the
+//                other tile.  Per block: read the half's 64 scores of S_t,j
+//                from TMEM (scores never leave the chip), swap the halves'
+//                maxima through shared memory (one barrier per tile), write
+//                P = exp2(scale*log2e*s - m) as packed fp16 over the first 64
+//                columns of S_t, and rescale O_t in TMEM only when the running
+//                max grows by more than 2^8 (the stale max cancels in O / l).
+//                S_t,j being complete implies O_t += P_t,j-1 V_j-1 is
+//                complete, so the rescale never races the accumulation.
+// Finally the halves add their row sums, and each divides its O columns by l,
+// stages them through swizzled shared memory (the drained K/V rings) and
+// TMA-stores them.  Head dims up to 64 use a 64-column tile, up to 128 a
+// 128-column tile; TMA zero-fills the padding and the key tail; keys >=
+// seq_len (and, causal, after the query) are masked to -inf.
 #pragma once
 #include <cuda_fp16.h>
 
@@ -37,7 +39,9 @@ namespace akili {
 constexpr int kFlashBM = 128;  // query rows per Q tile (two tiles per CTA)
 constexpr int kFlashBN = 128;  // keys per block
 constexpr int kFlashQTiles = 2;
-constexpr int kFlashThreads = 64 + 128 * kFlashQTiles;
+// Two threads per query row: each softmax warp takes 64 of a block's 128
+// scores for 32 rows, so a Q tile has 8 softmax warps (two halves of 4).
+constexpr int kFlashThreads = 64 + 256 * kFlashQTiles;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Of each group of kExpGroup consecutive score pairs, the last is exponentiated
@@ -70,13 +74,18 @@ struct FlashSmem {
   static constexpr int kKOff = kQOff + kFlashQTiles * kQ * kParts;
   static constexpr int kVOff = kKOff + 2 * kKV * kParts;
   static constexpr int kBarOff = kVOff + 2 * kKV;
-  static constexpr int kBytes = kBarOff + 256 + 1024;
+  // row-statistics exchange between the two halves of a row:
+  // [parity][tile][half][128 rows] floats
+  static constexpr int kXOff = kBarOff + 256;
+  static constexpr int kBytes = kXOff + 2 * kFlashQTiles * 2 * kFlashBM * 4 + 1024;
   // the output staging of both softmax groups reuses the drained K/V rings
-  static_assert(2 * 2 * kFlashBM * 32 * 4 <= 4 * kKV, "staging must fit in the K/V rings");
+  static_assert(2 * kFlashQTiles * (DP / 64) * kFlashBM * 32 * 4 <= 4 * kKV, "staging must fit in the K/V rings");
 };
 
+// 18 warps put five on two of the SM sub-partitions, whose 16384 registers
+// then allow at most 102 per thread.
 template <int DP, typename OutT, bool kSplit>
-__global__ void __launch_bounds__(kFlashThreads, 1)
+__global__ void __maxnreg__(96)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                      const __grid_constant__ CUtensorMap tmQlo, const __grid_constant__ CUtensorMap tmKlo,
@@ -101,7 +110,9 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
   uint64_t* o_done = bars + 13;   // [2] per Q tile
   uint64_t* drain = bars + 15;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);  // [2]
+  // [tile][parity]: a wait that gave up in block j sets slot j & 1, read by
+  // the whole tile after block j's barrier (the next block's slot is apart)
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
 
   const int N = fa.seq_len;
   // Causal: the CTA of query tile pair x visits 2x + 2 key blocks, so the
@@ -124,12 +135,11 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&rel[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_full[s], 4);  // one arrive per softmax warp
+      mbar_init(&p_full[s], 8);  // one arrive per softmax warp of the tile
       mbar_init(&o_done[s], 1);
     }
     mbar_init(drain, 1);
-    abort_flag[0] = 0;
-    abort_flag[1] = 0;
+    for (int i = 0; i < 2 * kFlashQTiles; ++i) abort_flag[i] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -245,80 +255,81 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     __syncwarp();
   } else {
     // --------------------------------------------------- softmax / output
-    const int grp = (static_cast<int>(warp) - 2) >> 2;  // Q tile of this warpgroup
-    const int ep_tid = threadIdx.x - 64 - 128 * grp;    // 0..127 within the group
+    // Warps 2 + 8t .. 9 + 8t serve Q tile t: half h = ((warp - 2) >> 2) & 1
+    // takes scores [64h, 64h + 64) of each block and O columns
+    // [h * DP/2, (h + 1) * DP/2) of its rows (thread = row within the TMEM
+    // lane quarter warp & 3).  The halves of a row swap their block maxima
+    // through shared memory behind one 256-thread barrier per block, which
+    // also orders every S load of the tile before any P store.
+    const int grp = (static_cast<int>(warp) - 2) >> 3;  // Q tile
+    const int half = ((static_cast<int>(warp) - 2) >> 2) & 1;
     const int wq = static_cast<int>(warp & 3);          // TMEM lane quarter
     const int r = wq * 32 + static_cast<int>(lane);
-    const uint32_t bar_id = 1 + grp;
+    const int gtid = threadIdx.x - 64 - 256 * grp - 128 * half;  // 0..127 within (tile, half)
+    const uint32_t tile_bar = 1 + grp;                  // 256 threads
+    const uint32_t half_bar = 3 + 2 * grp + half;       // 128 threads
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_off + grp * 128;
-    const uint32_t tO = tmem + lane_off + kColO + grp * 128;
+    const uint32_t tS = tmem + lane_off + grp * 128 + half * 64;   // this half's 64 scores
+    const uint32_t tP = tmem + lane_off + grp * 128 + half * 32;   // its 32 packed P columns
+    const uint32_t tO = tmem + lane_off + kColO + grp * 128 + half * (DP / 2);
+    float* xchg = reinterpret_cast<float*>(smem + L::kXOff);
     const float sl = fa.scale_log2;
     float m_use = -INFINITY;
     float m_true = -INFINITY;  // the row's exact running max (m_use may lag it by the rescale threshold)
-    float l = 0.0f;
+    float l = 0.0f;            // this half's share of the row sum
     const int qrow = m0 + grp * kFlashBM + r;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait(&s_full[grp], j & 1, kSiteFlashS)) abort_flag[grp] = 1;
-      named_bar_sync(bar_id, 128);
-      if (abort_flag[grp]) {
-        ok = false;
-        break;
-      }
+      if (!mbar_wait(&s_full[grp], j & 1, kSiteFlashS)) abort_flag[2 * grp + (j & 1)] = 1;
       tc_fence_after();
-      const int kv0 = j * kFlashBN;
-      // One wide TMEM load of the 128 scores of this row, then the row max in
-      // the log2 domain (keys past the end are masked).
-      float s[128];
-      tmem_ld128(tS, s);
-      // keys of this block the row may see: all but those past the end and,
+      const int kv0 = j * kFlashBN + half * 64;
+      float s[64];
+      tmem_ld64(tS, s);
+      // keys of this half the row may see: all but those past the end and,
       // when causal, those after the row's own index (may be <= 0)
       const int nvalid = fa.causal ? min(N - kv0, qrow - kv0 + 1) : N - kv0;
-      // Row max of the raw scores (the scale is positive, so it commutes with
-      // max); keys past the end exist only in the last block and are set to
-      // -inf there, so full blocks carry no per-element masking.
+      // Max of the raw scores (the scale is positive, so it commutes with
+      // max); masked keys exist only in a tail or diagonal block.
       float mx[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx[a] = -INFINITY;
-      if (nvalid >= kFlashBN) {
+      if (nvalid >= 64) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx[i & 7] = fmax3(mx[i & 7], s[2 * i], s[2 * i + 1]);
+        for (int i = 0; i < 32; ++i) mx[i & 7] = fmax3(mx[i & 7], s[2 * i], s[2 * i + 1]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < 64; ++i) {
           if (i >= nvalid) s[i] = -INFINITY;
           mx[i & 7] = fmaxf(mx[i & 7], s[i]);
         }
       }
-      const float rmax = sl * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float pmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      float* xs = xchg + ((j & 1) * kFlashQTiles + grp) * (2 * kFlashBM);
+      xs[half * kFlashBM + r] = pmax;
+      tc_fence_before();
+      named_bar_sync(tile_bar, 256);
+      tc_fence_after();
+      if (abort_flag[2 * grp + (j & 1)]) {
+        ok = false;
+        break;
+      }
+      const float rmax = sl * fmaxf(pmax, xs[(half ^ 1) * kFlashBM + r]);
       m_true = fmaxf(m_true, rmax);
       const bool grow = rmax > m_use + kRescaleThreshold;
       const float m_new = grow ? rmax : m_use;
       const float alpha = grow ? exp2f(m_use - m_new) : 1.0f;  // 0 on the first block
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll 1
-        for (int c = 0; c < DP / 32; ++c) {
-          float o[32];
-          tmem_ld32(tO + c * 32, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      // P = exp2(s * sl - m) as packed fp16 into the first 64 columns of S:
-      // per score pair one packed FFMA, two exponentials (MUFU, or the FMA
-      // pipe for one pair in kExpGroup), one packed add into the row sum and
-      // one pack; one TMEM store.
+      // P = exp2(s * sl - m) as packed fp16: per score pair one packed FFMA,
+      // two exponentials (MUFU, or the FMA pipe for one pair in kExpGroup),
+      // one packed add into the row sum and one pack; one TMEM store.
       const uint64_t sl2 = f2_pack(sl, sl);
       const uint64_t nm2 = f2_pack(-m_new, -m_new);
       uint64_t sm2[4];
 #pragma unroll
       for (int a = 0; a < 4; ++a) sm2[a] = 0ull;
-      uint32_t pk[64];
+      float pk[32];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const bool fma_pipe = kExpGroup > 0 && (i % (kExpGroup > 0 ? kExpGroup : 1)) == kExpGroup - 1;
         float x0, x1, p0, p1;
         f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2, nm2), x0, x1);
@@ -329,55 +340,74 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
           p1 = ex2_mufu(x1);
         }
         sm2[i & 3] = f2_add(sm2[i & 3], f2_pack(p0, p1));
-        pk[i] = pack_half2(p0, p1);
+        pk[i] = __uint_as_float(pack_half2(p0, p1));
       }
-      tmem_st64(tS, pk);
+      tmem_st32(tP, pk);
       float sv[8];
 #pragma unroll
       for (int a = 0; a < 4; ++a) f2_unpack(sm2[a], sv[2 * a], sv[2 * a + 1]);
       const float rsum = ((sv[0] + sv[1]) + (sv[2] + sv[3])) + ((sv[4] + sv[5]) + (sv[6] + sv[7]));
-      // P of this warp's 32 rows is in TMEM (tcgen05.st waited): one arrive
-      // per warp; 128 per-thread arrives on one mbarrier serialise for
-      // hundreds of cycles on the path from softmax to the P.V MMA.
+      // Rescale this half's O columns when the running max grew (rare after
+      // the first blocks): S_t,j being complete implies O_t += P_t,j-1 V_j-1
+      // is, and the next P.V waits for this warp's arrive below.
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+        for (int c = 0; c < DP / 64; ++c) {
+          float o[32];
+          tmem_ld32(tO + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      // this warp's P is in TMEM (tcgen05.st waited): one arrive per warp
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[grp]);
       l = l * alpha + rsum;
       m_use = m_new;
     }
-    if (ok && fa.m_out != nullptr && qrow < N) {
-      // softmax statistics in the reference's natural-log form
-      const size_t o = static_cast<size_t>(bh) * N + qrow;
-      fa.m_out[o] = m_true * 0.6931471805599453f;
-      fa.l_out[o] = l * exp2f(m_use - m_true);
-    }
     if (ok && nkv >= 1) {
-      if (!mbar_wait(&o_done[grp], 0, kSiteFlashPV)) abort_flag[grp] = 1;
-      named_bar_sync(bar_id, 128);
-      if (!abort_flag[grp]) {
+      // The row sum: the two halves' shares (slot of parity nkv, last read
+      // two blocks ago).
+      float* xs = xchg + ((nkv & 1) * kFlashQTiles + grp) * (2 * kFlashBM);
+      xs[half * kFlashBM + r] = l;
+      named_bar_sync(tile_bar, 256);
+      const float lt = l + xs[(half ^ 1) * kFlashBM + r];
+      if (fa.m_out != nullptr && half == 0 && qrow < N) {
+        // softmax statistics in the reference's natural-log form
+        const size_t o = static_cast<size_t>(bh) * N + qrow;
+        fa.m_out[o] = m_true * 0.6931471805599453f;
+        fa.l_out[o] = lt * exp2f(m_use - m_true);
+      }
+      if (!mbar_wait(&o_done[grp], 0, kSiteFlashPV)) abort_flag[2 * grp + (nkv & 1)] = 1;
+      named_bar_sync(tile_bar, 256);
+      if (!abort_flag[2 * grp + (nkv & 1)]) {
         tc_fence_after();
-        const float inv_l = 1.0f / l;
-        // Staging: each group takes its own 2 x kStageOut span of the K/V rings,
-        // drained once o_done fires (both groups fit in the 4 ring slots).
-        uint8_t* stg_base = sK + grp * 2 * kStageOut;
-        const int ncols = (fa.head_dim + 31) / 32;
+        const float inv_l = 1.0f / lt;
+        // Staging: each (tile, half) takes its own span of the drained K/V
+        // rings, one or two 128 x 32 buffers.
+        constexpr int kNBuf = DP / 64;  // 32-column chunks per half (1 or 2)
+        uint8_t* stg_base = sK + (2 * grp + half) * kNBuf * kStageOut;
+        const int c_lo = half * (DP / 2);
+        const int ncols = max(0, min(DP / 2, fa.head_dim - c_lo) + 31) / 32;
         for (int c = 0; c < ncols; ++c) {
           float o[32];
           tmem_ld32(tO + c * 32, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= inv_l;
-          uint8_t* stg = stg_base + (c & 1) * kStageOut;
-          if (ep_tid == 0) bulk_wait_read<1>();
-          named_bar_sync(bar_id, 128);
+          uint8_t* stg = stg_base + (c % kNBuf) * kStageOut;
+          if (gtid == 0) bulk_wait_read<kNBuf - 1>();
+          named_bar_sync(half_bar, 128);
           stage_row<OutT>(stg, r, o);
           fence_async_shared();
-          named_bar_sync(bar_id, 128);
-          if (ep_tid == 0) {
-            tma_store_3d(&tmO, stg, c * 32, m0 + grp * kFlashBM, bh);
+          named_bar_sync(half_bar, 128);
+          if (gtid == 0) {
+            tma_store_3d(&tmO, stg, c_lo + c * 32, m0 + grp * kFlashBM, bh);
             bulk_commit();
           }
         }
-        if (ep_tid == 0) bulk_wait<0>();
+        if (gtid == 0) bulk_wait<0>();
       }
     }
   }
