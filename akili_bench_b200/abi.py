@@ -105,6 +105,15 @@ class AttentionArg(C.Structure):  # benchmarks/attention/common.h:8-19
                 ("S_addr", _u64), ("P_addr", _u64), ("V_addr", _u64), ("O_addr", _u64), ("kernel_id", _u32)]
 
 
+class MatmulKernelArgs(C.Structure):  # benchmarks/llama2/common.h:3-12
+    _fields_ = [("grid_dim", _u32 * 2), ("block_dim", _u32 * 2), ("A_addr", _u64), ("B_addr", _u64),
+                ("C_addr", _u64), ("M", C.c_int32), ("N", C.c_int32), ("K", C.c_int32)]
+
+
+class MatvecSeg(C.Structure):  # include/akili.h akili_matvec_seg_t
+    _fields_ = [("W_addr", _u64), ("C_addr", _u64), ("rows", C.c_int32), ("reserved", C.c_int32)]
+
+
 # ---- kb2_* structs (benchmarks/kb2_<bench>/common.h): no launch fields ----
 _MNK = [("M", _u32), ("N", _u32), ("K", _u32)]
 
@@ -201,6 +210,10 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         fx.restype = C.c_int
     L.akili_attention.argtypes = [C.POINTER(AttentionArg), C.c_void_p]
     L.akili_attention.restype = C.c_int
+    L.akili_llama2_matmul.argtypes = [C.POINTER(MatmulKernelArgs), C.c_void_p]
+    L.akili_llama2_matmul.restype = C.c_int
+    L.akili_llama2_matvec_batch.argtypes = [C.POINTER(MatvecSeg), C.c_int, C.c_uint64, C.c_int32, C.c_void_p]
+    L.akili_llama2_matvec_batch.restype = C.c_int
     L.akili_flash_ml_ex.argtypes = [C.POINTER(FlashArg), C.POINTER(AkiliEx), C.c_uint64, C.c_uint64, C.c_void_p]
     L.akili_flash_ml_ex.restype = C.c_int
     L.akili_kbt_gemm_layernorm_noalloc.argtypes = [C.POINTER(KbtGemmLayernormArg), C.POINTER(AkiliEx), C.c_void_p]

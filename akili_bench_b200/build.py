@@ -10,8 +10,11 @@
 * ``libakili_vortex.so`` csrc/vortex_shim.cpp — the Vortex runtime API of
                          include/vortex.h on top of libakili.so, for
                          akili-bench's unchanged host harnesses.
+* ``libakili_vxmath.so`` csrc/vxmath_b200.cpp — the llama2 matmul offload
+                         API (benchmarks/llama2/vxmath.h) on top of
+                         libakili.so, for the unchanged llama2/llama.cpp.
 
-Both land next to this file so they travel with the working tree.
+All land next to this file so they travel with the working tree.
 """
 from __future__ import annotations
 
@@ -32,10 +35,12 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared"
 
 LIB = os.path.join(HERE, "libakili.so")
 VORTEX_LIB = os.path.join(HERE, "libakili_vortex.so")
+VXMATH_LIB = os.path.join(HERE, "libakili_vxmath.so")
 
 
 def _sources():
-    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC))] + [os.path.join(ROOT, "include", "akili.h")]
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith((".cu", ".cuh"))] + \
+        [os.path.join(ROOT, "include", "akili.h")]
 
 
 def _stale(out: str, deps: list[str]) -> bool:
@@ -58,18 +63,19 @@ def build(force: bool = False, verbose: bool = False) -> list[str]:
         if verbose:
             print(" ".join(cmd))
         _run(cmd)
-    vdeps = [os.path.join(CSRC, "vortex_shim.cpp"), os.path.join(ROOT, "include", "vortex.h"), LIB]
-    if force or _stale(VORTEX_LIB, vdeps):
-        cuda_inc = os.path.join(os.path.dirname(os.path.dirname(os.path.realpath(NVCC))), "include") \
-            if os.path.isabs(NVCC) else "/usr/local/cuda/include"
-        cuda_lib = os.path.join(os.path.dirname(cuda_inc), "lib64")
-        cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"), "-I", cuda_inc,
-               os.path.join(CSRC, "vortex_shim.cpp"), "-o", VORTEX_LIB, "-L", HERE, "-lakili",
-               f"-Wl,-rpath,{HERE}", "-L", cuda_lib, "-lcudart_static", "-ldl", "-lpthread", "-lrt"]
-        if verbose:
-            print(" ".join(cmd))
-        _run(cmd)
-    return [LIB, VORTEX_LIB]
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(os.path.realpath(NVCC))), "include") \
+        if os.path.isabs(NVCC) else "/usr/local/cuda/include"
+    cuda_lib = os.path.join(os.path.dirname(cuda_inc), "lib64")
+    for src, out, hdr in (("vortex_shim.cpp", VORTEX_LIB, "vortex.h"), ("vxmath_b200.cpp", VXMATH_LIB, "akili.h")):
+        hdeps = [os.path.join(CSRC, src), os.path.join(ROOT, "include", hdr), LIB]
+        if force or _stale(out, hdeps):
+            cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"), "-I",
+                   cuda_inc, os.path.join(CSRC, src), "-o", out, "-L", HERE, "-lakili", f"-Wl,-rpath,{HERE}", "-L",
+                   cuda_lib, "-lcudart_static", "-ldl", "-lpthread", "-lrt"]
+            if verbose:
+                print(" ".join(cmd))
+            _run(cmd)
+    return [LIB, VORTEX_LIB, VXMATH_LIB]
 
 
 if __name__ == "__main__":

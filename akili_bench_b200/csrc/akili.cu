@@ -12,7 +12,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cstdint>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -25,6 +27,7 @@
 #include "aux.cuh"
 #include "flash.cuh"
 #include "gemm.cuh"
+#include "matvec.cuh"
 #include "softmax_rows.cuh"
 
 using namespace akili;
@@ -1096,6 +1099,47 @@ int entry_kb2(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
   return run_job(j, md, S(s));
 }
 
+// ------------------------------------------------------ llama2 offload --
+// x is staged in shared memory up to this size (the largest llama2 K is the
+// FFN hidden size, 11008 for 7B: 44 KB).
+constexpr size_t kMatvecSmemMax = 200 * 1024;
+
+template <bool kVec, bool kSmemX>
+int launch_matvec_t(const DevInfo& di, const MatvecArgs& a, cudaStream_t st) {
+  auto kern = matvec_kernel<kVec, kSmemX>;
+  const size_t smem = kSmemX ? ((static_cast<size_t>(a.K) * 4 + 15) & ~size_t(15)) : 0;
+  static std::atomic<size_t> opted{48 * 1024};
+  if (smem > opted.load(std::memory_order_relaxed)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMatvecSmemMax)) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return AKILI_E_LAUNCH;
+    }
+    opted.store(kMatvecSmemMax, std::memory_order_relaxed);
+  }
+  // Enough CTAs to fill every SM to its shared-memory limit, never more than
+  // one row per warp.
+  const int per_sm = kSmemX ? std::max(1, std::min(8, static_cast<int>((227 * 1024) / (smem + 1024)))) : 8;
+  const int warps = kMatvecThreads / 32;
+  const int need = (a.rows + warps - 1) / warps;
+  const int blocks = std::max(1, std::min(need, di.sms * per_sm));
+  kern<<<blocks, kMatvecThreads, smem, st>>>(a);
+  return launch_status();
+}
+
+int launch_matvec(const DevInfo& di, const MatvecArgs& a, bool vec, cudaStream_t st) {
+  const bool smem = static_cast<size_t>(a.K) * 4 <= kMatvecSmemMax;
+  // without staging, x is read as float4s in place
+  if (!smem && reinterpret_cast<uintptr_t>(a.x) % 16) vec = false;
+  if (vec) return smem ? launch_matvec_t<true, true>(di, a, st) : launch_matvec_t<true, false>(di, a, st);
+  return smem ? launch_matvec_t<false, true>(di, a, st) : launch_matvec_t<false, false>(di, a, st);
+}
+
+int check_f32_ptr(uint64_t p) {
+  if (p == 0) return AKILI_E_NULL_ARG;
+  return (p % 4) ? AKILI_E_ALIGN : AKILI_OK;
+}
+
 }  // namespace
 
 // ===================================================================== ABI ==
@@ -1197,6 +1241,87 @@ int akili_attention(const attention_arg_t* a, akili_stream_t s) {
     attention_matmul_kernel<<<grid, dim3(kAtTile, 8), 0, st>>>(A, B, C, M, Nc, K);
   }
   return launch_status();
+}
+
+int akili_llama2_matmul(const matmul_kernel_args_t* a, akili_stream_t s) {
+  if (!a) return AKILI_E_NULL_ARG;
+  if (a->M < 0 || a->N < 0 || a->K < 0) return AKILI_E_SHAPE;
+  if (a->M == 0 || a->N == 0) return AKILI_OK;
+  int rc;
+  if ((rc = check_f32_ptr(a->C_addr))) return rc;
+  if (a->K > 0 && ((rc = check_f32_ptr(a->A_addr)) || (rc = check_f32_ptr(a->B_addr)))) return rc;
+  DevInfo di;
+  if ((rc = device_info(&di))) return rc;
+  cudaStream_t st = S(s);
+  const int M = a->M, N = a->N, K = a->K;
+  float* C = reinterpret_cast<float*>(static_cast<uintptr_t>(a->C_addr));
+  if (K == 0) {  // an empty sum: the reference kernel stores 0.0f
+    if (cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 4, st) != cudaSuccess) {
+      cudaGetLastError();
+      return AKILI_E_LAUNCH;
+    }
+    return AKILI_OK;
+  }
+  if (N == 1) {
+    MatvecArgs m{};
+    m.seg[0] = MatvecSeg{F(a->A_addr), C, M, 0};
+    m.nseg = 1;
+    m.rows = M;
+    m.K = K;
+    m.x = F(a->B_addr);
+    return launch_matvec(di, m, K % 4 == 0 && a->A_addr % 16 == 0, st);
+  }
+  if (M % 8 == 0 && N % 8 == 0 && K % 8 == 0 && a->A_addr % 16 == 0 && a->B_addr % 16 == 0 && a->C_addr % 16 == 0) {
+    GemmJob j;
+    j.epi = Epi::kPlain;
+    j.split = true;
+    j.M = M; j.N = N; j.K = K;
+    j.A = P(a->A_addr); j.B0 = P(a->B_addr); j.C = W(a->C_addr);
+    Mode md;
+    return run_job(j, md, st);
+  }
+  const dim3 grid((N + kAtTile - 1) / kAtTile, (M + kAtTile - 1) / kAtTile);
+  if (grid.y > 65535u) return AKILI_E_SHAPE;
+  attention_matmul_kernel<<<grid, dim3(kAtTile, 8), 0, st>>>(F(a->A_addr), F(a->B_addr), C, M, N, K);
+  return launch_status();
+}
+
+int akili_llama2_matvec_batch(const akili_matvec_seg_t* segs, int nseg, uint64_t x_addr, int32_t K,
+                              akili_stream_t s) {
+  if (!segs) return AKILI_E_NULL_ARG;
+  if (nseg < 1 || nseg > kMatvecMaxSegs) return AKILI_E_UNSUPPORTED;
+  if (K < 0) return AKILI_E_SHAPE;
+  int rc;
+  MatvecArgs m{};
+  int64_t rows = 0;
+  bool vec = K % 4 == 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (segs[i].rows < 0) return AKILI_E_SHAPE;
+    if (segs[i].rows == 0) continue;
+    if ((rc = check_f32_ptr(segs[i].C_addr)) || (K > 0 && (rc = check_f32_ptr(segs[i].W_addr)))) return rc;
+    vec = vec && segs[i].W_addr % 16 == 0;
+    m.seg[m.nseg++] = MatvecSeg{F(segs[i].W_addr), reinterpret_cast<float*>(static_cast<uintptr_t>(segs[i].C_addr)),
+                                segs[i].rows, static_cast<int>(rows)};
+    rows += segs[i].rows;
+  }
+  if (rows > INT32_MAX) return AKILI_E_SHAPE;
+  if (rows == 0) return AKILI_OK;
+  if (K > 0 && (rc = check_f32_ptr(x_addr))) return rc;
+  DevInfo di;
+  if ((rc = device_info(&di))) return rc;
+  cudaStream_t st = S(s);
+  if (K == 0) {
+    for (int i = 0; i < m.nseg; ++i)
+      if (cudaMemsetAsync(m.seg[i].C, 0, static_cast<size_t>(m.seg[i].rows) * 4, st) != cudaSuccess) {
+        cudaGetLastError();
+        return AKILI_E_LAUNCH;
+      }
+    return AKILI_OK;
+  }
+  m.rows = static_cast<int>(rows);
+  m.K = K;
+  m.x = F(x_addr);
+  return launch_matvec(di, m, vec, st);
 }
 
 int akili_flash_ml_ex(const flash_arg_t* a, const akili_ex_t* ex, uint64_t m_addr, uint64_t l_addr,

@@ -92,6 +92,9 @@ int dispatch(const std::string& op, const void* a) {
   AKILI_DISPATCH(kb2_gemm_rmsnorm_swiglu, kb2_gemm_rmsnorm_swiglu_arg_t)
   AKILI_DISPATCH(kb2_gemm_silu_mul, kb2_gemm_silu_mul_arg_t)
 #undef AKILI_DISPATCH
+  // benchmarks/llama2 builds its harness as "llama" (llama2/Makefile:4); its
+  // one kernel is the fp32 matmul of llama2/matmul_kernel.cpp.
+  if (op == "llama" || op == "llama2_matmul") return akili_llama2_matmul(static_cast<const matmul_kernel_args_t*>(a), nullptr);
   std::fprintf(stderr, "akili vortex shim: no akili op named '%s'\n", op.c_str());
   return AKILI_E_UNSUPPORTED;
 }
@@ -196,8 +199,18 @@ int vx_start(vx_device_h hdevice, vx_buffer_h hkernel, vx_buffer_h harguments) {
   auto* d = static_cast<Dev*>(hdevice);
   auto* k = static_cast<Buf*>(hkernel);
   auto* a = static_cast<Buf*>(harguments);
-  if (!d || !k || !a || a->host.empty()) return -1;
-  d->last_rc = dispatch(k->op, a->host.data());
+  if (!d || !k || !a) return -1;
+  // The argument block comes from vx_upload_bytes (the kbt harnesses) or
+  // is a device buffer written by vx_copy_to_dev (llama2/vxmath.cpp:127-135).
+  if (a->host.empty() && a->dptr && a->size > 0) {
+    a->host.resize(a->size);
+    if (cudaMemcpy(a->host.data(), a->dptr, a->size, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    d->last_rc = dispatch(k->op, a->host.data());
+    a->host.clear();
+  } else {
+    if (a->host.empty()) return -1;
+    d->last_rc = dispatch(k->op, a->host.data());
+  }
   if (d->last_rc != AKILI_OK)
     std::fprintf(stderr, "akili_%s: %s\n", k->op.c_str(), akili_strerror(d->last_rc));
   return d->last_rc == AKILI_OK ? 0 : -1;

@@ -235,6 +235,40 @@ def kb2_gemm_add_relu(a, w, bias, out=None, stream=None):
     return c
 
 
+def llama2_matmul(a, b, out=None, stream=None):
+    """The llama2 matmul offload (benchmarks/llama2/matmul_kernel.cpp):
+    out[M, N] = a[M, K] . b[K, N], fp32.  b may be a vector [K] (N = 1, the
+    matrix-vector product every llama2 call makes); out then is [M]."""
+    M, K = a.shape
+    vec = b.dim() == 1
+    N = 1 if vec else b.shape[1]
+    c = out if out is not None else torch.empty((M,) if vec else (M, N), device=a.device, dtype=torch.float32)
+    arg = abi.MatmulKernelArgs()
+    arg.block_dim[0], arg.block_dim[1] = 4, 1 if N == 1 else 4
+    arg.grid_dim[0], arg.grid_dim[1] = (M + 3) // 4, (N + arg.block_dim[1] - 1) // arg.block_dim[1]
+    arg.A_addr, arg.B_addr, arg.C_addr = _addr(a), _addr(b), _addr(c)
+    arg.M, arg.N, arg.K = M, N, K
+    rc = abi.load().akili_llama2_matmul(C.byref(arg), C.c_void_p(_stream(stream)))
+    if rc != abi.OK:
+        raise abi.AkiliError("llama2_matmul", rc)
+    return c
+
+
+def llama2_matvec_batch(ws, x, outs=None, stream=None):
+    """One launch of C_s = W_s . x for up to four weight matrices W_s [rows_s, K]
+    (the batched QKV / FFN products of benchmarks/llama2/vxmath.cpp)."""
+    K = x.shape[0]
+    outs = outs if outs is not None else [torch.empty(w.shape[0], device=x.device, dtype=torch.float32) for w in ws]
+    segs = (abi.MatvecSeg * len(ws))()
+    for i, (w, o) in enumerate(zip(ws, outs)):
+        assert w.shape[1] == K
+        segs[i].W_addr, segs[i].C_addr, segs[i].rows = _addr(w), _addr(o), w.shape[0]
+    rc = abi.load().akili_llama2_matvec_batch(segs, len(ws), _addr(x), K, C.c_void_p(_stream(stream)))
+    if rc != abi.OK:
+        raise abi.AkiliError("llama2_matvec_batch", rc)
+    return outs
+
+
 def launch_count() -> int:
     return int(abi.load().akili_launch_count())
 

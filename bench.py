@@ -67,9 +67,17 @@ class Workload:
     """One op at one shape: device inputs, the call, its algorithmic work."""
 
     def __init__(self, name, desc, flops, make, call, bound="tensor", io_bytes=None, host=None, cpu=None,
-                 kernel="gemm_kernel"):
+                 kernel="gemm_kernel", metric=None, unit="TFLOP/s", scale=1e12, dtype="f16", graph=False,
+                 e2e_host=None, e2e_step=None, cpu_fn=None):
         self.name, self.desc, self.flops, self.make, self.call = name, desc, flops, make, call
         self.bound, self.io_bytes, self.host, self.cpu, self.kernel = bound, io_bytes, host, cpu, kernel
+        # `flops` is the work of one step in `unit` * `scale` (FLOPs for TFLOP/s, 1 token for tok/s)
+        self.metric, self.unit, self.scale, self.dtype = metric or METRIC, unit, scale, dtype
+        # graph: time replays of one step captured as a CUDA graph (launch-bound sequences)
+        # e2e_host(d) -> pinned host buffers; e2e_step(d, host, stream) -> (h2d, d2h): one
+        # end-to-end step through the public API
+        # cpu_fn(d) -> cpu_baseline dict
+        self.graph, self.e2e_host, self.e2e_step, self.cpu_fn = graph, e2e_host, e2e_step, cpu_fn
 
 
 class Gens:
@@ -191,7 +199,109 @@ def workloads(torch, ops):
         lambda d, out, st: ops.flash(d["q"], d["k"], d["v"], softmax_scale=D ** -0.5, out=out, stream=st,
                                      causal=True),
         kernel="flash_fwd_kernel")
+
+    for key, shape in LLAMA2_SHAPES.items():
+        W[key] = llama2_workload(torch, ops, key, *shape)
     return W
+
+
+# llama2 decode (benchmarks/llama2/llama.cpp:246-407): per token, per layer the
+# batched QKV product, wo, the batched FFN w1/w3 product and w2, then the
+# classifier; each a matrix-vector product over fp32 weights resident in HBM.
+# (dim, hidden_dim, n_layers, kv_dim, vocab_size)
+LLAMA2_SHAPES = {
+    "llama2_7b_decode": (4096, 11008, 32, 4096, 32000),
+    "llama2_stories15m_decode": (288, 768, 6, 288, 32000),  # the reference's model (llama2/Makefile:9)
+}
+
+
+def llama2_calls(dim, hidden, layers, kv_dim, vocab):
+    """The offload calls of one token: (rows of each batched matrix, K)."""
+    calls = []
+    for _ in range(layers):
+        calls += [((dim, kv_dim, kv_dim), dim), ((dim,), dim), ((hidden, hidden), dim), ((dim,), hidden)]
+    return calls + [((vocab,), dim)]
+
+
+def llama2_workload(torch, ops, key, dim, hidden, layers, kv_dim, vocab):
+    import ctypes as C
+
+    from akili_bench_b200 import abi
+    calls = llama2_calls(dim, hidden, layers, kv_dim, vocab)
+    n_w = sum(r * K for rows, K in calls for r in rows)
+    n_out = sum(r for rows, _ in calls for r in rows)
+    n_in = sum(K for _, K in calls)
+
+    def make(gen):
+        d = {"x": {K: _rand(torch, gen.x, (K,)) for K in (dim, hidden)}, "calls": []}
+        for rows, K in calls:
+            ws = [_rand(torch, gen.w, (r, K), K ** -0.5) for r in rows]
+            outs = [torch.empty(r, device="cuda", dtype=torch.float32) for r in rows]
+            segs = (abi.MatvecSeg * len(rows))()
+            for i, (w, o) in enumerate(zip(ws, outs)):
+                segs[i].W_addr, segs[i].C_addr, segs[i].rows = w.data_ptr(), o.data_ptr(), w.shape[0]
+            d["calls"].append((segs, len(rows), K, ws, outs))
+        return d
+
+    def call(d, out, st):
+        L = abi.load()
+        s = C.c_void_p(int((st or torch.cuda.current_stream()).cuda_stream))
+        for segs, n, K, _, _ in d["calls"]:
+            rc = L.akili_llama2_matvec_batch(segs, n, d["x"][K].data_ptr(), K, s)
+            if rc != abi.OK:
+                raise abi.AkiliError("llama2_matvec_batch", rc)
+        return d["calls"][-1][4][0]  # the logits
+
+    def e2e_step(d, host, st):
+        """The vxmath API's contract per call (llama2/vxmath.cpp:82-145): the
+        activation comes from host memory, the product goes back to host
+        memory, and the call returns once it is there."""
+        L = abi.load()
+        s = C.c_void_p(int(st.cuda_stream))
+        h2d = d2h = 0
+        for i, (segs, n, K, _, outs) in enumerate(d["calls"]):
+            x = d["x"][K]
+            x.copy_(host["x"][K], non_blocking=True)
+            rc = L.akili_llama2_matvec_batch(segs, n, x.data_ptr(), K, s)
+            if rc != abi.OK:
+                raise abi.AkiliError("llama2_matvec_batch", rc)
+            for o, h in zip(outs, host["y"][i]):
+                h.copy_(o, non_blocking=True)
+            st.synchronize()
+            h2d += 4 * K
+            d2h += 4 * sum(o.numel() for o in outs)
+        return h2d, d2h
+
+    def e2e_host(d):
+        return {"x": {K: v.cpu().pin_memory() for K, v in d["x"].items()},
+                "y": [[torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in c[4]] for c in d["calls"]]}
+
+    def cpu_fn(d):
+        """The reference's CPU matmul (llama2/llama.cpp:236-243, restated by the
+        oracle) on the first layer's QKV rows, scaled to one token."""
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle_py
+        threads = host_threads()
+        w = d["calls"][0][3][0].cpu().numpy()
+        x = d["x"][dim].cpu().numpy().reshape(dim, 1)
+        rows = min(w.shape[0], max(threads * 64, 256))
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 or reps == 0:
+            oracle_py.llama2_matmul(np.ascontiguousarray(w[:rows]), x, rows, 1, dim, threads=threads)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        tok_s = (rows * dim / dt) / n_w
+        return {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": f"{rows} rows x K={dim} of layer 0's Wq, {reps} repetitions over {threads} threads, "
+                          f"scaled by multiply-adds to one token ({n_w / 1e6:.0f} M); oracle restating "
+                          "llama2/llama.cpp:236-243"}
+
+    return Workload(
+        key, {"dim": dim, "hidden_dim": hidden, "n_layers": layers, "kv_dim": kv_dim, "vocab": vocab,
+              "calls_per_token": len(calls), "weights_GB": round(4 * n_w / 1e9, 3)},
+        1.0, make, call, bound="hbm", io_bytes=4.0 * (n_w + n_out + n_in), kernel="matvec_kernel",
+        metric="llama2 decode matmul offload tokens/s (fp32 weights resident in HBM)", unit="tok/s", scale=1.0,
+        dtype="f32", graph=True, e2e_host=e2e_host, e2e_step=e2e_step, cpu_fn=cpu_fn)
 
 
 # ------------------------------------------------------------------- clocks --
@@ -333,9 +443,28 @@ def run_ours(args):
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
         flush = torch.empty(2 * L2_BYTES // 4, device="cuda", dtype=torch.float32)
+        graph = None
+        if wl.graph:
+            # A launch-bound step (many short kernels) is timed as replays of
+            # its launches captured once in a CUDA graph.
+            l0 = ops.launch_count()
+            wl.call(d, out, stream)
+            torch.cuda.synchronize()
+            launches_per_step = ops.launch_count() - l0
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                wl.call(d, out, torch.cuda.current_stream())
+            torch.cuda.synchronize()
+
+        def step():
+            if graph is not None:
+                graph.replay()
+            else:
+                wl.call(d, out, stream)
+
         for _ in range(args.warmup):
             flush.zero_()
-            wl.call(d, out, stream)
+            step()
         torch.cuda.synchronize()
         barrier()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -345,7 +474,7 @@ def run_ours(args):
             t_end = time.perf_counter() + seconds
             while time.perf_counter() < t_end:
                 for _ in range(8):
-                    wl.call(d, out, stream)
+                    step()
                 torch.cuda.synchronize()
 
         try:
@@ -360,10 +489,10 @@ def run_ours(args):
             for i in range(args.steps):
                 flush.zero_()
                 starts[i].record(stream)
-                wl.call(d, out, stream)
+                step()
                 ends[i].record(stream)
             torch.cuda.synchronize()
-            launches = ops.launch_count() - l0
+            launches = ops.launch_count() - l0 if graph is None else launches_per_step * args.steps
             barrier()
             soak(args.soak / 2)
         per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -372,40 +501,68 @@ def run_ours(args):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         max_ms = float(t.item())
-        value = wl.flops * world * args.steps / (max_ms * 1e-3) / 1e12
+        value = wl.flops * world * args.steps / (max_ms * 1e-3) / wl.scale
         status = ops.device_status()
+        del graph
 
         # --- end to end through the public API with host buffers (pinned) ---
-        host = {k: v.cpu().pin_memory() for k, v in d.items()}
-        host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-        d2 = {k: torch.empty_like(v) for k, v in d.items()}
-        h2d = sum(v.numel() * v.element_size() for v in host.values())
-        d2h = out.numel() * out.element_size()
         e_s = torch.cuda.Event(enable_timing=True)
         e_e = torch.cuda.Event(enable_timing=True)
-        for _ in range(max(1, args.warmup // 2)):
-            for k in d2:
-                d2[k].copy_(host[k], non_blocking=True)
-            o2 = wl.call(d2, out, stream)
-            host_out.copy_(o2, non_blocking=True)
-        torch.cuda.synchronize()
-        barrier()
-        e_s.record(stream)
-        for _ in range(args.steps):
-            for k in d2:
-                d2[k].copy_(host[k], non_blocking=True)
-            o2 = wl.call(d2, out, stream)
-            host_out.copy_(o2, non_blocking=True)
-        e_e.record(stream)
-        torch.cuda.synchronize()
+        if wl.e2e_step is not None:
+            host = wl.e2e_host(d)
+            for _ in range(max(1, args.warmup // 2)):
+                wl.e2e_step(d, host, stream)
+            torch.cuda.synchronize()
+            barrier()
+            e_s.record(stream)
+            for _ in range(args.steps):
+                h2d, d2h = wl.e2e_step(d, host, stream)
+            e_e.record(stream)
+            torch.cuda.synchronize()
+            del host
+        else:
+            host = {k: v.cpu().pin_memory() for k, v in d.items()}
+            host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+            d2 = {k: torch.empty_like(v) for k, v in d.items()}
+            h2d = sum(v.numel() * v.element_size() for v in host.values())
+            d2h = out.numel() * out.element_size()
+            for _ in range(max(1, args.warmup // 2)):
+                for k in d2:
+                    d2[k].copy_(host[k], non_blocking=True)
+                o2 = wl.call(d2, out, stream)
+                host_out.copy_(o2, non_blocking=True)
+            torch.cuda.synchronize()
+            barrier()
+            e_s.record(stream)
+            for _ in range(args.steps):
+                for k in d2:
+                    d2[k].copy_(host[k], non_blocking=True)
+                o2 = wl.call(d2, out, stream)
+                host_out.copy_(o2, non_blocking=True)
+            e_e.record(stream)
+            torch.cuda.synchronize()
         e2e_ms = e_s.elapsed_time(e_e)
         t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_value = wl.flops * world * args.steps / (float(t.item()) * 1e-3) / 1e12
+        e2e_value = wl.flops * world * args.steps / (float(t.item()) * 1e-3) / wl.scale
 
         # --- verification: sampled rows all-gathered to rank 0, checked against the oracle ---
         check = None
+        if name.startswith("llama2") and rank == 0:
+            # the classifier product of the last step against the oracle, sampled rows
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle_py
+            _, _, K, ws, outs = d["calls"][-1]
+            rows = np.linspace(0, ws[0].shape[0] - 1, 256).astype(np.int64)
+            a = ws[0][torch.from_numpy(rows).cuda()].cpu().numpy()
+            x = d["x"][K].cpu().numpy().reshape(K, 1)
+            ref = oracle_py.llama2_matmul(a, x, len(rows), 1, K)[:, 0]
+            got = outs[0][torch.from_numpy(rows).cuda()].cpu().numpy()
+            lim = 4e-6 * K ** 0.5 * (np.abs(a) @ np.abs(x))[:, 0]
+            err = np.abs(got.astype(np.float64) - ref)
+            check = {"rows_checked": len(rows), "ok": bool((err <= lim).all()),
+                     "max_err_frac": float(err.max() / np.abs(ref).max()), "gather": "local"}
         if name == "kbt_gemm_add_relu":
             sample = torch.tensor(shard.sample_rows(out.shape[0]), device="cuda")
             outs, ins = shard.gather_rows([out.index_select(0, sample).float(),
@@ -439,16 +596,18 @@ def run_ours(args):
         roof["traffic"] = NCU_TRAFFIC.get(name)
         roof["kernel"] = wl.kernel if wl.kernel != "gemm_kernel" or wl.desc.get("M", 0) <= 128 else "gemm_pair_kernel"
 
-        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
                 "config": {"workload": f"{name} " + " ".join(f"{k}={v}" for k, v in wl.desc.items()) + " per GPU",
                            "global_rows": (wl.desc.get("M", 0) * world) if "M" in wl.desc else None,
-                           "parallelism": f"rows sharded over {world} GPU(s), no collective in the timed loop",
+                           "parallelism": (f"{world} independent replica(s), one token stream per GPU"
+                                           if name.startswith("llama2") else
+                                           f"rows sharded over {world} GPU(s), no collective in the timed loop"),
                            "l2": "flushed (512 MB write) before every timed step, outside the events",
                            "inputs": "seeded synthetic, distributions of the configured workload"},
                 "roofline": roof,
-                "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+                "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
                         "d2h_bytes_per_step": int(d2h)},
                 "gpu_launches": int(launches),
                 "device_status": status,
@@ -469,6 +628,8 @@ def run_ours(args):
                 line["cpu_baseline"] = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                                         "sample": f"{rows} of 8192 rows ({dt:.1f} s), rows split over {threads} "
                                                   "threads; oracle restating kbt_gemm_add_relu/main.cpp:124-129"}
+            elif world == 1 and not args.no_cpu and W[name].cpu_fn is not None:
+                line["cpu_baseline"] = W[name].cpu_fn(d)
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

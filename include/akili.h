@@ -188,6 +188,31 @@ typedef struct {
   uint32_t kernel_id;
 } attention_arg_t;
 
+/* benchmarks/llama2/common.h:3-12 — the llama2 matmul offload:
+ * C[M x N] = A[M x K] . B[K x N], fp32, row-major.  The caller
+ * (llama2/vxmath.cpp:82-212) passes the weight matrix as A and the
+ * activation vector as B with N = 1 (llama2/llama.cpp:225-233). */
+typedef struct {
+  uint32_t grid_dim[2];
+  uint32_t block_dim[2];
+  uint64_t A_addr;
+  uint64_t B_addr;
+  uint64_t C_addr;
+  int32_t M;
+  int32_t N;
+  int32_t K;
+} matmul_kernel_args_t;
+
+/* One segment of a batched matrix-vector product: C[rows] = W[rows x K] . x.
+ * The batch replaces the reference's concatenate-then-multiply
+ * (llama2/vxmath.cpp:148-221) without copying the weights. */
+typedef struct {
+  uint64_t W_addr;
+  uint64_t C_addr;
+  int32_t rows;
+  int32_t reserved;
+} akili_matvec_seg_t;
+
 /* ---- the kb2_* SIMT family: fp32 operands, fp32 arithmetic --------------
  * benchmarks/kb2_<bench>/common.h: the same ops without the Vortex launch
  * fields.  Their plain entries keep fp32 semantics (no fp16 rounding of the
@@ -348,6 +373,20 @@ int akili_flash_ml_ex(const flash_arg_t* arg, const akili_ex_t* ex, uint64_t m_a
  * fp32 CUDA-core arithmetic (S and O summed in the reference's order). */
 int akili_attention(const attention_arg_t* arg, akili_stream_t stream);
 
+/* llama2/vxmath.cpp:82-141 (vx_matmul_optimized: one vx_start of
+ * llama2/matmul_kernel.cpp:4-24 per call): C = A.B in fp32.  N = 1 runs an
+ * HBM-bound matrix-vector kernel; N > 1 with M, N, K multiples of 8 and
+ * 16-byte aligned pointers runs the tensor-core GEMM in split precision
+ * (fp32-level accuracy); other shapes run a tiled fp32 CUDA-core kernel.
+ * Pointers need 4-byte alignment; M, N or K may be 0 (K = 0 writes zeros). */
+int akili_llama2_matmul(const matmul_kernel_args_t* arg, akili_stream_t stream);
+
+/* The batched products of llama2/vxmath.cpp:143-221 (QKV, FFN w1/w3) as one
+ * launch: for each of the nseg (1..4) segments, C_s = W_s . x, W_s row-major
+ * [rows_s x K], x and C_s fp32 device vectors. */
+int akili_llama2_matvec_batch(const akili_matvec_seg_t* segs, int nseg, uint64_t x_addr, int32_t K,
+                              akili_stream_t stream);
+
 /* kb2_* entries: each replaces the vx_upload_bytes + vx_start +
  * vx_ready_wait sequence of benchmarks/kb2_<bench>/main.cpp.  fp32 buffers,
  * fp32 results (see the kb2 structs above); the `_ex` form takes an
@@ -437,6 +476,11 @@ AKILI_CHECK_LAYOUT(attention_arg_t, 72);
 static_assert(offsetof(attention_arg_t, N) == 8 && offsetof(attention_arg_t, Q_addr) == 16 &&
               offsetof(attention_arg_t, O_addr) == 56 && offsetof(attention_arg_t, kernel_id) == 64,
               "attention offsets");
+AKILI_CHECK_LAYOUT(matmul_kernel_args_t, 56);
+static_assert(offsetof(matmul_kernel_args_t, A_addr) == 16 && offsetof(matmul_kernel_args_t, C_addr) == 32 &&
+              offsetof(matmul_kernel_args_t, M) == 40 && offsetof(matmul_kernel_args_t, K) == 48,
+              "matmul_kernel_args_t offsets");
+AKILI_CHECK_LAYOUT(akili_matvec_seg_t, 24);
 AKILI_CHECK_LAYOUT(kb2_gemm_add_relu_arg_t, 48);
 AKILI_CHECK_LAYOUT(kb2_gemm_mul_leakyrelu_arg_t, 56);
 AKILI_CHECK_LAYOUT(kb2_gemm_div_sum_scale_arg_t, 40);

@@ -15,6 +15,16 @@ TEST INFRASTRUCTURE.  Outputs:
   against the product's ``libakili_vortex.so`` (the Vortex runtime API on
   top of the akili_* C ABI): the reference harness driving the B200 kernels
   and judging them with its own gold check.
+* llama2 (``benchmarks/llama2``: the reference's ``llama.cpp`` and its
+  matmul offload ``vxmath.cpp``, unchanged):
+  ``oracle/_ref/pin/llama`` and ``oracle/_ref/pin/llama2_logits`` over the
+  host-memory device (``-v 0`` is the reference's CPU matmul, ``-v 1`` its
+  vxmath.cpp driving the oracle); ``oracle/_ref/b200/llama`` and
+  ``.../llama2_logits`` with vxmath.cpp over ``libakili_vortex.so``;
+  ``oracle/_ref/b200/llama_vxmath`` and ``.../llama2_logits_vxmath`` with
+  the product's ``libakili_vxmath.so`` in place of vxmath.cpp.
+  ``llama2_logits`` is ``oracle/llama2/llama2_logits.cpp``, a driver that
+  compiles llama.cpp with TESTING and writes each position's logits.
 
 The reference sources are read in place (``--ref``, default
 /root/reference); nothing is copied.  ``oracle/_ref/`` is git-ignored and
@@ -129,6 +139,43 @@ def build_b200_binaries(ref_root: str, libdir: str, force: bool = False) -> list
     return built
 
 
+def build_llama2_binaries(ref_root: str, libdir: str, force: bool = False) -> list[str]:
+    """The reference llama2 program (and the logits driver) against the
+    host-memory device, the product's Vortex shim and its vxmath library."""
+    src_dir = os.path.join(ref_root, "benchmarks", "llama2")
+    llama = os.path.join(src_dir, "llama.cpp")
+    vxmath = os.path.join(src_dir, "vxmath.cpp")
+    driver = os.path.join(HERE, "llama2", "llama2_logits.cpp")
+    inc = ["-I", os.path.join(ROOT, "include"), "-I", src_dir]
+    flags = [*REF_CXXFLAGS, "-ffp-contract=off", "-w"]
+    built = []
+    pin_objs = [os.path.join(REF_OUT, "vortex_host.o"), os.path.join(REF_OUT, "oracle_pin.o")]
+    os.makedirs(os.path.join(REF_OUT, "pin"), exist_ok=True)
+    for name, main_src in (("llama", llama), ("llama2_logits", driver)):
+        out = os.path.join(REF_OUT, "pin", name)
+        deps = [main_src, llama, vxmath, *pin_objs]
+        if force or not _newer(out, deps):
+            _run(["g++", *flags, *inc, main_src, vxmath, *pin_objs, "-o", out, "-lm"])
+        built.append(out)
+    vortex_lib = os.path.join(libdir, "libakili_vortex.so")
+    vxmath_lib = os.path.join(libdir, "libakili_vxmath.so")
+    os.makedirs(os.path.join(REF_OUT, "b200"), exist_ok=True)
+    for name, main_src, extra, lib in (
+            ("llama", llama, [vxmath], "akili_vortex"),
+            ("llama2_logits", driver, [vxmath], "akili_vortex"),
+            ("llama_vxmath", llama, [], "akili_vxmath"),
+            ("llama2_logits_vxmath", driver, [], "akili_vxmath")):
+        libpath = vortex_lib if lib == "akili_vortex" else vxmath_lib
+        if not os.path.exists(libpath):
+            continue
+        out = os.path.join(REF_OUT, "b200", name)
+        if force or not _newer(out, [main_src, llama, *extra, libpath]):
+            _run(["g++", *flags, *inc, main_src, *extra, "-L", libdir, f"-l{lib}", f"-Wl,-rpath,{libdir}", "-o",
+                  out, "-lm"])
+        built.append(out)
+    return built
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--ref", default="/root/reference")
@@ -142,6 +189,8 @@ def main() -> int:
         if os.path.exists(os.path.join(a.libdir, "libakili_vortex.so")):
             for p in build_b200_binaries(a.ref, a.libdir, a.force):
                 print(p)
+        for p in build_llama2_binaries(a.ref, a.libdir, a.force):
+            print(p)
     else:
         print(f"reference tree {a.ref} absent: pin binaries not rebuilt", file=sys.stderr)
     return 0

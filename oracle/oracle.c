@@ -591,3 +591,19 @@ float oracle_round_f16(float x) {
 void oracle_round_f16_array(float* x, uint64_t n) {
   for (uint64_t i = 0; i < n; ++i) x[i] = oracle_round_f16(x[i]);
 }
+
+/* ---- benchmarks/llama2: the matmul offload (fp32) ---- */
+
+/* llama2/matmul_kernel.cpp:15-22, one thread per output: C[row, col] =
+ * sum over k in order of A[row, k] * B[k, col]; with N = 1 this is the
+ * CPU matmul of llama2/llama.cpp:236-243 (val += w[i*n + j] * x[j]). */
+void oracle_llama2_matmul(float* C, const float* A, const float* B, uint32_t M, uint32_t N, uint32_t K,
+                          uint32_t row0, uint32_t row1) {
+  (void)M;
+  for (uint32_t row = row0; row < row1; ++row)
+    for (uint32_t col = 0; col < N; ++col) {
+      float sum = 0.0f;
+      for (uint32_t k = 0; k < K; ++k) sum += A[(uint64_t)row * K + k] * B[(uint64_t)k * N + col];
+      C[(uint64_t)row * N + col] = sum;
+    }
+}

@@ -67,6 +67,9 @@ void oracle_flash_causal(float* out, float* m_out, float* l_out, const float* q,
 void oracle_attention_matmul(float* out, const float* A, const float* B, uint32_t M, uint32_t N, uint32_t K,
                              uint32_t row0, uint32_t row1);
 void oracle_attention_softmax(float* out, const float* A, uint32_t M, uint32_t N, uint32_t row0, uint32_t row1);
+/* llama2 matmul offload: C[M x N] = A[M x K] . B[K x N], summed over k in order. */
+void oracle_llama2_matmul(float* C, const float* A, const float* B, uint32_t M, uint32_t N, uint32_t K,
+                          uint32_t row0, uint32_t row1);
 void oracle_kb2_gemm_add_relu(const float* a, const float* w, const float* bias, float* c, uint32_t M,
                               uint32_t N, uint32_t K, uint32_t row0, uint32_t row1);
 void oracle_kb2_gemm_mul_leakyrelu(const float* a, const float* w, const float* bias, float* c, uint32_t M,

@@ -48,6 +48,7 @@ _SIGS = {
     "oracle_kb2_gemm_silu_mul": [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_attention_matmul": [_f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_attention_softmax": [_f32p, _f32p, _u32, _u32, _u32, _u32],
+    "oracle_llama2_matmul": [_f32p, _f32p, _f32p, _u32, _u32, _u32, _u32, _u32],
     "oracle_round_f16_array": [_f32p, C.c_uint64],
 }
 
@@ -306,4 +307,14 @@ def attention_softmax(a, M, N, row0=0, row1=None, threads=1):
     row1 = M if row1 is None else row1
     c = np.zeros((M, N), np.float32)
     _rows(lib().oracle_attention_softmax, (_p(c), _p(a)), (M, N), row0, row1, threads)
+    return c
+
+
+# ---- benchmarks/llama2 (matmul offload, fp32) ----
+
+def llama2_matmul(a, b, M, N, K, row0=0, row1=None, threads=1):
+    """C[M x N] = A[M x K] . B[K x N] (llama2/matmul_kernel.cpp:15-22)."""
+    row1 = M if row1 is None else row1
+    c = np.zeros((M, N), np.float32)
+    _rows(lib().oracle_llama2_matmul, (_p(c), _p(a), _p(b)), (M, N, K), row0, row1, threads)
     return c

@@ -154,6 +154,9 @@ int run_oracle() {
       oracle_attention_softmax(fp(a->P_addr), fp(a->S_addr), a->N, a->N, 0, a->N);
     else
       oracle_attention_matmul(fp(a->O_addr), fp(a->P_addr), fp(a->V_addr), a->N, a->d, a->N, 0, a->N);
+  } else if (op == "llama" || op == "llama2_matmul") {
+    auto a = as<matmul_kernel_args_t>(g_args);
+    oracle_llama2_matmul(fp(a->C_addr), fp(a->A_addr), fp(a->B_addr), a->M, a->N, a->K, 0, a->M);
   } else if (op == "flash") {
     auto a = as<flash_arg_t>(g_args);
     oracle_flash(fp(a->O_addr), fp(a->Q_addr), fp(a->K_addr), fp(a->V_addr), a->seq_len,
@@ -275,7 +278,11 @@ int vx_upload_bytes(vx_device_h, const void* content, uint64_t size, vx_buffer_h
   *hbuffer = b;
   return 0;
 }
-int vx_start(vx_device_h, vx_buffer_h, vx_buffer_h) {
+int vx_start(vx_device_h, vx_buffer_h, vx_buffer_h harguments) {
+  /* the argument block is the buffer's bytes, whether it came from
+   * vx_upload_bytes (the kbt harnesses) or from vx_mem_alloc +
+   * vx_copy_to_dev (llama2/vxmath.cpp:127-135) */
+  if (harguments) g_args = static_cast<HostBuf*>(harguments)->bytes;
   const char* m = std::getenv("AKILI_HOST_DEVICE");
   if (m && std::strcmp(m, "zero") == 0) return 0;
   int rc = run_oracle();
@@ -287,6 +294,8 @@ int vx_start(vx_device_h, vx_buffer_h, vx_buffer_h) {
     } else if (g_op == "attention") {
       auto a = as<attention_arg_t>(g_args);
       out = a->kernel_id == 0 ? a->S_addr : (a->kernel_id == 1 ? a->P_addr : a->O_addr);
+    } else if (g_op == "llama" || g_op == "llama2_matmul") {
+      out = as<matmul_kernel_args_t>(g_args)->C_addr;
     } else {
       out = *reinterpret_cast<const uint64_t*>(g_args.data() + g_args.size() -
                                                8 * (g_op == "kbt_matmul_scale_residadd_clamp" ? 2 : 1));
