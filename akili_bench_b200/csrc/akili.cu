@@ -1117,9 +1117,14 @@ int launch_matvec_t(const DevInfo& di, const MatvecArgs& a, cudaStream_t st) {
     }
     opted.store(kMatvecSmemMax, std::memory_order_relaxed);
   }
-  // Enough CTAs to fill every SM to its shared-memory limit, never more than
-  // one row per warp.
-  const int per_sm = kSmemX ? std::max(1, std::min(8, static_cast<int>((227 * 1024) / (smem + 1024)))) : 8;
+  // One wave of persistent CTAs (as many as are resident at once, from the
+  // occupancy calculator), never more than one row group per CTA.
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kMatvecThreads, smem) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
   const int warps = kMatvecThreads / 32;
   const int need = (a.rows + warps - 1) / warps;
   const int blocks = std::max(1, std::min(need, di.sms * per_sm));

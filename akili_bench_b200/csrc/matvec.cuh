@@ -8,11 +8,14 @@
 // kernel is bound by HBM bandwidth (4 bytes of W per multiply-add).  Layout:
 //   * x (K floats) is staged once per CTA in shared memory;
 //   * one warp per output row; each lane streams float4s of the row
-//     (coalesced 512-byte warp loads, evict-first so the row does not push
-//     x or other rows out of L1), four loads in flight per lane;
-//   * the lane partials are added with a butterfly over the warp.
-// The rows of up to four segments (e.g. Wq, Wk, Wv of one layer) are one
-// index space, so a batched product is one launch with no weight copies.
+//     (coalesced 512-byte warp loads, evict-first so the weights do not push
+//     x out of L1), four loads in flight per lane;
+//   * the lane partials are added with a butterfly over the warp;
+//   * one wave of persistent CTAs, sized by the occupancy calculator (about
+//     62 registers a thread: four CTAs, 32 warps and 64 KB of reads in flight
+//     per SM).  A grid sized for more CTAs than fit ran as two waves at 0.76
+//     of HBM bandwidth, against 0.84 for one wave.  Splitting each row over 2
+//     to 8 warps (finer units for the last wave) measured slower.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -49,7 +52,7 @@ __global__ void __launch_bounds__(kMatvecThreads) matvec_kernel(const __grid_con
   }
   const float* xv = kSmemX ? xs : a.x;
   const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
+  const int warps = kMatvecThreads / 32;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < a.rows; row += gridDim.x * warps) {
     int s = 0;
 #pragma unroll

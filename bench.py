@@ -51,6 +51,9 @@ NCU_TRAFFIC = {
     # profiles/softmax_rows_kernel_kbt_attention_score_16384x4096x128.md: 5.5 MB read + 74.5 MB written
     # (part of the output is still in L2 when the kernel ends)
     "kbt_attention_score": 80.0e6,
+    # profiles/matvec_kernel_llama2_7b_qkv.md: the QKV launch read 207.33 MB (read + write) for
+    # 201.39 MB of algorithmic bytes; scaled by that ratio to one token's 26.43 GB
+    "llama2_7b_decode": 27.21e9,
 }
 
 
@@ -278,13 +281,14 @@ def llama2_workload(torch, ops, key, dim, hidden, layers, kv_dim, vocab):
 
     def cpu_fn(d):
         """The reference's CPU matmul (llama2/llama.cpp:236-243, restated by the
-        oracle) on the first layer's QKV rows, scaled to one token."""
+        oracle) on rows of the classifier, scaled to one token."""
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle_py
         threads = host_threads()
-        w = d["calls"][0][3][0].cpu().numpy()
+        wc = d["calls"][-1][3][0]
+        rows = min(wc.shape[0], max(threads * 64, (1 << 22) // dim))
+        w = wc[:rows].cpu().numpy()
         x = d["x"][dim].cpu().numpy().reshape(dim, 1)
-        rows = min(w.shape[0], max(threads * 64, 256))
         reps, t0 = 0, time.perf_counter()
         while time.perf_counter() - t0 < 10.0 or reps == 0:
             oracle_py.llama2_matmul(np.ascontiguousarray(w[:rows]), x, rows, 1, dim, threads=threads)
@@ -292,7 +296,7 @@ def llama2_workload(torch, ops, key, dim, hidden, layers, kv_dim, vocab):
         dt = (time.perf_counter() - t0) / reps
         tok_s = (rows * dim / dt) / n_w
         return {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
-                "sample": f"{rows} rows x K={dim} of layer 0's Wq, {reps} repetitions over {threads} threads, "
+                "sample": f"{rows} rows x K={dim} of the classifier, {reps} repetitions over {threads} threads, "
                           f"scaled by multiply-adds to one token ({n_w / 1e6:.0f} M); oracle restating "
                           "llama2/llama.cpp:236-243"}
 
@@ -654,9 +658,14 @@ def main():
                     help="seconds of untimed load before (and half after) the timed steps, for clock sampling")
     ap.add_argument("--flash-shape", type=int, nargs=4, metavar=("B", "H", "S", "D"), default=None,
                     help="flash workload shape (default: configs[4], 8 32 4096 128); smaller for profiling")
+    ap.add_argument("--llama2-layers", type=int, default=None,
+                    help="layers of the llama2 decode workloads (default: the model's); fewer for profiling")
     args = ap.parse_args()
     if args.flash_shape:
         FLASH_SHAPE[:] = args.flash_shape
+    if args.llama2_layers:
+        for k, v in LLAMA2_SHAPES.items():
+            LLAMA2_SHAPES[k] = (v[0], v[1], args.llama2_layers, v[3], v[4])
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

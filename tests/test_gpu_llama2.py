@@ -38,6 +38,7 @@ def bound(a, b, K):
     (288, 1, 288), (768, 1, 288), (288, 1, 768), (512, 1, 128), (4096, 1, 4096), (1000, 1, 11008),
     (33, 1, 7), (100, 1, 4), (3, 1, 1),            # matrix-vector, K % 4 != 0 and tiny
     (8, 1, 60000),                                 # x too large to stage in shared memory
+    (300, 1, 2048), (40, 1, 4099), (12, 1, 8),     # K % 4 != 0 at length, one short row
     (5, 3, 9), (100, 20, 30), (70, 2, 4096),       # N > 1, unaligned: CUDA-core tiles
     (64, 16, 128), (24, 40, 56), (256, 64, 4096),  # N > 1, aligned: tensor cores, split precision
 ])
