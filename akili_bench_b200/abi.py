@@ -210,6 +210,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
         fx.restype = C.c_int
     L.akili_attention.argtypes = [C.POINTER(AttentionArg), C.c_void_p]
     L.akili_attention.restype = C.c_int
+    L.akili_attention_ex.argtypes = [C.POINTER(AttentionArg), C.POINTER(AkiliEx), C.c_void_p]
+    L.akili_attention_ex.restype = C.c_int
     L.akili_llama2_matmul.argtypes = [C.POINTER(MatmulKernelArgs), C.c_void_p]
     L.akili_llama2_matmul.restype = C.c_int
     L.akili_llama2_matvec_batch.argtypes = [C.POINTER(MatvecSeg), C.c_int, C.c_uint64, C.c_int32, C.c_void_p]

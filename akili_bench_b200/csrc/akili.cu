@@ -1145,6 +1145,135 @@ int check_f32_ptr(uint64_t p) {
   return (p % 4) ? AKILI_E_ALIGN : AKILI_OK;
 }
 
+// ----------------------------------------------- unfused attention --
+// Per-head GEMMs of one launch stage run on kAttnStreams streams forked from
+// and joined back to the caller's stream (events; a CUDA graph captures them
+// as parallel branches): one head's P.V product (N = head_dim) fills only a
+// few CTA pairs.
+constexpr int kAttnStreams = 4;
+struct AttnStreams {
+  std::mutex mu;
+  bool ready = false;
+  cudaStream_t s[kAttnStreams] = {};
+  cudaEvent_t fork = nullptr, join[kAttnStreams] = {};
+};
+
+int attn_streams(AttnStreams** out) {
+  static AttnStreams per_dev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return AKILI_E_NO_DEVICE;
+  }
+  AttnStreams& a = per_dev[dev];
+  std::lock_guard<std::mutex> lk(a.mu);
+  if (!a.ready) {
+    bool ok = cudaEventCreateWithFlags(&a.fork, cudaEventDisableTiming) == cudaSuccess;
+    for (int i = 0; i < kAttnStreams && ok; ++i)
+      ok = cudaStreamCreateWithFlags(&a.s[i], cudaStreamNonBlocking) == cudaSuccess &&
+           cudaEventCreateWithFlags(&a.join[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+      cudaGetLastError();
+      return AKILI_E_LAUNCH;
+    }
+    a.ready = true;
+  }
+  *out = &a;
+  return AKILI_OK;
+}
+
+// One of the three launches of benchmarks/attention (kernel_id 0: S = Q.K
+// with K stored d x N, 1: P = softmax(scale * S) by rows, 2: O = P.V) for
+// each of batch*heads heads stored one after another.  fp32 buffers run the
+// reference's exact fp32 CUDA-core kernels head by head; fp16 buffers run
+// the two products on the tensor-core GEMM and the softmax as one HBM pass
+// over all heads' rows, with S and P materialised in between.
+int attention_run(const attention_arg_t* a, const Mode& md, cudaStream_t st) {
+  if (!a) return AKILI_E_NULL_ARG;
+  if (a->N == 0 || a->d == 0) return AKILI_E_SHAPE;
+  if (a->kernel_id > 2) return AKILI_E_UNSUPPORTED;
+  if (md.causal) return AKILI_E_UNSUPPORTED;
+  if (md.in_f32 != md.out_f32) return AKILI_E_DTYPE;
+  int rc;
+  if (a->kernel_id == 0) rc = check_ptrs({a->Q_addr, a->K_addr, a->S_addr});
+  else if (a->kernel_id == 1) rc = check_ptrs({a->S_addr, a->P_addr});
+  else rc = check_ptrs({a->P_addr, a->V_addr, a->O_addr});
+  if (rc) return rc;
+  DevInfo di;
+  if ((rc = device_info(&di))) return rc;
+  const int N = static_cast<int>(a->N), d = static_cast<int>(a->d);
+  const size_t heads = static_cast<size_t>(md.batch) * md.heads;
+  const size_t nd = static_cast<size_t>(N) * d, nn = static_cast<size_t>(N) * N;
+  const size_t esz = md.in_f32 ? 4 : 2;
+  auto at = [&](uint64_t base, size_t elems) { return reinterpret_cast<char*>(static_cast<uintptr_t>(base)) + elems * esz; };
+  if (md.in_f32) {
+    for (size_t h = 0; h < heads; ++h) {
+      if (a->kernel_id == 1) {
+        attention_softmax_kernel<<<grid_for(di, N, 8, 8), 256, 0, st>>>(
+            reinterpret_cast<const float*>(at(a->S_addr, h * nn)), reinterpret_cast<float*>(at(a->P_addr, h * nn)),
+            N, N, md.scale);
+      } else {
+        const int M = N, Nc = a->kernel_id == 0 ? N : d, K = a->kernel_id == 0 ? d : N;
+        const float* A = reinterpret_cast<const float*>(a->kernel_id == 0 ? at(a->Q_addr, h * nd)
+                                                                          : at(a->P_addr, h * nn));
+        const float* B = reinterpret_cast<const float*>(a->kernel_id == 0 ? at(a->K_addr, h * nd)
+                                                                          : at(a->V_addr, h * nd));
+        float* C = reinterpret_cast<float*>(a->kernel_id == 0 ? at(a->S_addr, h * nn) : at(a->O_addr, h * nd));
+        dim3 grid((Nc + kAtTile - 1) / kAtTile, (M + kAtTile - 1) / kAtTile);
+        if (grid.y > 65535u) return AKILI_E_SHAPE;
+        attention_matmul_kernel<<<grid, dim3(kAtTile, 8), 0, st>>>(A, B, C, M, Nc, K);
+      }
+      if ((rc = launch_status())) return rc;
+    }
+    return AKILI_OK;
+  }
+  // fp16: the tensor-core GEMM needs 16-byte rows
+  if (N % 8 || d % 8) return AKILI_E_SHAPE;
+  if (a->kernel_id == 1) {
+    const size_t rows = heads * N;
+    attention_softmax_f16_kernel<<<grid_for(di, rows, 8, 16), 256, 0, st>>>(
+        reinterpret_cast<const __half*>(at(a->S_addr, 0)), reinterpret_cast<__half*>(at(a->P_addr, 0)), rows, N,
+        md.scale * 1.4426950408889634f);
+    return launch_status();
+  }
+  Mode gm;
+  gm.in_f32 = gm.out_f32 = false;
+  gm.workspace = md.workspace;
+  gm.workspace_bytes = md.workspace_bytes;
+  AttnStreams* ax = nullptr;
+  if ((rc = attn_streams(&ax))) return rc;
+  std::lock_guard<std::mutex> lk(ax->mu);
+  const int nst = heads > 1 ? kAttnStreams : 0;
+  if (nst) {
+    bool ok = cudaEventRecord(ax->fork, st) == cudaSuccess;
+    for (int i = 0; i < nst && ok; ++i) ok = cudaStreamWaitEvent(ax->s[i], ax->fork, 0) == cudaSuccess;
+    if (!ok) {
+      cudaGetLastError();
+      return AKILI_E_LAUNCH;
+    }
+  }
+  for (size_t h = 0; h < heads && rc == AKILI_OK; ++h) {
+    GemmJob j;
+    j.epi = Epi::kPlain;
+    if (a->kernel_id == 0) {  // S_h[N x N] = Q_h[N x d] . K_h[d x N]
+      j.M = N; j.N = N; j.K = d;
+      j.A = at(a->Q_addr, h * nd); j.B0 = at(a->K_addr, h * nd); j.C = at(a->S_addr, h * nn);
+    } else {                  // O_h[N x d] = P_h[N x N] . V_h[N x d]
+      j.M = N; j.N = d; j.K = N;
+      j.A = at(a->P_addr, h * nn); j.B0 = at(a->V_addr, h * nd); j.C = at(a->O_addr, h * nd);
+    }
+    rc = run_job(j, gm, nst ? ax->s[h % nst] : st);
+  }
+  // join every branch back, also after an error, so the caller's stream (or
+  // capture) is left consistent
+  for (int i = 0; i < nst; ++i)
+    if (cudaEventRecord(ax->join[i], ax->s[i]) != cudaSuccess || cudaStreamWaitEvent(st, ax->join[i], 0) != cudaSuccess) {
+      cudaGetLastError();
+      if (rc == AKILI_OK) rc = AKILI_E_LAUNCH;
+    }
+  return rc;
+}
+
 }  // namespace
 
 // ===================================================================== ABI ==
@@ -1221,31 +1350,14 @@ int akili_flash_ex(const flash_arg_t* a, const akili_ex_t* ex, akili_stream_t s)
 }
 int akili_flash(const flash_arg_t* a, akili_stream_t s) { return akili_flash_ex(a, nullptr, s); }
 
-int akili_attention(const attention_arg_t* a, akili_stream_t s) {
-  if (!a) return AKILI_E_NULL_ARG;
-  if (a->N == 0 || a->d == 0) return AKILI_E_SHAPE;
-  if (a->kernel_id > 2) return AKILI_E_UNSUPPORTED;
-  int rc;
-  if (a->kernel_id == 0) rc = check_ptrs({a->Q_addr, a->K_addr, a->S_addr});
-  else if (a->kernel_id == 1) rc = check_ptrs({a->S_addr, a->P_addr});
-  else rc = check_ptrs({a->P_addr, a->V_addr, a->O_addr});
+int akili_attention(const attention_arg_t* a, akili_stream_t s) { return attention_run(a, Mode{}, S(s)); }
+
+int akili_attention_ex(const attention_arg_t* a, const akili_ex_t* ex, akili_stream_t s) {
+  if (!ex) return AKILI_E_NULL_ARG;
+  Mode md;
+  const int rc = parse_ex(ex, &md);
   if (rc) return rc;
-  DevInfo di;
-  if ((rc = device_info(&di))) return rc;
-  const int N = static_cast<int>(a->N), d = static_cast<int>(a->d);
-  auto fp = [](uint64_t v) { return reinterpret_cast<float*>(static_cast<uintptr_t>(v)); };
-  cudaStream_t st = S(s);
-  if (a->kernel_id == 1) {
-    attention_softmax_kernel<<<grid_for(di, N, 8, 8), 256, 0, st>>>(fp(a->S_addr), fp(a->P_addr), N, N);
-  } else {
-    const int M = N, Nc = a->kernel_id == 0 ? N : d, K = a->kernel_id == 0 ? d : N;
-    const float* A = fp(a->kernel_id == 0 ? a->Q_addr : a->P_addr);
-    const float* B = fp(a->kernel_id == 0 ? a->K_addr : a->V_addr);
-    float* C = fp(a->kernel_id == 0 ? a->S_addr : a->O_addr);
-    dim3 grid((Nc + kAtTile - 1) / kAtTile, (M + kAtTile - 1) / kAtTile);
-    attention_matmul_kernel<<<grid, dim3(kAtTile, 8), 0, st>>>(A, B, C, M, Nc, K);
-  }
-  return launch_status();
+  return attention_run(a, md, S(s));
 }
 
 int akili_llama2_matmul(const matmul_kernel_args_t* a, akili_stream_t s) {

@@ -235,6 +235,35 @@ def kb2_gemm_add_relu(a, w, bias, out=None, stream=None):
     return c
 
 
+def attention_unfused(q, k_t, v, softmax_scale=None, s=None, p=None, out=None, stream=None, stages=(0, 1, 2)):
+    """The reference's unfused attention (benchmarks/attention/kernel.cpp:6-68)
+    over heads [B, H, N, d] (or one head [N, d]): S = Q.K with K stored
+    transposed (k_t [B, H, d, N]), P = softmax(softmax_scale * S) by rows,
+    O = P.V, each its own launch with S and P materialised.  fp32 tensors run
+    the exact fp32 kernels, fp16 tensors the tensor-core path.  Returns
+    (O, S, P)."""
+    if q.dim() == 2:
+        B, H, (N, d) = 1, 1, q.shape
+    else:
+        B, H, N, d = q.shape
+    lead = q.shape[:-2]
+    s = s if s is not None else torch.empty((*lead, N, N), device=q.device, dtype=q.dtype)
+    p = p if p is not None else torch.empty((*lead, N, N), device=q.device, dtype=q.dtype)
+    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    ex = abi.make_ex(_dt(q), _dt(o), batch=B, heads=H, softmax_scale=float(softmax_scale or 0.0))
+    arg = abi.AttentionArg()
+    arg.N, arg.d = N, d
+    arg.Q_addr, arg.K_addr, arg.S_addr = _addr(q), _addr(k_t), _addr(s)
+    arg.P_addr, arg.V_addr, arg.O_addr = _addr(p), _addr(v), _addr(o)
+    L = abi.load()
+    for kid in stages:
+        arg.kernel_id = kid
+        rc = L.akili_attention_ex(C.byref(arg), C.byref(ex), C.c_void_p(_stream(stream)))
+        if rc != abi.OK:
+            raise abi.AkiliError("attention_ex", rc)
+    return o, s, p
+
+
 def llama2_matmul(a, b, out=None, stream=None):
     """The llama2 matmul offload (benchmarks/llama2/matmul_kernel.cpp):
     out[M, N] = a[M, K] . b[K, N], fp32.  b may be a vector [K] (N = 1, the

@@ -372,6 +372,14 @@ int akili_flash_ml_ex(const flash_arg_t* arg, const akili_ex_t* ex, uint64_t m_a
  * three vx_start launches, chosen by arg->kernel_id, on fp32 buffers with
  * fp32 CUDA-core arithmetic (S and O summed in the reference's order). */
 int akili_attention(const attention_arg_t* arg, akili_stream_t stream);
+/* The same launches for batch * heads heads stored one after another (Q, V,
+ * O: [heads][N][d]; K: [heads][d][N]; S, P: [heads][N][N]) with the
+ * softmax taken of ex->softmax_scale * S.  fp32 buffers run the exact fp32
+ * kernels above head by head; fp16 buffers (ex in_dtype = out_dtype = F16;
+ * N and d multiples of 8) run the two products on the tensor cores (fp32
+ * accumulation, fp16 S and O) and the softmax as one HBM pass over all rows.
+ * ex->causal must be 0. */
+int akili_attention_ex(const attention_arg_t* arg, const akili_ex_t* ex, akili_stream_t stream);
 
 /* llama2/vxmath.cpp:82-141 (vx_matmul_optimized: one vx_start of
  * llama2/matmul_kernel.cpp:4-24 per call): C = A.B in fp32.  N = 1 runs an

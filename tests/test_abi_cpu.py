@@ -26,8 +26,8 @@ def exported(lib: str) -> set[str]:
 
 def test_libakili_exports_every_declared_entry():
     names = declared("akili.h", "akili_")
-    # kbt+flash, kb2, attention, flash statistics, no-alloc LN, llama2 matmul + batch, helpers
-    assert len(names) == 24 + 20 + 1 + 1 + 1 + 2 + 6
+    # kbt+flash, kb2, attention (+ex), flash statistics, no-alloc LN, llama2 matmul + batch, helpers
+    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 6
     missing = names - exported(abi.LIB_PATH)
     assert not missing, missing
     L = abi.load()
@@ -130,3 +130,15 @@ def test_workspace_query_needs_no_buffers():
     assert L.akili_workspace_bytes(b"kbt_gemm_layernorm", C.byref(a), None, C.byref(n)) == 0
     assert n.value >= (16384 * 4096 + 4096 * 4096) * 2  # fp16 copies of the fp32 operands
     assert L.akili_workspace_bytes(b"nope", C.byref(a), None, C.byref(n)) == abi.E_UNSUPPORTED
+
+
+def test_attention_ex_rejects_bad_modes_before_cuda():
+    L = abi.load()
+    arg = abi.AttentionArg()
+    arg.N, arg.d, arg.kernel_id = 64, 16, 0
+    arg.Q_addr = arg.K_addr = arg.S_addr = arg.P_addr = arg.V_addr = arg.O_addr = 0x1000
+    assert L.akili_attention_ex(C.byref(arg), None, None) == abi.E_NULL_ARG
+    assert L.akili_attention_ex(C.byref(arg), C.byref(abi.make_ex(abi.DTYPE_F16, abi.DTYPE_F32)), None) == abi.E_DTYPE
+    assert L.akili_attention_ex(C.byref(arg), C.byref(abi.make_ex(causal=1)), None) == abi.E_UNSUPPORTED
+    arg.kernel_id = 3
+    assert L.akili_attention_ex(C.byref(arg), C.byref(abi.make_ex()), None) == abi.E_UNSUPPORTED
