@@ -468,13 +468,15 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // of exp2_fma and a cubic for 2^f on [-0.5, 0.5] (fitted for this library by
 // iteratively reweighted least squares on the relative error: max 7.5e-5,
 // below the 4.9e-4 of fp16), for values that are rounded to fp16 next.
-// Inputs are clamped at -127.
+// Inputs are clamped at -126.
 __device__ __forceinline__ void exp2_fma3_pair(float x0, float x1, float& y0, float& y1) {
-  constexpr float kMagic = 12582912.0f;
-  const uint64_t x = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + kMagic holds round(x) in its low mantissa bits
+  // Clamped at -126: round(x) >= -126 keeps the exponent field of the
+  // result >= 0 (at -127 a p just below 1 would wrap it to a NaN).
+  const uint64_t x = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
   const uint64_t magic = f2_pack(kMagic, kMagic);
   const uint64_t t = f2_add(x, magic);
-  const uint64_t f = f2_sub(x, f2_sub(t, magic));
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));  // x - round(x), in [-0.5, 0.5]
   uint64_t p = f2_fma(f2_pack(0.055174145847558975f, 0.055174145847558975f), f,
                       f2_pack(0.24261757731437683f, 0.24261757731437683f));
   p = f2_fma(p, f, f2_pack(0.6932610869407654f, 0.6932610869407654f));
@@ -482,8 +484,11 @@ __device__ __forceinline__ void exp2_fma3_pair(float x0, float x1, float& y0, fl
   float p0, p1, t0, t1;
   f2_unpack(p, p0, p1);
   f2_unpack(t, t0, t1);
-  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - __float_as_int(kMagic)) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - __float_as_int(kMagic)) << 23));
+  // 2^round(x) * p: bits(t) = bits(kMagic) + round(x), and kMagic's low 9
+  // bits are zero, so bits(t) << 23 = round(x) << 23 (mod 2^32), the
+  // exponent increment.
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 // 2^x for two fp16 values in one MUFU instruction (x packed as fp16x2).
