@@ -212,6 +212,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.akili_attention.restype = C.c_int
     L.akili_attention_ex.argtypes = [C.POINTER(AttentionArg), C.POINTER(AkiliEx), C.c_void_p]
     L.akili_attention_ex.restype = C.c_int
+    L.akili_host_call.argtypes = [C.c_char_p, C.c_void_p, C.POINTER(AkiliEx), C.c_void_p]
+    L.akili_host_call.restype = C.c_int
     L.akili_llama2_matmul.argtypes = [C.POINTER(MatmulKernelArgs), C.c_void_p]
     L.akili_llama2_matmul.restype = C.c_int
     L.akili_llama2_matvec_batch.argtypes = [C.POINTER(MatvecSeg), C.c_int, C.c_uint64, C.c_int32, C.c_void_p]

@@ -1274,6 +1274,154 @@ int attention_run(const attention_arg_t* a, const Mode& md, cudaStream_t st) {
   return rc;
 }
 
+// ------------------------------------------------------------ host calls --
+// One GEMM-family op on HOST buffers (the harness's copy-in / run / copy-out
+// as one pipelined call).  The whole operands (W, bias and affine vectors)
+// are copied once; then the rows go through in chunks on three streams:
+// host->device copy of chunk c+1, the fused GEMM of chunk c and the
+// device->host copy of chunk c-1 overlap, so the two copy engines and the
+// SMs work at once.  Row chunks are independent for every op here: each
+// output row (or row value) depends on its own input row only.
+constexpr int kHostSlots = 3;  // chunk buffers in flight
+
+struct HostPipe {
+  std::mutex mu;
+  bool ready = false;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t loaded[kHostSlots] = {}, computed[kHostSlots] = {}, stored[kHostSlots] = {};
+  void* whole = nullptr;  // W, B1 and the per-column vectors
+  size_t whole_bytes = 0;
+  void* rows = nullptr;   // kHostSlots x (A chunk + C chunk)
+  size_t rows_bytes = 0;
+};
+
+int host_pipe(HostPipe** out) {
+  static HostPipe per_dev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return AKILI_E_NO_DEVICE;
+  }
+  HostPipe& h = per_dev[dev];
+  *out = &h;
+  return AKILI_OK;
+}
+
+int grow_buffer(void** p, size_t* have, size_t need) {
+  if (*have >= need) return AKILI_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  if (cudaMalloc(p, need) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return AKILI_E_ALLOC;
+  }
+  *have = need;
+  return AKILI_OK;
+}
+
+bool epi_vector_out(Epi e) { return e == Epi::kRowSumHalf || e == Epi::kRowSumBias || e == Epi::kLseClamp; }
+
+int run_host_job(GemmJob j, const Mode& md, cudaStream_t st) {
+  if (j.M == 0) return AKILI_OK;
+  const bool dual = epi_dual(j.epi);
+  const bool bias = j.epi == Epi::kBiasRelu || j.epi == Epi::kBiasMulLeaky || j.epi == Epi::kRowSumBias ||
+                    j.epi == Epi::kLnPre || j.epi == Epi::kSiluMulBias;
+  if (!j.A || !j.B0 || !j.C || (dual && !j.B1) || (bias && !j.vec0) ||
+      (j.epi == Epi::kSiluMulBias && !j.vec1) || (j.epi == Epi::kLnPre && (!j.ln_w || !j.ln_b)) ||
+      (j.rmsnorm && !j.rms_w))
+    return AKILI_E_NULL_ARG;
+  HostPipe* hp = nullptr;
+  int rc = host_pipe(&hp);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(hp->mu);
+  if (!hp->ready) {
+    bool ok = cudaStreamCreateWithFlags(&hp->h2d, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&hp->d2h, cudaStreamNonBlocking) == cudaSuccess;
+    for (int i = 0; i < kHostSlots && ok; ++i)
+      ok = cudaEventCreateWithFlags(&hp->loaded[i], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&hp->computed[i], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&hp->stored[i], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+      cudaGetLastError();
+      return AKILI_E_LAUNCH;
+    }
+    hp->ready = true;
+  }
+  const size_t ein = md.in_f32 ? 4 : 2, eout = md.out_f32 ? 4 : 2;
+  const size_t M = j.M, N = j.N, K = j.K;
+  const size_t a_row = K * ein, c_row = (epi_vector_out(j.epi) ? 1 : N) * eout;
+  // the whole operands, 256-byte aligned pieces
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  struct Piece { const void* host; size_t bytes; const void** dev; };
+  Piece pieces[8];
+  int np = 0;
+  pieces[np++] = {j.B0, K * N * ein, &j.B0};
+  if (dual) pieces[np++] = {j.B1, K * N * ein, &j.B1};
+  const void* v0 = j.vec0; const void* v1 = j.vec1; const void* lw = j.ln_w; const void* lb = j.ln_b;
+  const void* rw = j.rms_w;
+  if (v0) pieces[np++] = {v0, N * 4, &v0};
+  if (v1) pieces[np++] = {v1, N * 4, &v1};
+  if (lw) pieces[np++] = {lw, N * 4, &lw};
+  if (lb) pieces[np++] = {lb, N * 4, &lb};
+  if (rw) pieces[np++] = {rw, K * 4, &rw};
+  size_t whole = 0;
+  for (int i = 0; i < np; ++i) whole += up(pieces[i].bytes);
+  // chunks of a multiple of 128 rows, about 8 of them
+  size_t chunk = ((M + 7) / 8 + 127) / 128 * 128;
+  if (chunk > M) chunk = M;
+  const size_t slot_bytes = up(chunk * a_row) + up(chunk * c_row);
+  if ((rc = grow_buffer(&hp->whole, &hp->whole_bytes, whole)) ||
+      (rc = grow_buffer(&hp->rows, &hp->rows_bytes, slot_bytes * kHostSlots)))
+    return rc;
+  bool ok = true;
+  size_t off = 0;
+  for (int i = 0; i < np && ok; ++i) {
+    char* d = static_cast<char*>(hp->whole) + off;
+    ok = cudaMemcpyAsync(d, pieces[i].host, pieces[i].bytes, cudaMemcpyHostToDevice, hp->h2d) == cudaSuccess;
+    *pieces[i].dev = d;
+    off += up(pieces[i].bytes);
+  }
+  j.vec0 = static_cast<const float*>(v0); j.vec1 = static_cast<const float*>(v1);
+  j.ln_w = static_cast<const float*>(lw); j.ln_b = static_cast<const float*>(lb);
+  j.rms_w = static_cast<const float*>(rw);
+  j.stats_hint = nullptr; j.stats_hint_bytes = 0; j.xhat_hint = nullptr;  // scratch from the pool
+  const char* hA = static_cast<const char*>(j.A);
+  char* hC = static_cast<char*>(j.C);
+  const size_t nchunks = (M + chunk - 1) / chunk;
+  for (size_t c = 0; c < nchunks && ok && rc == AKILI_OK; ++c) {
+    const int sl = static_cast<int>(c % kHostSlots);
+    const size_t r0 = c * chunk, rows = std::min(chunk, M - r0);
+    char* dA = static_cast<char*>(hp->rows) + sl * slot_bytes;
+    char* dC = dA + up(chunk * a_row);
+    // the slot is free once chunk c - kHostSlots has been copied out
+    if (c >= static_cast<size_t>(kHostSlots)) ok = cudaStreamWaitEvent(hp->h2d, hp->stored[sl], 0) == cudaSuccess;
+    ok = ok && cudaMemcpyAsync(dA, hA + r0 * a_row, rows * a_row, cudaMemcpyHostToDevice, hp->h2d) == cudaSuccess &&
+         cudaEventRecord(hp->loaded[sl], hp->h2d) == cudaSuccess &&
+         cudaStreamWaitEvent(st, hp->loaded[sl], 0) == cudaSuccess;
+    if (!ok) break;
+    GemmJob jc = j;
+    jc.M = static_cast<uint32_t>(rows);
+    jc.A = dA;
+    jc.C = dC;
+    rc = run_job(jc, md, st);
+    ok = rc == AKILI_OK && cudaEventRecord(hp->computed[sl], st) == cudaSuccess &&
+         cudaStreamWaitEvent(hp->d2h, hp->computed[sl], 0) == cudaSuccess &&
+         cudaMemcpyAsync(hC + r0 * c_row, dC, rows * c_row, cudaMemcpyDeviceToHost, hp->d2h) == cudaSuccess &&
+         cudaEventRecord(hp->stored[sl], hp->d2h) == cudaSuccess;
+  }
+  // the call returns with the outputs in host memory (and every stream idle)
+  const bool synced = cudaStreamSynchronize(hp->h2d) == cudaSuccess && cudaStreamSynchronize(st) == cudaSuccess &&
+                      cudaStreamSynchronize(hp->d2h) == cudaSuccess;
+  if (rc) return rc;
+  if (!ok || !synced) {
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
+  return AKILI_OK;
+}
+
 }  // namespace
 
 // ===================================================================== ABI ==
@@ -1517,6 +1665,46 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
     *bytes = flash_scratch_bytes(fj, md);
     return AKILI_OK;
   }
+  return AKILI_E_UNSUPPORTED;
+}
+
+int akili_host_call(const char* op, const void* arg, const akili_ex_t* ex, akili_stream_t s) {
+  if (!op || !arg) return AKILI_E_NULL_ARG;
+  Mode md;
+  int rc = parse_ex(ex, &md);
+  if (rc) return rc;
+  if (md.causal || md.batch != 1 || md.heads != 1) return AKILI_E_UNSUPPORTED;
+  GemmJob j;
+  const std::string name(op);
+  const bool kb2 = name.rfind("kb2_", 0) == 0;
+  if (kb2 && (!md.in_f32 || !md.out_f32)) return AKILI_E_DTYPE;
+#define AKILI_HC(nm, T, build)                                          \
+  if (name == #nm) {                                                    \
+    if ((rc = build(static_cast<const T*>(arg), j, false))) return rc; \
+    return run_host_job(j, md, S(s));                                   \
+  }
+  AKILI_HC(kbt_sgemm, kbt_sgemm_arg_t, job_sgemm)
+  AKILI_HC(kbt_gemm_add_relu, kbt_gemm_add_relu_arg_t, job_add_relu)
+  AKILI_HC(kbt_gemm_mul_leakyrelu, kbt_gemm_mul_leakyrelu_arg_t, job_mul_leakyrelu)
+  AKILI_HC(kbt_gemm_div_sum_scale, kbt_gemm_div_sum_scale_arg_t, job_div_sum_scale)
+  AKILI_HC(kbt_gemm_layernorm, kbt_gemm_layernorm_arg_t, job_layernorm)
+  AKILI_HC(kbt_attention_score, kbt_attention_score_arg_t, job_attention_score)
+  AKILI_HC(kbt_matmul_softmax, kbt_matmul_softmax_arg_t, job_matmul_softmax)
+  AKILI_HC(kbt_matmul_scale_residadd_clamp, kbt_matmul_scale_residadd_clamp_arg_t, job_clamp)
+  AKILI_HC(kbt_matmul_sum_max_avgpool, kbt_matmul_sum_max_avgpool_arg_t, job_sum_max_avgpool)
+  AKILI_HC(kbt_gemm_rmsnorm_swiglu, kbt_gemm_rmsnorm_swiglu_arg_t, job_rmsnorm_swiglu)
+  AKILI_HC(kbt_gemm_silu_mul, kbt_gemm_silu_mul_arg_t, job_silu_mul)
+  AKILI_HC(kb2_gemm_add_relu, kb2_gemm_add_relu_arg_t, job_kb2_add_relu)
+  AKILI_HC(kb2_gemm_mul_leakyrelu, kb2_gemm_mul_leakyrelu_arg_t, job_kb2_mul_leakyrelu)
+  AKILI_HC(kb2_gemm_div_sum_scale, kb2_gemm_div_sum_scale_arg_t, job_kb2_div_sum_scale)
+  AKILI_HC(kb2_gemm_layernorm, kb2_gemm_layernorm_arg_t, job_kb2_layernorm)
+  AKILI_HC(kb2_attention_score, kb2_attention_score_arg_t, job_kb2_attention_score)
+  AKILI_HC(kb2_matmul_softmax, kb2_matmul_softmax_arg_t, job_kb2_matmul_softmax)
+  AKILI_HC(kb2_matmul_scale_residadd_clamp, kb2_matmul_scale_residadd_clamp_arg_t, job_kb2_clamp)
+  AKILI_HC(kb2_matmul_sum_max_avgpool, kb2_matmul_sum_max_avgpool_arg_t, job_kb2_sum_max_avgpool)
+  AKILI_HC(kb2_gemm_rmsnorm_swiglu, kb2_gemm_rmsnorm_swiglu_arg_t, job_kb2_rmsnorm_swiglu)
+  AKILI_HC(kb2_gemm_silu_mul, kb2_gemm_silu_mul_arg_t, job_kb2_silu_mul)
+#undef AKILI_HC
   return AKILI_E_UNSUPPORTED;
 }
 

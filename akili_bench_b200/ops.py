@@ -298,6 +298,38 @@ def llama2_matvec_batch(ws, x, outs=None, stream=None):
     return outs
 
 
+def _haddr(t: torch.Tensor | None) -> int:
+    if t is None:
+        return 0
+    assert not t.is_cuda and t.is_contiguous(), "host calls take contiguous CPU tensors (page-locked to overlap)"
+    return int(t.data_ptr())
+
+
+def host_call(op: str, arg, in_dtype, out_dtype, stream=None) -> None:
+    """akili_host_call: `arg` holds HOST addresses; blocks until the output
+    is in host memory (copies and the fused GEMM pipelined over row chunks)."""
+    ex = None
+    if in_dtype != torch.float32 or out_dtype != torch.float32:
+        ex = abi.make_ex(abi.DTYPE_F16 if in_dtype == torch.float16 else abi.DTYPE_F32,
+                         abi.DTYPE_F16 if out_dtype == torch.float16 else abi.DTYPE_F32)
+    rc = abi.load().akili_host_call(op.encode(), C.byref(arg), C.byref(ex) if ex is not None else None,
+                                    C.c_void_p(_stream(stream)))
+    if rc != abi.OK:
+        raise abi.AkiliError(f"host_call({op})", rc)
+
+
+def kbt_gemm_add_relu_host(x, w, bias, out=None, out_dtype=None, stream=None):
+    """kbt_gemm_add_relu on CPU tensors (x [M, K], w [K, N], bias [N] fp32):
+    the harness's copy-in / run / copy-out as one pipelined call."""
+    M, K = x.shape
+    N = w.shape[1]
+    c = out if out is not None else torch.empty((M, N), dtype=out_dtype or x.dtype, pin_memory=True)
+    arg = _hdr(abi.KbtGemmAddReluArg, M, N, K)
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _haddr(x), _haddr(w), _haddr(bias), _haddr(c)
+    host_call("kbt_gemm_add_relu", arg, x.dtype, c.dtype, stream)
+    return c
+
+
 def launch_count() -> int:
     return int(abi.load().akili_launch_count())
 

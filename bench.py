@@ -114,10 +114,22 @@ def workloads(torch, ops):
         return make
 
     M2, N2, K2 = 8192, 4096, 4096
+
+    # end to end: akili_host_call on page-locked host buffers, the copies and
+    # the fused GEMM pipelined over row chunks inside the call
+    def ar_host(d):
+        return {k: d[k].cpu().pin_memory() for k in ("x", "w", "b")} | {
+            "out": torch.empty((M2, N2), dtype=f16, pin_memory=True)}
+
+    def ar_e2e(d, h, st):
+        ops.kbt_gemm_add_relu_host(h["x"], h["w"], h["b"], out=h["out"], stream=st)
+        return (sum(h[k].numel() * h[k].element_size() for k in ("x", "w", "b")),
+                h["out"].numel() * h["out"].element_size())
+
     W["kbt_gemm_add_relu"] = Workload(
         "kbt_gemm_add_relu", {"M": M2, "N": N2, "K": K2}, 2.0 * M2 * N2 * K2, gemm_inputs(M2, N2, K2),
         lambda d, out, st: ops.kbt_gemm_add_relu(d["x"], d["w"], d["b"], out=out, stream=st),
-        host=("x", "w", "b"), cpu="add_relu")
+        host=("x", "w", "b"), cpu="add_relu", e2e_host=ar_host, e2e_step=ar_e2e)
     W["kbt_gemm_mul_leakyrelu"] = Workload(
         "kbt_gemm_mul_leakyrelu", {"M": M2, "N": N2, "K": K2}, 2.0 * M2 * N2 * K2, gemm_inputs(M2, N2, K2),
         lambda d, out, st: ops.kbt_gemm_mul_leakyrelu(d["x"], d["w"], d["b"], 1.5, 0.01, out=out, stream=st))

@@ -440,6 +440,20 @@ const char* akili_strerror(int code);
  * `arg` pointer must point at that op's struct.  Returns AKILI_OK. */
 int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex, uint64_t* bytes);
 
+/* One kbt_* / kb2_* GEMM op on HOST buffers: every *_addr field of `arg`
+ * (named by `op`, e.g. "kbt_gemm_add_relu") is a host address.  Replaces the
+ * harness's whole device round trip (vx_copy_to_dev of the inputs, vx_start,
+ * vx_ready_wait, vx_copy_from_dev of the output; e.g.
+ * kbt_gemm_add_relu/main.cpp:98-124).  W and the vectors are copied once;
+ * the rows then go through in chunks with the host->device copy, the fused
+ * GEMM and the device->host copy of successive chunks overlapped on three
+ * streams (compute on `stream`).  Returns when the output is in host memory.
+ * Page-locked host buffers (cudaHostAlloc / cudaHostRegister) let the copies
+ * overlap; pageable ones work but serialise.  The scratch fields (norm, gate,
+ * temp) are not written.  ex as for the op's _ex entry (batch, heads and
+ * causal must be defaults); NULL = fp32 in and out. */
+int akili_host_call(const char* op, const void* arg, const akili_ex_t* ex, akili_stream_t stream);
+
 /* Device status word of the current device: 0 when no kernel has timed out
  * on a device-side wait since the last clear, else the code of the first wait
  * that gave up.  Synchronises the device. `clear` != 0 resets it. */

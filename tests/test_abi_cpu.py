@@ -27,7 +27,7 @@ def exported(lib: str) -> set[str]:
 def test_libakili_exports_every_declared_entry():
     names = declared("akili.h", "akili_")
     # kbt+flash, kb2, attention (+ex), flash statistics, no-alloc LN, llama2 matmul + batch, helpers
-    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 6
+    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 7  # helpers: + akili_host_call
     missing = names - exported(abi.LIB_PATH)
     assert not missing, missing
     L = abi.load()
@@ -142,3 +142,18 @@ def test_attention_ex_rejects_bad_modes_before_cuda():
     assert L.akili_attention_ex(C.byref(arg), C.byref(abi.make_ex(causal=1)), None) == abi.E_UNSUPPORTED
     arg.kernel_id = 3
     assert L.akili_attention_ex(C.byref(arg), C.byref(abi.make_ex()), None) == abi.E_UNSUPPORTED
+
+
+def test_host_call_validates_before_cuda():
+    L = abi.load()
+    arg = abi.KbtGemmAddReluArg()
+    arg.M, arg.N, arg.K = 64, 64, 64
+    assert L.akili_host_call(b"no_such_op", C.byref(arg), None, None) == abi.E_UNSUPPORTED
+    assert L.akili_host_call(None, C.byref(arg), None, None) == abi.E_NULL_ARG
+    assert L.akili_host_call(b"kbt_gemm_add_relu", C.byref(arg), None, None) == abi.E_NULL_ARG  # host pointers 0
+    arg.N = 60
+    assert L.akili_host_call(b"kbt_gemm_add_relu", C.byref(arg), None, None) == abi.E_SHAPE
+    k2 = abi.Kb2GemmAddReluArg(64, 64, 64, 0, 0, 0, 0)
+    assert L.akili_host_call(b"kb2_gemm_add_relu", C.byref(k2), C.byref(abi.make_ex()), None) == abi.E_DTYPE
+    assert L.akili_host_call(b"kbt_gemm_add_relu", C.byref(arg), C.byref(abi.make_ex(batch=2)), None) == \
+        abi.E_UNSUPPORTED
