@@ -11,6 +11,7 @@ per-column vectors fp32 [N]; attention-score K is [N, D]; flash tensors are
 from __future__ import annotations
 
 import ctypes as C
+import threading
 
 import torch
 
@@ -29,6 +30,23 @@ def _addr(t: torch.Tensor | None) -> int:
     return int(t.data_ptr())
 
 
+_tls = threading.local()
+
+
+def _a(t: torch.Tensor | None) -> int:
+    """Address of an operand of a kbt_* GEMM op: CUDA tensors for the device
+    entry, CPU tensors (page-locked to overlap) for akili_host_call.  The
+    places of one call's operands are checked together in _launch."""
+    if t is None:
+        return 0
+    assert t.is_contiguous(), "akili ops take contiguous tensors"
+    places = getattr(_tls, "places", None)
+    if places is None:
+        _tls.places = places = set()
+    places.add(bool(t.is_cuda))
+    return int(t.data_ptr())
+
+
 def _dt(t: torch.Tensor) -> int:
     if t.dtype == torch.float16:
         return abi.DTYPE_F16
@@ -39,6 +57,11 @@ def _dt(t: torch.Tensor) -> int:
 
 def _launch(op: str, arg, in_t: torch.Tensor, out_t: torch.Tensor, stream=None, ex_extra=None,
             workspace: torch.Tensor | None = None) -> None:
+    places = getattr(_tls, "places", None) or set()
+    _tls.places = set()
+    on_gpu = bool(in_t.is_cuda)
+    if places and places != {on_gpu}:
+        raise ValueError(f"akili_{op}: all tensors of one call must be CUDA tensors, or all host tensors")
     plain = in_t.dtype == torch.float32 and out_t.dtype == torch.float32 and not ex_extra and workspace is None
     ex = None
     if not plain:
@@ -46,7 +69,16 @@ def _launch(op: str, arg, in_t: torch.Tensor, out_t: torch.Tensor, stream=None, 
         if workspace is not None:
             ex.workspace = _addr(workspace)
             ex.workspace_bytes = workspace.numel() * workspace.element_size()
-    abi.check(op, arg, ex, _stream(stream))
+    if on_gpu:
+        abi.check(op, arg, ex, _stream(stream))
+        return
+    # host tensors: the pipelined copy-in / run / copy-out of akili_host_call
+    if workspace is not None:
+        raise ValueError("a device workspace does not apply to a host call")
+    rc = abi.load().akili_host_call(op.encode(), C.byref(arg), C.byref(ex) if ex is not None else None,
+                                    C.c_void_p(_stream(stream)))
+    if rc != abi.OK:
+        raise abi.AkiliError(f"host_call({op})", rc)
 
 
 def _hdr(st, M, N, K, kname="K"):
@@ -64,7 +96,7 @@ def _out(x, M, N, out_dtype, out):
     if out is not None:
         return out
     shape = (M, N) if N is not None else (M,)
-    return torch.empty(shape, device=x.device, dtype=out_dtype or x.dtype)
+    return torch.empty(shape, device=x.device, dtype=out_dtype or x.dtype, pin_memory=not x.is_cuda)
 
 
 def kbt_sgemm(a, b, out=None, out_dtype=None, stream=None):
@@ -72,7 +104,7 @@ def kbt_sgemm(a, b, out=None, out_dtype=None, stream=None):
     N = b.shape[1]
     c = _out(a, M, N, out_dtype or torch.float32, out)
     arg = _hdr(abi.KbtSgemmArg, M, N, K)
-    arg.a_addr, arg.b_addr, arg.c_addr = _addr(a), _addr(b), _addr(c)
+    arg.a_addr, arg.b_addr, arg.c_addr = _a(a), _a(b), _a(c)
     _launch("kbt_sgemm", arg, a, c, stream)
     return c
 
@@ -82,7 +114,7 @@ def kbt_gemm_add_relu(x, w, bias, out=None, out_dtype=None, stream=None, workspa
     N = w.shape[1]
     c = _out(x, M, N, out_dtype, out)
     arg = _hdr(abi.KbtGemmAddReluArg, M, N, K)
-    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _addr(x), _addr(w), _addr(bias), _addr(c)
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _a(x), _a(w), _a(bias), _a(c)
     _launch("kbt_gemm_add_relu", arg, x, c, stream, workspace=workspace)
     return c
 
@@ -94,7 +126,7 @@ def kbt_gemm_mul_leakyrelu(x, w, bias, multiplier=1.5, negative_slope=0.01, out=
     c = _out(x, M, N, out_dtype, out)
     arg = _hdr(abi.KbtGemmMulLeakyreluArg, M, N, K)
     arg.multiplier, arg.negative_slope = multiplier, negative_slope
-    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _addr(x), _addr(w), _addr(bias), _addr(c)
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _a(x), _a(w), _a(bias), _a(c)
     _launch("kbt_gemm_mul_leakyrelu", arg, x, c, stream)
     return c
 
@@ -105,7 +137,7 @@ def kbt_gemm_div_sum_scale(x, w, scaling_factor=2.0, out=None, out_dtype=torch.f
     c = _out(x, M, None, out_dtype, out)
     arg = _hdr(abi.KbtGemmDivSumScaleArg, M, N, K)
     arg.scaling_factor = scaling_factor
-    arg.a_addr, arg.w_addr, arg.c_addr = _addr(x), _addr(w), _addr(c)
+    arg.a_addr, arg.w_addr, arg.c_addr = _a(x), _a(w), _a(c)
     _launch("kbt_gemm_div_sum_scale", arg, x, c, stream)
     return c
 
@@ -116,8 +148,8 @@ def kbt_gemm_layernorm(x, w, bias, ln_w, ln_b, eps=1e-5, out=None, out_dtype=Non
     c = _out(x, M, N, out_dtype, out)
     arg = _hdr(abi.KbtGemmLayernormArg, M, N, K)
     arg.eps = eps
-    arg.a_addr, arg.w_addr, arg.bias_addr = _addr(x), _addr(w), _addr(bias)
-    arg.ln_w_addr, arg.ln_b_addr, arg.c_addr = _addr(ln_w), _addr(ln_b), _addr(c)
+    arg.a_addr, arg.w_addr, arg.bias_addr = _a(x), _a(w), _a(bias)
+    arg.ln_w_addr, arg.ln_b_addr, arg.c_addr = _a(ln_w), _a(ln_b), _a(c)
     _launch("kbt_gemm_layernorm", arg, x, c, stream, workspace=workspace)
     return c
 
@@ -127,7 +159,7 @@ def kbt_attention_score(q, k, out=None, out_dtype=None, stream=None):
     N = k.shape[0]
     c = _out(q, M, N, out_dtype, out)
     arg = _hdr(abi.KbtAttentionScoreArg, M, N, D, kname="D")
-    arg.q_addr, arg.k_addr, arg.c_addr = _addr(q), _addr(k), _addr(c)
+    arg.q_addr, arg.k_addr, arg.c_addr = _a(q), _a(k), _a(c)
     _launch("kbt_attention_score", arg, q, c, stream)
     return c
 
@@ -137,7 +169,7 @@ def kbt_matmul_softmax(a, b, out=None, out_dtype=None, stream=None):
     N = b.shape[1]
     c = _out(a, M, N, out_dtype, out)
     arg = _hdr(abi.KbtMatmulSoftmaxArg, M, N, K)
-    arg.a_addr, arg.b_addr, arg.c_addr = _addr(a), _addr(b), _addr(c)
+    arg.a_addr, arg.b_addr, arg.c_addr = _a(a), _a(b), _a(c)
     _launch("kbt_matmul_softmax", arg, a, c, stream)
     return c
 
@@ -149,7 +181,7 @@ def kbt_matmul_scale_residadd_clamp(a, b, scale_factor=0.5, clamp_min=-2.0, clam
     c = _out(a, M, None, out_dtype, out)
     arg = _hdr(abi.KbtMatmulScaleResidaddClampArg, M, N, K)
     arg.scale_factor, arg.clamp_min, arg.clamp_max = scale_factor, clamp_min, clamp_max
-    arg.a_addr, arg.b_addr, arg.c_addr, arg.temp_addr = _addr(a), _addr(b), _addr(c), _addr(temp)
+    arg.a_addr, arg.b_addr, arg.c_addr, arg.temp_addr = _a(a), _a(b), _a(c), _a(temp)
     _launch("kbt_matmul_scale_residadd_clamp", arg, a, c, stream)
     return c
 
@@ -159,7 +191,7 @@ def kbt_matmul_sum_max_avgpool(x, w, bias, out=None, out_dtype=torch.float32, st
     N = w.shape[1]
     c = _out(x, M, None, out_dtype, out)
     arg = _hdr(abi.KbtMatmulSumMaxAvgpoolArg, M, N, K)
-    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _addr(x), _addr(w), _addr(bias), _addr(c)
+    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _a(x), _a(w), _a(bias), _a(c)
     _launch("kbt_matmul_sum_max_avgpool", arg, x, c, stream)
     return c
 
@@ -170,8 +202,8 @@ def kbt_gemm_rmsnorm_swiglu(x, rms_w, wg, wu, eps=1e-5, norm=None, out=None, out
     c = _out(x, M, N, out_dtype, out)
     arg = _hdr(abi.KbtGemmRmsnormSwigluArg, M, N, K)
     arg.eps = eps
-    arg.x_addr, arg.rms_w_addr, arg.wg_addr, arg.wu_addr = _addr(x), _addr(rms_w), _addr(wg), _addr(wu)
-    arg.norm_addr, arg.gate_addr, arg.c_addr = _addr(norm), 0, _addr(c)
+    arg.x_addr, arg.rms_w_addr, arg.wg_addr, arg.wu_addr = _a(x), _a(rms_w), _a(wg), _a(wu)
+    arg.norm_addr, arg.gate_addr, arg.c_addr = _a(norm), 0, _a(c)
     _launch("kbt_gemm_rmsnorm_swiglu", arg, x, c, stream)
     return c
 
@@ -181,8 +213,8 @@ def kbt_gemm_silu_mul(x, wa, ba, wb, bb, out=None, out_dtype=None, stream=None):
     N = wa.shape[1]
     c = _out(x, M, N, out_dtype, out)
     arg = _hdr(abi.KbtGemmSiluMulArg, M, N, K)
-    arg.a_addr, arg.wa_addr, arg.ba_addr = _addr(x), _addr(wa), _addr(ba)
-    arg.wb_addr, arg.bb_addr, arg.gate_addr, arg.c_addr = _addr(wb), _addr(bb), 0, _addr(c)
+    arg.a_addr, arg.wa_addr, arg.ba_addr = _a(x), _a(wa), _a(ba)
+    arg.wb_addr, arg.bb_addr, arg.gate_addr, arg.c_addr = _a(wb), _a(bb), 0, _a(c)
     _launch("kbt_gemm_silu_mul", arg, x, c, stream)
     return c
 
@@ -320,14 +352,10 @@ def host_call(op: str, arg, in_dtype, out_dtype, stream=None) -> None:
 
 def kbt_gemm_add_relu_host(x, w, bias, out=None, out_dtype=None, stream=None):
     """kbt_gemm_add_relu on CPU tensors (x [M, K], w [K, N], bias [N] fp32):
-    the harness's copy-in / run / copy-out as one pipelined call."""
-    M, K = x.shape
-    N = w.shape[1]
-    c = out if out is not None else torch.empty((M, N), dtype=out_dtype or x.dtype, pin_memory=True)
-    arg = _hdr(abi.KbtGemmAddReluArg, M, N, K)
-    arg.a_addr, arg.w_addr, arg.bias_addr, arg.c_addr = _haddr(x), _haddr(w), _haddr(bias), _haddr(c)
-    host_call("kbt_gemm_add_relu", arg, x.dtype, c.dtype, stream)
-    return c
+    the harness's copy-in / run / copy-out as one pipelined call (every kbt_*
+    wrapper above takes this path when its tensors are CPU tensors)."""
+    assert not x.is_cuda
+    return kbt_gemm_add_relu(x, w, bias, out=out, out_dtype=out_dtype, stream=stream)
 
 
 def launch_count() -> int:
