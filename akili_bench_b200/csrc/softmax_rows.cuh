@@ -97,9 +97,26 @@ __device__ __forceinline__ float sm_exp2(int j, float x) {
   return ex2_mufu(x);
 }
 
+// Sweep 1 by pairs: of each kSmFmaPairs consecutive column pairs the last
+// goes to the FMA pipe as one packed cubic (exp2_fma3_pair, relative error
+// 7.5e-5, below the rounding of an fp16 output), the rest to the MUFU; 0
+// keeps all on the MUFU (then kSmFmaEvery applies).  The two sweeps'
+// exponentials keep the MUFU about 73% busy; at the 16384 x 4096 x 128
+// attention score one pair in 6 or 5 on the FMA pipe measured 301 / 300
+// TFLOP/s against 284 for none, one in 4 / 3 / 2 295 / 289 / 281.  The same
+// offload in sweep 2 (the fp16 stores) gained nothing.
+#ifndef AKILI_SM_FMA_PAIRS
+#define AKILI_SM_FMA_PAIRS 6
+#endif
+constexpr int kSmFmaPairs = AKILI_SM_FMA_PAIRS;
+
 // Two passes over 64 accumulator columns (the first `nvalid` of which
 // exist): the block maximum first, then sum exp2(x - max); merged into the
 // row's running (m, l), m = max of x = acc * c, l = sum exp2(x - m).
+// kPairs: the FMA-pipe share of kSmFmaPairs applies (fp16 outputs, whose
+// rounding hides the cubic's 7.5e-5; fp32 outputs keep every exponential on
+// the MUFU).
+template <bool kPairs>
 __device__ __forceinline__ void softmax_fold64(const float (&v)[64], int nvalid, float c, float& m, float& l) {
   float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -107,8 +124,24 @@ __device__ __forceinline__ void softmax_fold64(const float (&v)[64], int nvalid,
 #pragma unroll
     for (int j = 0; j < 64; ++j) cm[j & 3] = fmaxf(cm[j & 3], v[j]);
     const float mnew = fmaxf(m, max4(cm) * c);
+    if constexpr (kPairs && kSmFmaPairs > 0) {
 #pragma unroll
-    for (int j = 0; j < 64; ++j) la[j & 3] += sm_exp2(j, fmaf(v[j], c, -mnew));
+      for (int jp = 0; jp < 32; ++jp) {
+        const float x0 = fmaf(v[2 * jp], c, -mnew), x1 = fmaf(v[2 * jp + 1], c, -mnew);
+        float p0, p1;
+        if (jp % (kSmFmaPairs > 0 ? kSmFmaPairs : 1) == kSmFmaPairs - 1) {
+          exp2_fma3_pair(x0, x1, p0, p1);
+        } else {
+          p0 = ex2_mufu(x0);
+          p1 = ex2_mufu(x1);
+        }
+        la[(2 * jp) & 3] += p0;
+        la[(2 * jp + 1) & 3] += p1;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) la[j & 3] += sm_exp2(j, fmaf(v[j], c, -mnew));
+    }
     l = l * ex2_mufu(m - mnew) + sum4(la);
     m = mnew;
   } else {
@@ -331,7 +364,7 @@ __global__ void __launch_bounds__(kSmThreads, 1)
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
         const int cb = (i < T ? i : i - T) * 256 + grp * kSmGroupCols;  // first column of this warp's 64
         if (i < T) {
-          if (cb < N) softmax_fold64(v, N - cb, c, m, l);
+          if (cb < N) softmax_fold64<sizeof(OutT) == 2>(v, N - cb, c, m, l);
           if (i == T - 1) {
             // Merge the groups' statistics of each row (double-buffered by
             // row-block parity; the mbarrier wait is bounded).
