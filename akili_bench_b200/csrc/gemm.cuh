@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   constexpr bool kStore = epi_stores(E);
   constexpr int kStats = epi_stats(E);
   constexpr int BN = epi_bn(E);   // output columns per tile
-  constexpr int BNH = BN / 2;     // B columns (per operand) this CTA loads
+  constexpr int BNH = BN / 2;     // B columns this CTA loads (dual: BN columns of its operand)
   constexpr int kOutBytes = sizeof(OutT);
   constexpr int kStageOut = kBM * 32 * kOutBytes;
   constexpr int kPairStages = pair_stages(kStore, kOutBytes);
@@ -645,8 +645,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if constexpr (kBKMajor) {
             tma_load_2d_pair(sb, &tmB0, fb, kb * kBK, col0);
           } else if constexpr (kDual) {
-            tma_load_2d_pair(sb, &tmB0, fb, col0, kb * kBK);
-            tma_load_2d_pair(sb + 8192, &tmB1, fb, col0, kb * kBK);
+            // the even CTA supplies the tile's 128 columns of B0, the odd CTA
+            // the same columns of B1: one N = 256 pair MMA then writes
+            // A.B0 to accumulator columns 0..127 and A.B1 to 128..255
+            const CUtensorMap* tb = leader ? &tmB0 : &tmB1;
+            tma_load_2d_pair(sb, tb, fb, n_blk * BN, kb * kBK);
+            tma_load_2d_pair(sb + 8192, tb, fb, n_blk * BN + 64, kb * kBK);
           } else {
             tma_load_2d_pair(sb, &tmB0, fb, col0, kb * kBK);
             tma_load_2d_pair(sb + 8192, &tmB0, fb, col0 + 64, kb * kBK);
@@ -661,8 +665,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA (even CTA)
-    constexpr uint32_t idesc = kDual ? make_idesc_f16(2 * kBM, 128, false, !kBKMajor)
-                                     : make_idesc_f16(2 * kBM, 256, false, !kBKMajor);
+    // Dual GEMMs too are one N = 256 MMA per K-step (B0 | B1, see the
+    // producer): two N = 128 MMAs of 64 tensor cycles each kept the tensor
+    // pipe 62% busy, one of 128 cycles leaves the issuing thread twice the slack.
+    constexpr uint32_t idesc = make_idesc_f16(2 * kBM, 256, false, !kBKMajor);
     if (leader && lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -687,10 +693,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             const uint32_t accum = (kb | k) != 0;
             if constexpr (kBKMajor) {
               umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
-            } else if constexpr (kDual) {
-              umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
-              umma_f16_ss_pair(d_tmem + 128, ad, make_sdesc(sb + 8192 + k * 2048, 8192, 1024, kSw128), idesc,
-                               accum);
             } else {
               umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
             }
