@@ -666,8 +666,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA (even CTA)
     // Dual GEMMs too are one N = 256 MMA per K-step (B0 | B1, see the
-    // producer): two N = 128 MMAs of 64 tensor cycles each kept the tensor
-    // pipe 62% busy, one of 128 cycles leaves the issuing thread twice the slack.
+    // producer).  Two N = 128 pair MMAs (64 columns per CTA) kept the tensor
+    // pipe 62% busy; MMAs of 64 columns run at 48 cycles for 32 of work.
     constexpr uint32_t idesc = make_idesc_f16(2 * kBM, 256, false, !kBKMajor);
     if (leader && lane == 0) {
       int stage = 0;
