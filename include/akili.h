@@ -451,7 +451,10 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
  * Page-locked host buffers (cudaHostAlloc / cudaHostRegister) let the copies
  * overlap; pageable ones work but serialise.  The scratch fields (norm, gate,
  * temp) are not written.  ex as for the op's _ex entry (batch, heads and
- * causal must be defaults); NULL = fp32 in and out. */
+ * causal must be defaults); NULL = fp32 in and out.  The device buffers it
+ * stages through (W and the vectors, three row-chunk slots) are kept per
+ * device, grow-only, for later calls until the process exits; calls on one
+ * device are serialised by a lock. */
 int akili_host_call(const char* op, const void* arg, const akili_ex_t* ex, akili_stream_t stream);
 
 /* Device status word of the current device: 0 when no kernel has timed out
