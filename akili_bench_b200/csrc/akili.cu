@@ -1321,6 +1321,23 @@ int grow_buffer(void** p, size_t* have, size_t need) {
   return AKILI_OK;
 }
 
+// Streams and events of the pipeline, created on first use (call with hp->mu held).
+int host_pipe_ready(HostPipe* hp) {
+  if (hp->ready) return AKILI_OK;
+  bool ok = cudaStreamCreateWithFlags(&hp->h2d, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&hp->d2h, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; i < kHostSlots && ok; ++i)
+    ok = cudaEventCreateWithFlags(&hp->loaded[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&hp->computed[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&hp->stored[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
+  hp->ready = true;
+  return AKILI_OK;
+}
+
 bool epi_vector_out(Epi e) { return e == Epi::kRowSumHalf || e == Epi::kRowSumBias || e == Epi::kLseClamp; }
 
 int run_host_job(GemmJob j, const Mode& md, cudaStream_t st) {
@@ -1336,19 +1353,7 @@ int run_host_job(GemmJob j, const Mode& md, cudaStream_t st) {
   int rc = host_pipe(&hp);
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(hp->mu);
-  if (!hp->ready) {
-    bool ok = cudaStreamCreateWithFlags(&hp->h2d, cudaStreamNonBlocking) == cudaSuccess &&
-              cudaStreamCreateWithFlags(&hp->d2h, cudaStreamNonBlocking) == cudaSuccess;
-    for (int i = 0; i < kHostSlots && ok; ++i)
-      ok = cudaEventCreateWithFlags(&hp->loaded[i], cudaEventDisableTiming) == cudaSuccess &&
-           cudaEventCreateWithFlags(&hp->computed[i], cudaEventDisableTiming) == cudaSuccess &&
-           cudaEventCreateWithFlags(&hp->stored[i], cudaEventDisableTiming) == cudaSuccess;
-    if (!ok) {
-      cudaGetLastError();
-      return AKILI_E_LAUNCH;
-    }
-    hp->ready = true;
-  }
+  if ((rc = host_pipe_ready(hp))) return rc;
   const size_t ein = md.in_f32 ? 4 : 2, eout = md.out_f32 ? 4 : 2;
   const size_t M = j.M, N = j.N, K = j.K;
   const size_t a_row = K * ein, c_row = (epi_vector_out(j.epi) ? 1 : N) * eout;
@@ -1412,6 +1417,67 @@ int run_host_job(GemmJob j, const Mode& md, cudaStream_t st) {
          cudaEventRecord(hp->stored[sl], hp->d2h) == cudaSuccess;
   }
   // the call returns with the outputs in host memory (and every stream idle)
+  const bool synced = cudaStreamSynchronize(hp->h2d) == cudaSuccess && cudaStreamSynchronize(st) == cudaSuccess &&
+                      cudaStreamSynchronize(hp->d2h) == cudaSuccess;
+  if (rc) return rc;
+  if (!ok || !synced) {
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
+  return AKILI_OK;
+}
+
+// Flash on HOST buffers: the batch*heads heads go through in about 8
+// chunks, the host->device copy of Q, K, V of chunk c+1, the flash kernel
+// of chunk c and the device->host copy of O of chunk c-1 overlapped, as in
+// run_host_job (heads are independent).
+int run_host_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
+  if (!j.Q || !j.K || !j.V || !j.O) return AKILI_E_NULL_ARG;
+  HostPipe* hp = nullptr;
+  int rc = host_pipe(&hp);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(hp->mu);
+  if ((rc = host_pipe_ready(hp))) return rc;
+  const size_t heads = static_cast<size_t>(md.batch) * md.heads;
+  const size_t ein = md.in_f32 ? 4 : 2, eout = md.out_f32 ? 4 : 2;
+  const size_t elems = static_cast<size_t>(j.seq_len) * j.head_dim;  // per head
+  const size_t hin = elems * ein, hout = elems * eout;
+  const size_t chunk = std::max<size_t>(1, (heads + 7) / 8);
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t slot_bytes = 3 * up(chunk * hin) + up(chunk * hout);
+  if ((rc = grow_buffer(&hp->rows, &hp->rows_bytes, slot_bytes * kHostSlots))) return rc;
+  const char* hq = static_cast<const char*>(j.Q);
+  const char* hk = static_cast<const char*>(j.K);
+  const char* hv = static_cast<const char*>(j.V);
+  char* ho = static_cast<char*>(j.O);
+  const size_t nchunks = (heads + chunk - 1) / chunk;
+  bool ok = true;
+  for (size_t c = 0; c < nchunks && ok && rc == AKILI_OK; ++c) {
+    const int sl = static_cast<int>(c % kHostSlots);
+    const size_t h0 = c * chunk, nh = std::min(chunk, heads - h0);
+    char* dq = static_cast<char*>(hp->rows) + sl * slot_bytes;
+    char* dk = dq + up(chunk * hin);
+    char* dv = dk + up(chunk * hin);
+    char* d_o = dv + up(chunk * hin);
+    if (c >= static_cast<size_t>(kHostSlots)) ok = cudaStreamWaitEvent(hp->h2d, hp->stored[sl], 0) == cudaSuccess;
+    ok = ok && cudaMemcpyAsync(dq, hq + h0 * hin, nh * hin, cudaMemcpyHostToDevice, hp->h2d) == cudaSuccess &&
+         cudaMemcpyAsync(dk, hk + h0 * hin, nh * hin, cudaMemcpyHostToDevice, hp->h2d) == cudaSuccess &&
+         cudaMemcpyAsync(dv, hv + h0 * hin, nh * hin, cudaMemcpyHostToDevice, hp->h2d) == cudaSuccess &&
+         cudaEventRecord(hp->loaded[sl], hp->h2d) == cudaSuccess &&
+         cudaStreamWaitEvent(st, hp->loaded[sl], 0) == cudaSuccess;
+    if (!ok) break;
+    FlashJob jc = j;
+    jc.Q = dq; jc.K = dk; jc.V = dv; jc.O = d_o;
+    jc.m_out = nullptr; jc.l_out = nullptr;
+    Mode mc = md;
+    mc.batch = 1;
+    mc.heads = static_cast<uint32_t>(nh);
+    rc = run_flash(jc, mc, st);
+    ok = rc == AKILI_OK && cudaEventRecord(hp->computed[sl], st) == cudaSuccess &&
+         cudaStreamWaitEvent(hp->d2h, hp->computed[sl], 0) == cudaSuccess &&
+         cudaMemcpyAsync(ho + h0 * hout, d_o, nh * hout, cudaMemcpyDeviceToHost, hp->d2h) == cudaSuccess &&
+         cudaEventRecord(hp->stored[sl], hp->d2h) == cudaSuccess;
+  }
   const bool synced = cudaStreamSynchronize(hp->h2d) == cudaSuccess && cudaStreamSynchronize(st) == cudaSuccess &&
                       cudaStreamSynchronize(hp->d2h) == cudaSuccess;
   if (rc) return rc;
@@ -1673,9 +1739,14 @@ int akili_host_call(const char* op, const void* arg, const akili_ex_t* ex, akili
   Mode md;
   int rc = parse_ex(ex, &md);
   if (rc) return rc;
+  const std::string name(op);
+  if (name == "flash") {
+    FlashJob fj;
+    if ((rc = job_flash(static_cast<const flash_arg_t*>(arg), fj, false))) return rc;
+    return run_host_flash(fj, md, S(s));
+  }
   if (md.causal || md.batch != 1 || md.heads != 1) return AKILI_E_UNSUPPORTED;
   GemmJob j;
-  const std::string name(op);
   const bool kb2 = name.rfind("kb2_", 0) == 0;
   if (kb2 && (!md.in_f32 || !md.out_f32)) return AKILI_E_DTYPE;
 #define AKILI_HC(nm, T, build)                                          \

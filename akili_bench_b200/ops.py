@@ -233,14 +233,18 @@ def flash(q, k, v, softmax_scale=None, out=None, out_dtype=None, stream=None, ke
         B, H, (S, D) = 1, 1, q.shape
     else:
         B, H, S, D = q.shape
-    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=out_dtype or q.dtype)
+    o = out if out is not None else torch.empty(q.shape, device=q.device, dtype=out_dtype or q.dtype,
+                                                pin_memory=not q.is_cuda)
     arg = abi.FlashArg()
     arg.grid_dim[0] = (S + 7) // 8
     arg.block_dim[0] = 8
     arg.kernel_type = kernel_type
     arg.seq_len, arg.head_dim = S, D
     arg.block_size_r = arg.block_size_c = 8
-    arg.Q_addr, arg.K_addr, arg.V_addr, arg.O_addr = _addr(q), _addr(k), _addr(v), _addr(o)
+    if not return_stats:  # CPU tensors: the pipelined host call
+        arg.Q_addr, arg.K_addr, arg.V_addr, arg.O_addr = _a(q), _a(k), _a(v), _a(o)
+    else:
+        arg.Q_addr, arg.K_addr, arg.V_addr, arg.O_addr = _addr(q), _addr(k), _addr(v), _addr(o)
     extra = None
     if B * H != 1 or softmax_scale is not None or causal:
         extra = {"batch": B, "heads": H, "softmax_scale": float(softmax_scale or 0.0), "causal": int(causal)}

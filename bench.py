@@ -198,14 +198,14 @@ def workloads(torch, ops):
     W["flash"] = Workload(
         "flash", {"batch": B, "heads": H, "seq": S, "head_dim": D, "causal": False}, 4.0 * B * H * S * S * D,
         fl_make, lambda d, out, st: ops.flash(d["q"], d["k"], d["v"], softmax_scale=D ** -0.5, out=out, stream=st),
-        kernel="flash_fwd_kernel")
+        kernel="flash_fwd_kernel", host_call=True)
     # causal: query i sees keys 0..i, so the useful work is 2*B*H*S*(S+1)*D
     W["flash_causal"] = Workload(
         "flash_causal", {"batch": B, "heads": H, "seq": S, "head_dim": D, "causal": True},
         2.0 * B * H * S * (S + 1) * D, fl_make,
         lambda d, out, st: ops.flash(d["q"], d["k"], d["v"], softmax_scale=D ** -0.5, out=out, stream=st,
                                      causal=True),
-        kernel="flash_fwd_kernel")
+        kernel="flash_fwd_kernel", host_call=True)
 
     # The reference's unfused three-kernel attention (benchmarks/attention) at
     # the flash shape, fp16 on the tensor cores, S and P materialised in HBM:

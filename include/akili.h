@@ -440,8 +440,8 @@ const char* akili_strerror(int code);
  * `arg` pointer must point at that op's struct.  Returns AKILI_OK. */
 int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex, uint64_t* bytes);
 
-/* One kbt_* / kb2_* GEMM op on HOST buffers: every *_addr field of `arg`
- * (named by `op`, e.g. "kbt_gemm_add_relu") is a host address.  Replaces the
+/* One kbt_* / kb2_* GEMM op, or "flash", on HOST buffers: every *_addr field
+ * of `arg` (named by `op`, e.g. "kbt_gemm_add_relu") is a host address.  Replaces the
  * harness's whole device round trip (vx_copy_to_dev of the inputs, vx_start,
  * vx_ready_wait, vx_copy_from_dev of the output; e.g.
  * kbt_gemm_add_relu/main.cpp:98-124).  W and the vectors are copied once;
@@ -450,8 +450,10 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
  * streams (compute on `stream`).  Returns when the output is in host memory.
  * Page-locked host buffers (cudaHostAlloc / cudaHostRegister) let the copies
  * overlap; pageable ones work but serialise.  The scratch fields (norm, gate,
- * temp) are not written.  ex as for the op's _ex entry (batch, heads and
- * causal must be defaults); NULL = fp32 in and out.  The device buffers it
+ * temp) are not written.  ex as for the op's _ex entry (for the GEMM ops
+ * batch, heads and causal must be defaults); NULL = fp32 in and out.  Flash
+ * goes through in chunks of heads (flash/main.cpp:280-315 is its round
+ * trip).  The device buffers it
  * stages through (W and the vectors, three row-chunk slots) are kept per
  * device, grow-only, for later calls until the process exits; calls on one
  * device are serialised by a lock. */

@@ -94,3 +94,26 @@ def test_swiglu_and_kb2_host_calls(oracle):
     ops.host_call("kb2_gemm_add_relu", a2, torch.float32, torch.float32)
     ref = oracle.kb2_gemm_add_relu(x.numpy(), wg.numpy(), b.numpy(), M, N, K)
     assert np.abs(out.numpy() - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("B,H,S,D,causal", [(2, 5, 300, 64, False), (1, 12, 256, 128, True), (3, 1, 64, 32, False)])
+def test_flash_host_call_matches_device_call(B, H, S, D, causal):
+    """Flash on host tensors goes through in chunks of heads; each head runs
+    the same kernel as on the device path, so O is identical."""
+    g = torch.Generator(device="cuda").manual_seed(S + H)
+    q, k, v = (torch.randn((B, H, S, D), generator=g, device="cuda").half() for _ in range(3))
+    dev = ops.flash(q, k, v, softmax_scale=D ** -0.5, causal=causal).cpu()
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    got = ops.flash(hq, hk, hv, softmax_scale=D ** -0.5, causal=causal)
+    assert not got.is_cuda
+    assert torch.equal(got, dev)
+
+
+def test_flash_host_call_fp32_reference_semantics():
+    """The plain fp32 form (one unscaled head, pageable buffers)."""
+    S, D = 200, 16
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn((S, D), generator=g) for _ in range(3))
+    dev = ops.flash(q.cuda(), k.cuda(), v.cuda()).cpu()
+    got = ops.flash(q, k, v)
+    assert torch.equal(got, dev)
