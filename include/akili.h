@@ -444,7 +444,7 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
  * of `arg` (named by `op`, e.g. "kbt_gemm_add_relu") is a host address.  Replaces the
  * harness's whole device round trip (vx_copy_to_dev of the inputs, vx_start,
  * vx_ready_wait, vx_copy_from_dev of the output; e.g.
- * kbt_gemm_add_relu/main.cpp:98-124).  W and the vectors are copied once;
+ * kbt_gemm_add_relu/main.cpp:110-120).  W and the vectors are copied once;
  * the rows then go through in chunks with the host->device copy, the fused
  * GEMM and the device->host copy of successive chunks overlapped on three
  * streams (compute on `stream`).  Returns when the output is in host memory.
@@ -452,7 +452,7 @@ int akili_workspace_bytes(const char* op, const void* arg, const akili_ex_t* ex,
  * overlap; pageable ones work but serialise.  The scratch fields (norm, gate,
  * temp) are not written.  ex as for the op's _ex entry (for the GEMM ops
  * batch, heads and causal must be defaults); NULL = fp32 in and out.  Flash
- * goes through in chunks of heads (flash/main.cpp:280-315 is its round
+ * goes through in chunks of heads (flash/main.cpp:279-311 is its round
  * trip).  The device buffers it
  * stages through (W and the vectors, three row-chunk slots) are kept per
  * device, grow-only, for later calls until the process exits; calls on one
