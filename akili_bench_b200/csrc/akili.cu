@@ -333,12 +333,13 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
 
 // Persistent launch of the CTA-pair kernel: clusters of 2, as many pairs as
 // can be resident at once (cudaOccupancyMaxActiveClusters), at most one per tile.
-template <Epi E, typename OutT, bool BK>
+template <Epi E, typename OutT, bool BK, bool kSplit = false>
 int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1,
-                     const CUtensorMap& tmC, const EpiArgs& ea, cudaStream_t st) {
+                     const CUtensorMap& tmC, const CUtensorMap& tmAlo, const CUtensorMap& tmB0lo,
+                     const CUtensorMap& tmB1lo, const EpiArgs& ea, cudaStream_t st) {
   constexpr int BN = epi_bn(E);
-  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT));
-  auto kern = gemm_pair_kernel<E, OutT, BK>;
+  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT), kSplit);
+  auto kern = gemm_pair_kernel<E, OutT, BK, kSplit>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -376,7 +377,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
   const int tiles = ((ea.M + 2 * kBM - 1) / (2 * kBM)) * ((ea.N + BN - 1) / BN);
   const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
   cfg.gridDim = dim3(2 * pairs);
-  if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, ea) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) != cudaSuccess) {
     cudaGetLastError();
     return AKILI_E_LAUNCH;
   }
@@ -391,8 +392,8 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   const uint64_t M = j.M, N = j.N, K = j.K;
   bool ok = map2d(&tmA, jb.A, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, M, K * 2, 64, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   // CTA pairs (two SMs per 256-row tile) whenever M fills more than one 128-row
-  // block; the split (fp32) mode runs on the single-CTA kernel only.
-  const bool pair = !kSplit && M > static_cast<uint64_t>(kBM);
+  // block, in the split (fp32) mode too.
+  const bool pair = M > static_cast<uint64_t>(kBM);
   if (BK) {
     ok = ok && map2d(&tmB0, jb.B0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, K, N, K * 2, 64, pair ? BN / 2 : BN,
                      CU_TENSOR_MAP_SWIZZLE_128B);
@@ -430,18 +431,19 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.K = static_cast<int>(K);
   ea.num_n_tiles = static_cast<int>(2 * ((N + BN - 1) / BN));  // statistics slots: two per tile
 
-  if (pair) return launch_gemm_pair<E, OutT, BK>(di, tmA, tmB0, tmB1, tmC, ea, st);
   // the lo parts of the split mode: the same boxes over the lo copies
   CUtensorMap tmAlo = tmA, tmB0lo = tmB0, tmB1lo = tmB1;
   if constexpr (kSplit) {
     constexpr auto kF16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     constexpr auto kSw = CU_TENSOR_MAP_SWIZZLE_128B;
     ok = map2d(&tmAlo, jb.Alo, kF16, K, M, K * 2, 64, kBM, kSw);
-    if (BK) ok = ok && map2d(&tmB0lo, jb.B0lo, kF16, K, N, K * 2, 64, BN, kSw);
+    if (BK) ok = ok && map2d(&tmB0lo, jb.B0lo, kF16, K, N, K * 2, 64, pair ? BN / 2 : BN, kSw);
     else ok = ok && map2d(&tmB0lo, jb.B0lo, kF16, N, K, N * 2, 64, 64, kSw);
     if (epi_dual(E)) ok = ok && map2d(&tmB1lo, jb.B1lo, kF16, N, K, N * 2, 64, 64, kSw);
     if (!ok) return AKILI_E_LAUNCH;
   }
+  if (pair)
+    return launch_gemm_pair<E, OutT, BK, kSplit>(di, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea, st);
   const int smem = gemm_smem_bytes(kStore, sizeof(OutT), kSplit);
   static std::mutex mu;
   static std::map<int, bool> attr_done;

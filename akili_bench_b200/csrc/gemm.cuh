@@ -544,21 +544,27 @@ namespace akili {
 // ---------------------------------------------------------------------------
 constexpr int kPairThreads = 320;  // TMA, MMA, 8 epilogue warps (two per TMEM lane quarter)
 constexpr int kPairStageBytes = kATileBytes + kBTileBytes / 2;  // 16 KB A + 16 KB half of B
-// Ring depth: 6 slots, 5 when the two epilogue groups stage fp32 output.
-__host__ __device__ constexpr int pair_stages(bool stores, int out_bytes) { return stores && out_bytes == 4 ? 5 : 6; }
+// Split mode (fp32 operands as fp16 hi + lo) stages [A_hi][B_hi][A_lo][B_lo].
+__host__ __device__ constexpr int pair_stage_bytes(bool split) { return split ? 2 * kPairStageBytes : kPairStageBytes; }
+// Ring depth: 6 slots, 5 when the two epilogue groups stage fp32 output;
+// split mode 3 (2 with fp32 staging).
+__host__ __device__ constexpr int pair_stages(bool stores, int out_bytes, bool split = false) {
+  return split ? (stores && out_bytes == 4 ? 2 : 3) : (stores && out_bytes == 4 ? 5 : 6);
+}
 
-__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes) {
-  int s = pair_stages(stores, out_bytes) * kPairStageBytes;
+__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes, bool split = false) {
+  int s = pair_stages(stores, out_bytes, split) * pair_stage_bytes(split);
   if (stores) s += 2 * 2 * kBM * 32 * out_bytes;
   s += 256 + 1024;
   return s;
 }
 
-template <Epi E, typename OutT, bool kBKMajor>
+template <Epi E, typename OutT, bool kBKMajor, bool kSplit = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                      const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmC,
-                     const EpiArgs ea) {
+                     const __grid_constant__ CUtensorMap tmAlo, const __grid_constant__ CUtensorMap tmB0lo,
+                     const __grid_constant__ CUtensorMap tmB1lo, const EpiArgs ea) {
   constexpr bool kDual = epi_dual(E);
   constexpr bool kStore = epi_stores(E);
   constexpr int kStats = epi_stats(E);
@@ -566,12 +572,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   constexpr int BNH = BN / 2;     // B columns this CTA loads (dual: BN columns of its operand)
   constexpr int kOutBytes = sizeof(OutT);
   constexpr int kStageOut = kBM * 32 * kOutBytes;
-  constexpr int kPairStages = pair_stages(kStore, kOutBytes);
+  constexpr int kPairStages = pair_stages(kStore, kOutBytes, kSplit);
+  constexpr int kSB = pair_stage_bytes(kSplit);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint8_t* staging = ring + kPairStages * kPairStageBytes;  // [group][2 ping-pong buffers]
+  uint8_t* staging = ring + kPairStages * kSB;  // [group][2 ping-pong buffers]
   uint64_t* bars = reinterpret_cast<uint64_t*>(staging + (kStore ? 2 * 2 * kStageOut : 0));
   uint64_t* full = bars;                       // [stages], used in the even CTA
   uint64_t* empty = bars + kPairStages;        // [stages]
@@ -637,10 +644,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int kb = 0; kb < num_kb && ok; ++kb) {
           ok = mbar_wait_cluster(&empty[stage], phase ^ 1, kSiteProducerEmpty);
           if (!ok) break;
-          uint8_t* sa = ring + stage * kPairStageBytes;
+          uint8_t* sa = ring + stage * kSB;
           uint8_t* sb = sa + kATileBytes;
           const uint32_t fb = full_c + stage * 8;
-          if (leader) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
+          if (leader) mbar_expect_tx(&full[stage], 2 * kSB);
           tma_load_2d_pair(sa, &tmA, fb, kb * kBK, row0);
           if constexpr (kBKMajor) {
             tma_load_2d_pair(sb, &tmB0, fb, kb * kBK, col0);
@@ -654,6 +661,21 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           } else {
             tma_load_2d_pair(sb, &tmB0, fb, col0, kb * kBK);
             tma_load_2d_pair(sb + 8192, &tmB0, fb, col0 + 64, kb * kBK);
+          }
+          if constexpr (kSplit) {  // the lo parts, same boxes, behind the hi parts
+            uint8_t* sal = sa + kPairStageBytes;
+            uint8_t* sbl = sal + kATileBytes;
+            tma_load_2d_pair(sal, &tmAlo, fb, kb * kBK, row0);
+            if constexpr (kBKMajor) {
+              tma_load_2d_pair(sbl, &tmB0lo, fb, kb * kBK, col0);
+            } else if constexpr (kDual) {
+              const CUtensorMap* tbl = leader ? &tmB0lo : &tmB1lo;
+              tma_load_2d_pair(sbl, tbl, fb, n_blk * BN, kb * kBK);
+              tma_load_2d_pair(sbl + 8192, tbl, fb, n_blk * BN + 64, kb * kBK);
+            } else {
+              tma_load_2d_pair(sbl, &tmB0lo, fb, col0, kb * kBK);
+              tma_load_2d_pair(sbl + 8192, &tmB0lo, fb, col0 + 64, kb * kBK);
+            }
           }
           if (++stage == kPairStages) {
             stage = 0;
@@ -685,16 +707,19 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           ok = mbar_wait_cluster(&full[stage], phase, kSiteMmaFull);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t sa = smem_u32(ring + stage * kPairStageBytes);
+          const uint32_t sa = smem_u32(ring + stage * kSB);
           const uint32_t sb = sa + kATileBytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
             const uint32_t accum = (kb | k) != 0;
-            if constexpr (kBKMajor) {
-              umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
-            } else {
-              umma_f16_ss_pair(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+            const uint64_t bd = kBKMajor ? make_sdesc(sb + k * 32, 16, 1024, kSw128)
+                                         : make_sdesc(sb + k * 2048, 8192, 1024, kSw128);
+            umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
+            if constexpr (kSplit) {  // + A_hi.B_lo + A_lo.B_hi (lo parts kPairStageBytes behind)
+              constexpr uint64_t lo = kPairStageBytes >> 4;
+              umma_f16_ss_pair(d_tmem, ad, bd + lo, idesc, 1);
+              umma_f16_ss_pair(d_tmem, ad + lo, bd, idesc, 1);
             }
           }
           umma_commit_pair(&empty[stage], 0x3);
