@@ -34,7 +34,10 @@ constexpr int kBTileBytes = 256 * kBK * 2;       // 32 KB (256 columns, or 2 x 1
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kAccCols = 256;     // TMEM columns per accumulator buffer
 constexpr int kTmemCols = 512;
-constexpr int kGroupM = 16;       // tile raster: row-blocks per group
+#ifndef AKILI_GROUP_M
+#define AKILI_GROUP_M 16
+#endif
+constexpr int kGroupM = AKILI_GROUP_M;  // tile raster: row-blocks per group
 
 enum class Epi : int {
   kPlain = 0,        // C = acc                                   (kbt_sgemm)
