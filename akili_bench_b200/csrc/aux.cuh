@@ -228,46 +228,109 @@ __device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, flo
   n = ntot;
 }
 
+// Rows per CTA of the LayerNorm finaliser.  Each pass keeps 8 rows (fp16) or
+// 4 rows (fp32) of 16-byte loads in flight per thread, held raw, so that
+// four CTAs (fp16; three for fp32) fit per SM and about 128 KB per SM is in
+// flight.
+#ifndef AKILI_LN_BLOCK_ROWS
+#define AKILI_LN_BLOCK_ROWS 16
+#endif
+constexpr int kLnBlockRows = AKILI_LN_BLOCK_ROWS;
+constexpr int kLnThreads = 256;
+constexpr int kLnCols = kLnThreads * 8;  // columns per CTA
+template <typename T>
+constexpr int ln_rows_in_flight() { return sizeof(T) == 2 ? 8 : 4; }
+static_assert(kLnBlockRows % 8 == 0, "whole passes");
+
+// Eight consecutive values of T, as loaded (16 or 32 bytes).
+template <typename T>
+struct Raw8 {
+  uint4 v[sizeof(T) / 2];
+};
+template <typename T>
+__device__ __forceinline__ void load_raw8(const T* p, Raw8<T>& r) {
+#pragma unroll
+  for (int k = 0; k < static_cast<int>(sizeof(T) / 2); ++k) r.v[k] = reinterpret_cast<const uint4*>(p)[k];
+}
+template <typename T>
+__device__ __forceinline__ void raw8_to_float(const Raw8<T>& r, float (&f)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    const __half2* h = reinterpret_cast<const __half2*>(&r.v[0]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  } else {
+    const float* x = reinterpret_cast<const float*>(&r.v[0]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = x[i];
+  }
+}
+
 // In-place LayerNorm of the pre-normalised rows y = x.W + b written by the
 // GEMM epilogue.  Per-tile (mean, M2) partials over `tile_n` columns are
 // (half tiles; a slot past the row's end is empty) merged with Chan et al.'s
 // pairwise formula; var = M2 / N (biased, as
 // benchmarks/kbt_gemm_layernorm/main.cpp:159-166); inv_std = 1/sqrtf(var+eps).
-// One warp per row, 16-byte accesses, four row chunks in flight per lane.
+// A CTA owns kLnBlockRows rows x kLnCols columns (grid: row blocks x column
+// blocks).  Its warps first merge the rows' partials (a warp per row, a lane
+// per partial, a butterfly) into shared memory; then each thread keeps gamma
+// and beta of its 8 columns in registers and streams the rows, 16-byte
+// accesses that a warp makes contiguous, ln_rows_in_flight<T>() per pass.
 template <typename T>
-__global__ void layernorm_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws,
-                                          const float* __restrict__ ln_w, const float* __restrict__ ln_b, int M,
-                                          int N, int ntiles, int tile_n, float eps) {
-  const int warps = blockDim.x >> 5;
+__global__ void __launch_bounds__(kLnThreads, sizeof(T) == 2 ? 4 : 3)
+    layernorm_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws, const float* __restrict__ ln_w,
+                              const float* __restrict__ ln_b, int M, int N, int ntiles, int tile_n, float eps) {
+  __shared__ float s_mean[kLnBlockRows], s_inv[kLnBlockRows];
+  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
-    float n = 0.0f, mean = 0.0f, m2 = 0.0f;
+  const int row0 = blockIdx.x * kLnBlockRows;
+  for (int r = warp; r < kLnBlockRows; r += kLnThreads / 32) {
+    const int row = min(row0 + r, M - 1);
+    float n = 0.0f, mu = 0.0f, m2 = 0.0f;
     for (int t = lane; t < ntiles; t += 32)
-      chan_merge(n, mean, m2, static_cast<float>(max(0, min(tile_n, N - t * tile_n))), ws[static_cast<size_t>(t) * M + row],
-                 ws[static_cast<size_t>(ntiles + t) * M + row]);
+      chan_merge(n, mu, m2, static_cast<float>(max(0, min(tile_n, N - t * tile_n))),
+                 ws[static_cast<size_t>(t) * M + row], ws[static_cast<size_t>(ntiles + t) * M + row]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float nb = __shfl_xor_sync(0xffffffffu, n, o);
-      const float mb = __shfl_xor_sync(0xffffffffu, mean, o);
+      const float mb = __shfl_xor_sync(0xffffffffu, mu, o);
       const float m2b = __shfl_xor_sync(0xffffffffu, m2, o);
-      chan_merge(n, mean, m2, nb, mb, m2b);
+      chan_merge(n, mu, m2, nb, mb, m2b);
     }
-    const float var = m2 / static_cast<float>(N);
-    const float inv_std = 1.0f / sqrtf(var + eps);
-    T* cr = c + static_cast<size_t>(row) * N;
-#pragma unroll 4
-    for (int j = lane * 8; j < N; j += 256) {
-      float f[8];
-      load8(cr + j, f);
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(ln_w + j));
-      const float4 g1 = __ldg(reinterpret_cast<const float4*>(ln_w + j) + 1);
-      const float4 b0 = __ldg(reinterpret_cast<const float4*>(ln_b + j));
-      const float4 b1 = __ldg(reinterpret_cast<const float4*>(ln_b + j) + 1);
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    if (lane == 0) {
+      s_mean[r] = mu;
+      s_inv[r] = 1.0f / sqrtf(m2 / static_cast<float>(N) + eps);
+    }
+  }
+  __syncthreads();
+  const int j = blockIdx.y * kLnCols + threadIdx.x * 8;
+  if (j >= N) return;  // N % 8 == 0: a thread's 8 columns are all in or all out
+  const float4 g0 = __ldg(reinterpret_cast<const float4*>(ln_w + j));
+  const float4 g1 = __ldg(reinterpret_cast<const float4*>(ln_w + j) + 1);
+  const float4 b0 = __ldg(reinterpret_cast<const float4*>(ln_b + j));
+  const float4 b1 = __ldg(reinterpret_cast<const float4*>(ln_b + j) + 1);
+  const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  constexpr int kR = ln_rows_in_flight<T>();
+  const int nrows = min(kLnBlockRows, M - row0);
+  for (int r0 = 0; r0 < nrows; r0 += kR) {
+    Raw8<T> raw[kR];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = ((f[i] - mean) * inv_std) * g[i] + b[i];
-      store8(cr + j, f);
+    for (int q = 0; q < kR; ++q)
+      if (r0 + q < nrows) load_raw8(c + static_cast<size_t>(row0 + r0 + q) * N + j, raw[q]);
+#pragma unroll
+    for (int q = 0; q < kR; ++q) {
+      if (r0 + q < nrows) {
+        float f[8];
+        raw8_to_float(raw[q], f);
+        const float mean = s_mean[r0 + q], inv_std = s_inv[r0 + q];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = ((f[i] - mean) * inv_std) * g[i] + b[i];
+        store8(c + static_cast<size_t>(row0 + r0 + q) * N + j, f);
+      }
     }
   }
 }
