@@ -596,6 +596,7 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
   // 3. finalisers
   const int M = static_cast<int>(j.M), N = static_cast<int>(j.N);
   const int nt = 2 * ((N + epi_bn(j.epi) - 1) / epi_bn(j.epi));  // statistics slots (half tiles)
+  const dim3 fin_grid((M + kFinRows - 1) / kFinRows, (N + kFinCols - 1) / kFinCols);  // LayerNorm finaliser
   switch (j.epi) {
     case Epi::kRowSumHalf:
     case Epi::kRowSumBias:
@@ -614,16 +615,14 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
         finalize_lse_mish_kernel<__half><<<grid_for(di, M, 256), 256, 0, st>>>(
             jb.stats, static_cast<__half*>(j.C), M, nt);
       return launch_status();
-    case Epi::kLnPre: {
-      const dim3 grid((M + kLnBlockRows - 1) / kLnBlockRows, (N + kLnCols - 1) / kLnCols);
+    case Epi::kLnPre:
       if (md.out_f32)
-        layernorm_finalize_kernel<float><<<grid, kLnThreads, 0, st>>>(
+        layernorm_finalize_kernel<float><<<fin_grid, kFinThreads, 0, st>>>(
             static_cast<float*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi) / 2, j.eps);
       else
-        layernorm_finalize_kernel<__half><<<grid, kLnThreads, 0, st>>>(
+        layernorm_finalize_kernel<__half><<<fin_grid, kFinThreads, 0, st>>>(
             static_cast<__half*>(j.C), jb.stats, j.ln_w, j.ln_b, M, N, nt, epi_bn(j.epi) / 2, j.eps);
       return launch_status();
-    }
     case Epi::kSoftmaxPre:
       if (md.out_f32)
         softmax_finalize_kernel<float><<<grid_for(di, M, 8, 8), 256, 0, st>>>(static_cast<float*>(j.C), jb.stats,

@@ -228,19 +228,22 @@ __device__ __forceinline__ void chan_merge(float& n, float& mean, float& m2, flo
   n = ntot;
 }
 
-// Rows per CTA of the LayerNorm finaliser.  Each pass keeps 8 rows (fp16) or
-// 4 rows (fp32) of 16-byte loads in flight per thread, held raw, so that
-// four CTAs (fp16; three for fp32) fit per SM and about 128 KB per SM is in
-// flight.
-#ifndef AKILI_LN_BLOCK_ROWS
-#define AKILI_LN_BLOCK_ROWS 16
+// The in-place LayerNorm finaliser is run by CTAs that each own
+// kFinRows rows x kFinCols columns of the output (grid: row blocks x column
+// blocks).  The CTA's warps first merge its rows' statistics into shared
+// memory; then each thread owns 8 columns and streams the rows, 16-byte
+// accesses that a warp makes contiguous.  Each pass keeps 8 rows (fp16) or 4
+// rows (fp32) of loads in flight per thread, held raw, so that four CTAs
+// (fp16; three for fp32) fit per SM and about 128 KB per SM is in flight.
+#ifndef AKILI_FIN_ROWS
+#define AKILI_FIN_ROWS 16
 #endif
-constexpr int kLnBlockRows = AKILI_LN_BLOCK_ROWS;
-constexpr int kLnThreads = 256;
-constexpr int kLnCols = kLnThreads * 8;  // columns per CTA
+constexpr int kFinRows = AKILI_FIN_ROWS;
+constexpr int kFinThreads = 256;
+constexpr int kFinCols = kFinThreads * 8;  // columns per CTA
 template <typename T>
-constexpr int ln_rows_in_flight() { return sizeof(T) == 2 ? 8 : 4; }
-static_assert(kLnBlockRows % 8 == 0, "whole passes");
+constexpr int fin_rows_in_flight() { return sizeof(T) == 2 ? 8 : 4; }
+static_assert(kFinRows % 8 == 0, "whole passes");
 
 // Eight consecutive values of T, as loaded (16 or 32 bytes).
 template <typename T>
@@ -269,25 +272,44 @@ __device__ __forceinline__ void raw8_to_float(const Raw8<T>& r, float (&f)[8]) {
   }
 }
 
+// Rows [row0, row0 + nrows) x columns [j, j + 8) of c, in place: f = op(r, f)
+// with r the row within the block.
+template <typename T, typename Op>
+__device__ __forceinline__ void stream_block_rows(T* __restrict__ c, int N, int row0, int nrows, int j, Op op) {
+  constexpr int kR = fin_rows_in_flight<T>();
+  for (int r0 = 0; r0 < nrows; r0 += kR) {
+    Raw8<T> raw[kR];
+#pragma unroll
+    for (int q = 0; q < kR; ++q)
+      if (r0 + q < nrows) load_raw8(c + static_cast<size_t>(row0 + r0 + q) * N + j, raw[q]);
+#pragma unroll
+    for (int q = 0; q < kR; ++q) {
+      if (r0 + q < nrows) {
+        float f[8];
+        raw8_to_float(raw[q], f);
+        op(r0 + q, f);
+        store8(c + static_cast<size_t>(row0 + r0 + q) * N + j, f);
+      }
+    }
+  }
+}
+
 // In-place LayerNorm of the pre-normalised rows y = x.W + b written by the
 // GEMM epilogue.  Per-tile (mean, M2) partials over `tile_n` columns are
 // (half tiles; a slot past the row's end is empty) merged with Chan et al.'s
-// pairwise formula; var = M2 / N (biased, as
-// benchmarks/kbt_gemm_layernorm/main.cpp:159-166); inv_std = 1/sqrtf(var+eps).
-// A CTA owns kLnBlockRows rows x kLnCols columns (grid: row blocks x column
-// blocks).  Its warps first merge the rows' partials (a warp per row, a lane
-// per partial, a butterfly) into shared memory; then each thread keeps gamma
-// and beta of its 8 columns in registers and streams the rows, 16-byte
-// accesses that a warp makes contiguous, ln_rows_in_flight<T>() per pass.
+// pairwise formula (a warp per row, a lane per partial, a butterfly);
+// var = M2 / N (biased, as benchmarks/kbt_gemm_layernorm/main.cpp:159-166);
+// inv_std = 1/sqrtf(var+eps).  Gamma and beta of a thread's 8 columns stay in
+// registers.
 template <typename T>
-__global__ void __launch_bounds__(kLnThreads, sizeof(T) == 2 ? 4 : 3)
+__global__ void __launch_bounds__(kFinThreads, sizeof(T) == 2 ? 4 : 3)
     layernorm_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws, const float* __restrict__ ln_w,
                               const float* __restrict__ ln_b, int M, int N, int ntiles, int tile_n, float eps) {
-  __shared__ float s_mean[kLnBlockRows], s_inv[kLnBlockRows];
+  __shared__ float s_mean[kFinRows], s_inv[kFinRows];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kLnBlockRows;
-  for (int r = warp; r < kLnBlockRows; r += kLnThreads / 32) {
+  const int row0 = blockIdx.x * kFinRows;
+  for (int r = warp; r < kFinRows; r += kFinThreads / 32) {
     const int row = min(row0 + r, M - 1);
     float n = 0.0f, mu = 0.0f, m2 = 0.0f;
     for (int t = lane; t < ntiles; t += 32)
@@ -306,7 +328,7 @@ __global__ void __launch_bounds__(kLnThreads, sizeof(T) == 2 ? 4 : 3)
     }
   }
   __syncthreads();
-  const int j = blockIdx.y * kLnCols + threadIdx.x * 8;
+  const int j = blockIdx.y * kFinCols + threadIdx.x * 8;
   if (j >= N) return;  // N % 8 == 0: a thread's 8 columns are all in or all out
   const float4 g0 = __ldg(reinterpret_cast<const float4*>(ln_w + j));
   const float4 g1 = __ldg(reinterpret_cast<const float4*>(ln_w + j) + 1);
@@ -314,25 +336,11 @@ __global__ void __launch_bounds__(kLnThreads, sizeof(T) == 2 ? 4 : 3)
   const float4 b1 = __ldg(reinterpret_cast<const float4*>(ln_b + j) + 1);
   const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
   const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-  constexpr int kR = ln_rows_in_flight<T>();
-  const int nrows = min(kLnBlockRows, M - row0);
-  for (int r0 = 0; r0 < nrows; r0 += kR) {
-    Raw8<T> raw[kR];
+  stream_block_rows(c, N, row0, min(kFinRows, M - row0), j, [&](int r, float (&f)[8]) {
+    const float mean = s_mean[r], inv_std = s_inv[r];
 #pragma unroll
-    for (int q = 0; q < kR; ++q)
-      if (r0 + q < nrows) load_raw8(c + static_cast<size_t>(row0 + r0 + q) * N + j, raw[q]);
-#pragma unroll
-    for (int q = 0; q < kR; ++q) {
-      if (r0 + q < nrows) {
-        float f[8];
-        raw8_to_float(raw[q], f);
-        const float mean = s_mean[r0 + q], inv_std = s_inv[r0 + q];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = ((f[i] - mean) * inv_std) * g[i] + b[i];
-        store8(c + static_cast<size_t>(row0 + r0 + q) * N + j, f);
-      }
-    }
-  }
+    for (int i = 0; i < 8; ++i) f[i] = ((f[i] - mean) * inv_std) * g[i] + b[i];
+  });
 }
 
 // Merge of (max, sum of exp2) partials in the log2 domain; -inf max = empty.
@@ -365,7 +373,9 @@ __device__ __forceinline__ void row_lse2(const float* __restrict__ ws, int M, in
 
 // In-place softmax of the rows y written by the GEMM epilogue, from the
 // per-tile (max, sumexp) partials in the log2 domain:
-// out = exp2(y * log2 e - m2) * (1 / l).
+// out = exp2(y * log2 e - m2) * (1 / l).  One warp per row.  (The
+// column-owning form of the LayerNorm finaliser measured 2% slower here: with
+// no per-column operands the row walk is not L1-bound.)
 template <typename T>
 __global__ void softmax_finalize_kernel(T* __restrict__ c, const float* __restrict__ ws, int M, int N,
                                         int ntiles) {
