@@ -124,6 +124,12 @@ __global__ void __maxnreg__(96)
   // them the same way); keys after a row's own index are masked per row.
   const int nkv_all = (N + kFlashBN - 1) / kFlashBN;
   const int nkv = fa.causal ? min(nkv_all, (m0 + kFlashBM * kFlashQTiles + kFlashBN - 1) / kFlashBN) : nkv_all;
+  // Under causal masking Q tile 0 (rows m0 .. m0 + 127) sees no key past
+  // m0 + 127, so unless the sequence end cuts the range its last key block is
+  // fully masked.  That block is skipped for tile 0: no S or P.V MMAs and no
+  // softmax pass (its P would be all zeros, so the result is unchanged).
+  const int nkv_t0 = fa.causal ? min(nkv_all, (m0 + kFlashBM + kFlashBN - 1) / kFlashBN) : nkv_all;
+  static_assert(kFlashQTiles == 2, "two Q tiles per CTA");
   const int bh = blockIdx.y;
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -206,13 +212,14 @@ __global__ void __maxnreg__(96)
         const int jj = j - 1;  // the block whose P.V this iteration issues
         // K_j, V_j-1 and P_0,j-1 in one wait; P_1,j-1 before its P.V.
         ok = mbar_wait3(j < nkv ? &k_full[st] : nullptr, (j >> 1) & 1, j >= 1 ? &v_full[jj & 1] : nullptr,
-                        (jj >> 1) & 1, j >= 1 ? &p_full[0] : nullptr, jj & 1, kSiteFlashKV);
+                        (jj >> 1) & 1, (j >= 1 && j <= nkv_t0) ? &p_full[0] : nullptr, jj & 1, kSiteFlashKV);
         const uint64_t kd = kd0 + static_cast<uint64_t>((st * L::kKV) >> 4);
         const uint64_t vd = vd0 + static_cast<uint64_t>(((jj & 1) * L::kKV) >> 4);
 #pragma unroll
         for (int t = 0; t < kFlashQTiles; ++t) {
           if (!ok) break;
-          if (j >= 1) {
+          const int nkv_t = t == 0 ? nkv_t0 : nkv;
+          if (j >= 1 && j <= nkv_t) {
             // O_t += P_t,j-1 . V_j-1
             if (t > 0) ok = mbar_wait(&p_full[t], jj & 1, kSiteFlashP);
             if (!ok) break;
@@ -223,9 +230,12 @@ __global__ void __maxnreg__(96)
             for (int k = 0; k < kFlashBN / 16; ++k)
               umma_f16_ts(o_tmem, p_tmem + k * 8, vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_o,
                           (jj | k) != 0);
-            if (j == nkv) umma_commit(&o_done[t]);
           }
-          if (j < nkv) {
+          // O_t is final once every MMA issued so far completes; both tiles
+          // commit in the last iteration, when the K/V rings that the output
+          // staging reuses are drained.
+          if (j == nkv) umma_commit(&o_done[t]);
+          if (j < nkv_t) {
             // S_t,j = Q_t . K_j^T
             tc_fence_after();
             const uint64_t qd = qd0 + static_cast<uint64_t>((t * L::kQ) >> 4);
@@ -278,8 +288,9 @@ __global__ void __maxnreg__(96)
     float m_true = -INFINITY;  // the row's exact running max (m_use may lag it by the rescale threshold)
     float l = 0.0f;            // this half's share of the row sum
     const int qrow = m0 + grp * kFlashBM + r;
+    const int nkv_my = grp == 0 ? nkv_t0 : nkv;  // this tile's key blocks
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
+    for (int j = 0; j < nkv_my; ++j) {
       if (!mbar_wait(&s_full[grp], j & 1, kSiteFlashS)) abort_flag[2 * grp + (j & 1)] = 1;
       tc_fence_after();
       const int kv0 = j * kFlashBN + half * 64;
@@ -367,10 +378,10 @@ __global__ void __maxnreg__(96)
       l = l * alpha + rsum;
       m_use = m_new;
     }
-    if (ok && nkv >= 1) {
-      // The row sum: the two halves' shares (slot of parity nkv, last read
+    if (ok && nkv_my >= 1) {
+      // The row sum: the two halves' shares (slot of parity nkv_my, last read
       // two blocks ago).
-      float* xs = xchg + ((nkv & 1) * kFlashQTiles + grp) * (2 * kFlashBM);
+      float* xs = xchg + ((nkv_my & 1) * kFlashQTiles + grp) * (2 * kFlashBM);
       xs[half * kFlashBM + r] = l;
       named_bar_sync(tile_bar, 256);
       const float lt = l + xs[(half ^ 1) * kFlashBM + r];
@@ -380,9 +391,9 @@ __global__ void __maxnreg__(96)
         fa.m_out[o] = m_true * 0.6931471805599453f;
         fa.l_out[o] = lt * exp2f(m_use - m_true);
       }
-      if (!mbar_wait(&o_done[grp], 0, kSiteFlashPV)) abort_flag[2 * grp + (nkv & 1)] = 1;
+      if (!mbar_wait(&o_done[grp], 0, kSiteFlashPV)) abort_flag[2 * grp + (nkv_my & 1)] = 1;
       named_bar_sync(tile_bar, 256);
-      if (!abort_flag[2 * grp + (nkv & 1)]) {
+      if (!abort_flag[2 * grp + (nkv_my & 1)]) {
         tc_fence_after();
         const float inv_l = 1.0f / lt;
         // Staging: each (tile, half) takes its own span of the drained K/V
