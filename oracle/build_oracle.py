@@ -25,9 +25,14 @@ TEST INFRASTRUCTURE.  Outputs:
   the product's ``libakili_vxmath.so`` in place of vxmath.cpp.
   ``llama2_logits`` is ``oracle/llama2/llama2_logits.cpp``, a driver that
   compiles llama.cpp with TESTING and writes each position's logits.
+* ``oracle/_ref/libdao_flash_ref.so`` — the CuPBoP causal flash benchmark
+  ``benchmarks/cupbop_dao_flash/dao_flash_cupbop.cu`` (plain CUDA: its CPU
+  gold ``attention_cpu`` and its kernel ``dao_flash_fwd``), compiled by nvcc
+  through ``oracle/shim/dao_flash_ref.cu``, which gives both C entry points.
+  It pins the causal flash oracle and the m / l row statistics.
 
-The reference sources are read in place (``--ref``, default
-/root/reference); nothing is copied.  ``oracle/_ref/`` is git-ignored and
+The reference sources are read in place (``--ref``, or the
+``AKILI_REFERENCE_ROOT`` environment variable); nothing is copied.  ``oracle/_ref/`` is git-ignored and
 travels with the working tree like the other built artefacts.
 """
 from __future__ import annotations
@@ -176,23 +181,57 @@ def build_llama2_binaries(ref_root: str, libdir: str, force: bool = False) -> li
     return built
 
 
+def build_dao_flash_ref(ref_root: str, force: bool = False) -> str:
+    """benchmarks/cupbop_dao_flash/dao_flash_cupbop.cu, unchanged, as a
+    shared library with C entry points (oracle/shim/dao_flash_ref.cu)."""
+    src_dir = os.path.join(ref_root, "benchmarks", "cupbop_dao_flash")
+    wrapper = os.path.join(HERE, "shim", "dao_flash_ref.cu")
+    out = os.path.join(REF_OUT, "libdao_flash_ref.so")
+    os.makedirs(REF_OUT, exist_ok=True)
+    if force or not _newer(out, [wrapper, os.path.join(src_dir, "dao_flash_cupbop.cu")]):
+        nvcc = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+        if not os.path.exists(nvcc):
+            nvcc = "nvcc"
+        # host code: the reference's -O2 and, like the oracle, no FMA contraction
+        _run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-shared",
+              "-Xcompiler", "-fPIC,-ffp-contract=off", "-I", src_dir, "-Dmain=akili_ref_dao_main", wrapper,
+              "-o", out])
+    return out
+
+
+# Where this recipe reads the reference tree when neither --ref nor
+# $AKILI_REFERENCE_ROOT names one: the read-only checkout of the build
+# container.  GPU boxes have no reference tree and use the prebuilt files.
+DEFAULT_REFERENCE_ROOT = "/root/reference"
+
+
+def reference_root(arg: str | None = None) -> str | None:
+    """The reference tree: the argument, else $AKILI_REFERENCE_ROOT, else
+    DEFAULT_REFERENCE_ROOT; None when that is not a directory."""
+    ref = arg or os.environ.get("AKILI_REFERENCE_ROOT") or DEFAULT_REFERENCE_ROOT
+    return ref if os.path.isdir(ref) else None
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None,
+                    help="reference tree (default: $AKILI_REFERENCE_ROOT, else DEFAULT_REFERENCE_ROOT)")
     ap.add_argument("--libdir", default=os.path.join(ROOT, "akili_bench_b200"))
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     print(build_oracle_lib(a.force))
-    if os.path.isdir(a.ref):
-        for p in build_pin_binaries(a.ref, a.force):
+    ref = reference_root(a.ref)
+    if ref:
+        for p in build_pin_binaries(ref, a.force):
             print(p)
         if os.path.exists(os.path.join(a.libdir, "libakili_vortex.so")):
-            for p in build_b200_binaries(a.ref, a.libdir, a.force):
+            for p in build_b200_binaries(ref, a.libdir, a.force):
                 print(p)
-        for p in build_llama2_binaries(a.ref, a.libdir, a.force):
+        for p in build_llama2_binaries(ref, a.libdir, a.force):
             print(p)
+        print(build_dao_flash_ref(ref, a.force))
     else:
-        print(f"reference tree {a.ref} absent: pin binaries not rebuilt", file=sys.stderr)
+        print("no reference tree: pin binaries not rebuilt", file=sys.stderr)
     return 0
 
 

@@ -6,7 +6,8 @@
  * where each scalar is applied and the libm calls (expf, logf, tanhf, sqrtf)
  * follow the reference so that, compiled with the reference's host flags
  * (-O2, no fast-math, no FMA ISA), the outputs are bit-identical to it.
- * oracle/build_ref.sh proves that per op at several sizes.
+ * oracle/build_oracle.py builds the reference harnesses that prove that
+ * per op at several sizes.
  */
 #include "oracle.h"
 

@@ -8,7 +8,7 @@
  * __graft_entry__.smoke() and bench.py's CPU-baseline leg may load it.  The
  * product library never links it.
  *
- * Parity pin: oracle/build_ref.sh compiles each reference main.cpp unchanged
+ * Parity pin: oracle/build_oracle.py compiles each reference main.cpp unchanged
  * against a host-memory Vortex runtime whose "device" runs these functions
  * and a probe that turns the reference's own verify loop into an
  * exact-equality check; the binaries print PASSED! only when every output of

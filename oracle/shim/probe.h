@@ -1,6 +1,6 @@
 /*
  * probe.h — force-included (g++ -include) into an unchanged akili-bench
- * benchmarks/<bench>/main.cpp when oracle/build_ref.sh builds the oracle pin
+ * benchmarks/<bench>/main.cpp when oracle/build_oracle.py builds the oracle pin
  * and golden-vector capture binaries.  TEST INFRASTRUCTURE.
  *
  * In the reference harnesses `fabsf` / `std::fabs` appear only in the verify

@@ -6,6 +6,9 @@ batch x heads ([B, H, S, D] fp16) and the 1/sqrt(d) scale of the benchmark
 configuration.  Operands are fp16-rounded once so both sides see the same
 values.  Tolerance: max|err| <= 1e-2 * max|ref| and per-row cosine >= 0.9999.
 """
+import ctypes as C
+import os
+
 import numpy as np
 import pytest
 
@@ -144,3 +147,58 @@ def test_flash_causal_fp32_reference_semantics(oracle):
     assert_parity(got_o.cpu().numpy(), ref_o, what="flash causal fp32")
     np.testing.assert_allclose(got_m.cpu().numpy(), ref_m, rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(got_l.cpu().numpy(), ref_l, rtol=2e-3)
+
+
+# ---- the m / l statistics against the reference's own causal flash kernel ----
+
+DAO_LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                       "libdao_flash_ref.so")
+
+
+def _dao_lib():
+    if not os.path.exists(DAO_LIB):
+        pytest.skip("reference-built libdao_flash_ref.so not present (python oracle/build_oracle.py)")
+    return C.CDLL(DAO_LIB)
+
+
+def test_reference_dao_flash_kernel_passes_its_own_tests():
+    """The reference's CUDA kernel dao_flash_fwd, built unchanged from
+    cupbop_dao_flash/dao_flash_cupbop.cu, passes the reference's own eight
+    tests (its main(), :246-345) on this GPU before it serves as a pin."""
+    assert _dao_lib().akili_ref_dao_selftest() == 0
+
+
+# Bc = Br threads per block and N a multiple of Bc: the reference kernel's
+# own launch conditions (dao_flash_cupbop.cu:216-222), checked by the wrapper.
+@pytest.mark.parametrize("B,H,S,D,Bc", [(1, 1, 8, 8, 8), (1, 2, 64, 64, 16), (2, 2, 256, 128, 16),
+                                        (1, 1, 512, 64, 32), (1, 3, 136, 8, 8)])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_flash_stats_match_reference_kernel(oracle, B, H, S, D, Bc, causal):
+    """akili_flash_ml_ex's O, m and l against the m / l / O buffers of the
+    reference kernel dao_flash_fwd (online softmax over Bc-key tiles,
+    dao_flash_cupbop.cu:79-131: m = running max of the scaled scores, l =
+    sum exp(score - m) rescaled tile by tile), both on the same fp16-rounded
+    operands with the reference's scale 1/sqrt(d).  The oracle's m is the
+    same maximum, so it is checked against the reference kernel too."""
+    lib = _dao_lib()
+    rng = np.random.default_rng(S * 5 + D + causal)
+    q, k, v = f16(rng, (B, H, S, D)), f16(rng, (B, H, S, D)), f16(rng, (B, H, S, D))
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(D)))
+    ro, rm, rl = np.zeros_like(q), np.zeros((B, H, S), np.float32), np.zeros((B, H, S), np.float32)
+    f = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))  # noqa: E731
+    rc = lib.akili_ref_dao_flash_fwd(f(q), f(k), f(v), f(ro), f(rm), f(rl), B, H, S, D, Bc, C.c_float(scale),
+                                     causal)
+    assert rc == 0
+    got_o, got_m, got_l = ops.flash(dev(q, torch.float16), dev(k, torch.float16), dev(v, torch.float16),
+                                    softmax_scale=scale, out_dtype=torch.float32, causal=bool(causal),
+                                    return_stats=True)
+    assert ops.device_status() == 0
+    got_o = got_o.cpu().numpy()
+    for b in range(B):
+        for h in range(H):
+            assert_parity(got_o[b, h], ro[b, h], what=f"flash vs dao_flash_fwd b={b} h={h}")
+    np.testing.assert_allclose(got_m.cpu().numpy(), rm, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(got_l.cpu().numpy(), rl, rtol=2e-3)
+    _, om, ol = _heads(oracle, q, k, v, scale, bool(causal))
+    np.testing.assert_allclose(om, rm, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(ol, rl, rtol=1e-5)

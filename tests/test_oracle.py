@@ -141,3 +141,67 @@ def test_reference_attention_harness_exact_pin(argv):
     assert "PASSED!" in out and "*** error" not in out, out[-400:]
     rc, out = _pin("attention", argv, AKILI_HOST_DEVICE="oracle_ulp")
     assert out.count("*** error") == 3  # one moved element per stage
+
+
+# ---- causal flash: the oracle against the reference's own CPU gold ----
+
+DAO_LIB = os.path.join(ROOT, "oracle", "_ref", "libdao_flash_ref.so")
+DAO_GOLDEN = sorted(f for f in os.listdir(os.path.join(ROOT, "tests", "golden")) if f.startswith("dao_flash__"))
+
+
+def _dao_oracle(oracle, q, k, v, causal):
+    """oracle_flash_causal head by head, with attention_cpu's own scale
+    1.0f / sqrtf((float)d) (dao_flash_cupbop.cu:136) formed in fp32."""
+    B, nh, N, d = q.shape
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(d)))
+    o = np.zeros_like(q)
+    for b in range(B):
+        for h in range(nh):
+            o[b, h] = oracle.flash_causal(q[b, h].copy(), k[b, h].copy(), v[b, h].copy(), N, d, scale,
+                                          causal=causal)[0]
+    return o
+
+
+def _bit_equal(a, b):
+    return (a.view(np.uint32) == b.view(np.uint32)) | ((a == 0) & (b == 0))
+
+
+def test_dao_flash_golden_cases_cover_the_reference_tests():
+    names = {f[len("dao_flash__"):-4] for f in DAO_GOLDEN}
+    for n in ("noncausal_single", "noncausal_multi_tile", "noncausal_multi_head", "causal_single",
+              "causal_multi_tile", "causal_multi_head"):
+        assert n in names
+
+
+@pytest.mark.parametrize("name", DAO_GOLDEN, ids=lambda f: f[len("dao_flash__"):-4])
+def test_causal_flash_oracle_bit_exact_vs_reference_golden(oracle, name):
+    """tests/golden/dao_flash__*.npz hold attention_cpu's outputs
+    (cupbop_dao_flash/dao_flash_cupbop.cu:134-169), captured by
+    tests/golden/make_dao_flash_golden.py; the oracle must equal them bit for bit."""
+    d = np.load(os.path.join(ROOT, "tests", "golden", name))
+    got = _dao_oracle(oracle, d["q"], d["k"], d["v"], int(d["causal"]))
+    same = _bit_equal(got, d["expected"])
+    assert same.all(), f"{(~same).sum()} of {same.size} differ"
+
+
+@pytest.mark.parametrize("B,nh,N,d", [(1, 1, 1, 8), (1, 1, 33, 16), (2, 3, 64, 32), (1, 2, 57, 128), (1, 1, 64, 8)])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_causal_flash_oracle_bit_exact_vs_reference_build(oracle, B, nh, N, d, causal):
+    """The same pin live: attention_cpu compiled unchanged from the reference
+    source (oracle/_ref/libdao_flash_ref.so) against the oracle, seeded
+    N(0,1) operands, N up to the gold's 64-entry score array."""
+    if not os.path.exists(DAO_LIB):
+        pytest.skip("reference-built libdao_flash_ref.so not present (python oracle/build_oracle.py)")
+    import ctypes as C
+    lib = C.CDLL(DAO_LIB)
+    rng = np.random.default_rng(N * 31 + d + causal)
+    q, k, v = (rng.standard_normal((B, nh, N, d), dtype=np.float32) * 2 for _ in range(3))
+    exp = np.zeros_like(q)
+    f = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))  # noqa: E731
+    assert lib.akili_ref_attention_cpu(f(q), f(k), f(v), f(exp), B, nh, N, d, causal) == 0
+    got = _dao_oracle(oracle, q, k, v, causal)
+    assert _bit_equal(got, exp).all()
+    # a planted one-ulp change in the oracle's output is seen
+    bad = got.copy()
+    bad.view(np.uint32)[0, 0, N - 1, 0] += 1
+    assert not _bit_equal(bad, exp).all()

@@ -8,9 +8,11 @@ LayerNorm row statistics) in a fixed device array inside the library.
 
 The GPU test calls it through the C ABI twice in a row (the second call sees
 the array holding the first call's contents) and checks each output against
-the existing akili_kbt_gemm_layernorm_ex on the same inputs, within the
-parity tolerance the other tests use.  This file is named so pytest collects
-it last.
+the existing akili_kbt_gemm_layernorm_ex on the same inputs, and against the
+CPU oracle (the reference's LayerNorm gold loop) on the same fp16-rounded
+operands, within the parity tolerance the other tests use.  It also checks
+that the device's free memory is the same before and after the second call.  This
+file is named so pytest collects it last.
 """
 import ctypes as C
 
@@ -48,7 +50,7 @@ def test_noalloc_rejects_what_it_cannot_hold_without_touching_the_gpu():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K,out_dtype", [(200, 4096, 256, "f16"), (136, 1048, 72, "f32")])
-def test_noalloc_matches_existing_entry_on_two_calls_in_a_row(M, N, K, out_dtype):
+def test_noalloc_matches_existing_entry_on_two_calls_in_a_row(oracle, M, N, K, out_dtype):
     torch = pytest.importorskip("torch")
     from akili_bench_b200 import ops
     rng = np.random.default_rng(M + N)
@@ -65,8 +67,16 @@ def test_noalloc_matches_existing_entry_on_two_calls_in_a_row(M, N, K, out_dtype
         out = torch.full((M, N), float("nan"), device="cuda", dtype=odt)
         arg = _arg(M, N, K, (x.data_ptr(), w.data_ptr(), b.data_ptr(), g.data_ptr(), beta.data_ptr(),
                              out.data_ptr()))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         rc = _noalloc(arg, abi.make_ex(abi.DTYPE_F16, odt_code), torch.cuda.current_stream().cuda_stream)
         assert rc == abi.OK, abi.strerror(rc)
         torch.cuda.synchronize()
+        if call:  # (the first call on a device may still load kernel code lazily and resolves the array's address)
+            assert torch.cuda.mem_get_info()[0] == free_before  # nothing was allocated on the device
         assert ops.device_status() == 0
-        assert_parity(out.float().cpu().numpy(), ref.float().cpu().numpy(), what=f"noalloc call {call}")
+        got = out.float().cpu().numpy()
+        assert_parity(got, ref.float().cpu().numpy(), what=f"noalloc call {call} vs akili_kbt_gemm_layernorm_ex")
+        gold = oracle.kbt_gemm_layernorm(x.float().cpu().numpy(), w.float().cpu().numpy(), b.cpu().numpy(),
+                                         g.cpu().numpy(), beta.cpu().numpy(), M, N, K, 1e-5, threads=8)
+        assert_parity(got, gold, what=f"noalloc call {call} vs oracle")
