@@ -7,7 +7,7 @@ ReLU(x.W + b) with x[8192,4096] fp16 ~N(0,1), W[4096,4096] fp16 ~N(0,1/4096),
 b[4096] fp32 ~N(0,0.1), fp32 accumulation, fp16 output, per GPU.  Inputs are
 seeded synthetic data with the configured shapes and distributions.
 
-* value      whole-job TFLOP/s: 2*M*N*K per GPU-step, all ranks, over the
+* value      whole-job TFLOP/s: 2*M*N*K summed over all ranks, over the
              max-over-ranks device time of the K timed steps (CUDA events on
              the launching stream; L2 flushed before every step, outside the
              events).
@@ -16,13 +16,22 @@ seeded synthetic data with the configured shapes and distributions.
              device->host copy of the output, all inside the timed region.
 * roofline   the fused GEMM kernel against the measured dense tensor peak.
 * cpu_baseline  the oracle (a bit-exact restatement of the reference's CPU
-             gold loop) on a bounded row sample, rank 0 at N=1.
+             gold loop) on a bounded row sample, rank 0 at N=1: one thread
+             (the reference's serial loop), plus a row-parallel run on all
+             host threads as "all_cores".
 * --impl reference  times that reference CPU path alone (all host threads).
+* clocks     sm_mhz of the timed steps measured on the device (SM cycles
+             over globaltimer nanoseconds in a short spin after each step);
+             throttle reasons from nvidia-smi sampled over the soak around them.
 
-Multi-GPU (torchrun, one rank per GPU): each rank runs the full per-GPU
-workload on its own row shard of a G*M-row batch (weak scaling, no
-collective in the timed loop); afterwards sampled output rows are
-all-gathered over NCCL and checked on rank 0 against the oracle.
+Multi-GPU (torchrun, one rank per GPU): by default (--scaling strong) the
+configured global problem is split across the ranks -- GEMM rows in
+contiguous slices, flash (batch, head) pairs -- with no collective in the
+timed loop; a weak-scaling run (every rank the full per-GPU workload)
+follows and is reported as the line's "weak" field.  Afterwards sampled
+output rows are all-gathered over NCCL and checked on rank 0 against the
+oracle.  Each rank binds to its GPU's NUMA node before allocating its
+page-locked buffers.
 """
 from __future__ import annotations
 
@@ -43,17 +52,21 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 L2_BYTES = 126 * 1024 * 1024
 FLASH_SHAPE = [8, 32, 4096, 128]  # batch, heads, seq, head_dim; --flash-shape overrides
 
-# DRAM bytes (read + write) per launch of the dominant kernel, from the ncu
-# capture summarised in profiles/ (None until captured for that workload).
+# DRAM bytes (read + write) per launch of the dominant kernel, keyed by
+# (workload, rows per GPU), from one ncu capture of that launch
+# (dram__bytes_read.sum + dram__bytes_write.sum; the capture runs with ncu's
+# cache flush, so every operand is read cold).  Workloads or shapes without
+# a capture report null.
 NCU_TRAFFIC = {
-    # profiles/gemm_pair_kernel_kbt_gemm_add_relu_8192x4096x4096.md: 171.7 MB read + 49.7 MB written
-    "kbt_gemm_add_relu": 221.4e6,
-    # profiles/softmax_rows_kernel_kbt_attention_score_16384x4096x128.md: 5.5 MB read + 74.5 MB written
-    # (part of the output is still in L2 when the kernel ends)
-    "kbt_attention_score": 80.0e6,
-    # profiles/matvec_kernel_llama2_7b_qkv.md: the QKV launch read 207.33 MB (read + write) for
-    # 201.39 MB of algorithmic bytes; scaled by that ratio to one token's 26.43 GB
-    "llama2_7b_decode": 27.21e9,
+    # gemm_pair_kernel, C2: 171.7 MB read + 49.7 MB written
+    ("kbt_gemm_add_relu", 8192): 221.4e6,
+    # softmax_rows_kernel: 5.5 MB read + 74.5 MB written (part of the output
+    # is still in L2 when the kernel ends)
+    ("kbt_attention_score", 16384): 80.0e6,
+    # matvec_kernel: the QKV launch moved 207.33 MB for 201.39 MB of
+    # algorithmic bytes; scaled by that ratio to one token's 26.43 GB (the
+    # whole token's 26 GB of weights is too large for a multi-pass capture)
+    ("llama2_7b_decode", 0): 27.21e9,
 }
 
 
@@ -103,9 +116,42 @@ def _rand(torch, gen, shape, std=1.0, mean=0.0, dtype=None):
     return t.to(dtype) if dtype is not None else t
 
 
-def workloads(torch, ops):
+class Part:
+    """This rank's share of a workload.  "strong": the configured global
+    problem is split across the ranks (GEMM rows in multiples of 8, flash
+    (batch, head) pairs), as the row / head partition of the multi-GPU layout
+    prescribes; "weak": every rank runs the full per-GPU workload.  Workloads
+    that do not split (kbt_sgemm's one 128-row tile, llama2 decode) run as
+    replicas in both modes."""
+
+    def __init__(self, world: int, rank: int, mode: str):
+        self.world, self.rank, self.mode = world, rank, mode
+
+    def rows(self, M: int) -> int:
+        if self.mode != "strong":
+            return M
+        from akili_bench_b200 import shard
+        r0, r1 = shard.row_range(M, self.world, self.rank)
+        return r1 - r0
+
+    def heads(self, B: int, H: int) -> tuple[int, int]:
+        """Local (batch, heads) of a [B, H, S, D] attention workload."""
+        if self.mode != "strong":
+            return B, H
+        from akili_bench_b200 import shard
+        u0, u1 = shard.unit_range(B * H, self.world, self.rank)
+        n = u1 - u0
+        return (n // H, H) if n % H == 0 else (1, n)
+
+    def total(self, local_flops: float, global_flops: float) -> float:
+        """Work of one step summed over all ranks."""
+        return global_flops if self.mode == "strong" else local_flops * self.world
+
+
+def workloads(torch, ops, part: "Part | None" = None):
     f16, f32 = torch.float16, torch.float32
     W = {}
+    part = part or Part(1, 0, "weak")
 
     def gemm_inputs(M, N, K, bias_std=0.1, dual=False):
         def make(gen):
@@ -117,7 +163,8 @@ def workloads(torch, ops):
             return d
         return make
 
-    M2, N2, K2 = 8192, 4096, 4096
+    G2, N2, K2 = 8192, 4096, 4096  # the C2 shape; G = global rows, M = this rank's rows
+    M2 = part.rows(G2)
     W["kbt_gemm_add_relu"] = Workload(
         "kbt_gemm_add_relu", {"M": M2, "N": N2, "K": K2}, 2.0 * M2 * N2 * K2, gemm_inputs(M2, N2, K2),
         lambda d, out, st: ops.kbt_gemm_add_relu(d["x"], d["w"], d["b"], out=out, stream=st),
@@ -139,7 +186,8 @@ def workloads(torch, ops):
         "kbt_matmul_sum_max_avgpool", {"M": M2, "N": N2, "K": K2}, 2.0 * M2 * N2 * K2, gemm_inputs(M2, N2, K2),
         lambda d, out, st: ops.kbt_matmul_sum_max_avgpool(d["x"], d["w"], d["b"], stream=st))
 
-    M3 = 16384
+    G3 = 16384
+    M3 = part.rows(G3)
 
     def ln_make(gen):
         d = gemm_inputs(M3, N2, K2, 0.02)(gen)
@@ -175,7 +223,8 @@ def workloads(torch, ops):
         2.0 * M2 * N2 * K2, kb2_make, lambda d, out, st: ops.kb2_gemm_add_relu(d["x"], d["w"], d["b"], out=out,
                                                                                stream=st))
 
-    Ma, Na, Da = 16384, 4096, 128
+    Ga, Na, Da = 16384, 4096, 128
+    Ma = part.rows(Ga)
 
     def as_make(gen):
         return {"q": _rand(torch, gen.x, (Ma, Da), dtype=f16), "k": _rand(torch, gen.w, (Na, Da), dtype=f16)}
@@ -191,7 +240,8 @@ def workloads(torch, ops):
         "kbt_sgemm", {"M": 128, "N": 128, "K": 128}, 2.0 * 128 ** 3, sg_make,
         lambda d, out, st: ops.kbt_sgemm(d["a"], d["bm"], out=out, out_dtype=f32, stream=st))
 
-    B, H, S, D = FLASH_SHAPE
+    GB, GH, S, D = FLASH_SHAPE
+    B, H = part.heads(GB, GH)
 
     def fl_make(gen):
         return {k: _rand(torch, gen.x, (B, H, S, D), dtype=f16) for k in ("q", "k", "v")}
@@ -225,6 +275,20 @@ def workloads(torch, ops):
 
     for key, shape in LLAMA2_SHAPES.items():
         W[key] = llama2_workload(torch, ops, key, *shape)
+    # work of one step over all ranks, and the partition each workload uses
+    for name, wl in W.items():
+        if name.startswith("llama2") or name == "kbt_sgemm":
+            wl.split, wl.flops_total = "replicas", wl.flops * part.world
+        elif "M" in wl.desc:
+            G = {"kbt_gemm_layernorm": G3, "kbt_gemm_rmsnorm_swiglu": G3, "kbt_gemm_silu_mul": G3,
+                 "kbt_attention_score": Ga}.get(name, G2)
+            wl.split = "rows"
+            wl.flops_total = part.total(wl.flops, wl.flops * G / max(1, wl.desc["M"]))
+            wl.desc["global_M"] = G if part.mode == "strong" else G * part.world
+        else:
+            wl.split = "heads"
+            wl.flops_total = part.total(wl.flops, wl.flops * (GB * GH) / max(1, B * H))
+            wl.desc["global_batch_heads"] = GB * GH if part.mode == "strong" else GB * GH * part.world
     return W
 
 
@@ -422,6 +486,7 @@ def reference_arm(args):
         flops = fl
     tot = sum(times)
     value = flops * len(times) / tot / 1e12
+    _, dt1, fl1 = cpu_sample("kbt_gemm_add_relu", d, min(rows_per_step, 16), 1)
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * tot / len(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
@@ -430,24 +495,359 @@ def reference_arm(args):
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                              "sample": f"{rows_per_step} of {M} rows per step, rows split over {threads} threads; "
                                        "oracle/oracle.c restates benchmarks/kbt_gemm_add_relu/main.cpp:124-129 "
-                                       "bit-exactly (pinned against the reference harness)"},
+                                       "bit-exactly (pinned against the reference harness)",
+                             "one_core": {"value": fl1 / dt1 / 1e12, "unit": "TFLOP/s", "cores": 1,
+                                          "sample": f"{min(rows_per_step, 16)} rows on one thread ({dt1:.1f} s)"},
+                             "nproc": threads},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
 # ------------------------------------------------------------------ GPU leg --
+def numa_bind(torch, local: int):
+    """Bind this process to the CPUs of its GPU's NUMA node, so the
+    page-locked host buffers it allocates afterwards sit on that node.
+    Returns the node, or None where the topology cannot be read."""
+    try:
+        p = torch.cuda.get_device_properties(local)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        node = int(open(f"/sys/bus/pci/devices/{bus}/numa_node").read().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
+def link_probe(torch, nbytes: int = 256 << 20, reps: int = 4) -> dict:
+    """The host link's ceiling for e2e: plain cudaMemcpyAsync copies between
+    page-locked host memory and the device, host->device alone,
+    device->host alone, and both at once on two streams (duplex)."""
+    hu = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    hd = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    du = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dd = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    s_up, s_dn = torch.cuda.Stream(), torch.cuda.Stream()
+    cur = torch.cuda.current_stream()
+
+    def timed(up: bool, dn: bool) -> float:
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            for s, on in ((s_up, up), (s_dn, dn)):
+                if on:
+                    s.wait_event(e0)
+            if up:
+                with torch.cuda.stream(s_up):
+                    du.copy_(hu, non_blocking=True)
+            if dn:
+                with torch.cuda.stream(s_dn):
+                    hd.copy_(dd, non_blocking=True)
+            for s, on in ((s_up, up), (s_dn, dn)):
+                if on:
+                    cur.wait_stream(s)
+            e1.record(cur)
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1) * 1e-3)
+        return best
+
+    t_up, t_dn, t_both = timed(True, False), timed(False, True), timed(True, True)
+    del hu, hd, du, dd
+    return {"h2d_gbs": nbytes / t_up / 1e9, "d2h_gbs": nbytes / t_dn / 1e9,
+            "duplex_gbs": 2 * nbytes / t_both / 1e9,
+            "how": f"{nbytes >> 20} MiB cudaMemcpyAsync page-locked<->device, best of {reps}; duplex = "
+                   "both directions at once on two streams"}
+
+
+def cpu_leg(d, threads: int, rows_per_thread: int) -> dict:
+    """The reference CPU gold (oracle) on the kbt_gemm_add_relu workload:
+    the single-thread figure (the reference's gold is a single-threaded loop,
+    kbt_gemm_add_relu/main.cpp:124-129) and a row-parallel run on all host
+    threads, each on a bounded row sample."""
+    M = 8192
+    rows1 = 48
+    all_rows = min(M, max(8, threads * rows_per_thread))
+    rows = max(rows1, all_rows)
+    dh = {"x": d["x"][:rows].float().cpu().numpy(), "w": d["w"].float().cpu().numpy(),
+          "b": d["b"].float().cpu().numpy()}
+    _, dt1, fl1 = cpu_sample("kbt_gemm_add_relu", dh, rows1, 1)
+    _, dtn, fln = cpu_sample("kbt_gemm_add_relu", dh, all_rows, threads)
+    return {"value": fl1 / dt1 / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "sample": f"{rows1} of {M} rows ({dt1:.1f} s) on one thread; oracle restating "
+                      "kbt_gemm_add_relu/main.cpp:124-129 (bit-exact, pinned against the reference harness)",
+            "nproc": threads,
+            "all_cores": {"value": fln / dtn / 1e12, "unit": "TFLOP/s", "cores": threads,
+                          "sample": f"{all_rows} rows ({dtn:.1f} s), rows split over {threads} threads "
+                                    "(a labelled row-parallel run; the reference's loop is serial)"}}
+
+
+class ClockProbe:
+    """SM clock of the timed steps, measured on the device: after each timed
+    step (outside its events) one thread spins for `spin_ns` and counts SM
+    cycles (akili_sm_clock_probe); cycles / ns over all steps is the clock."""
+
+    def __init__(self, torch, spin_ns: int = 40000):
+        self.torch, self.spin = torch, spin_ns
+        self.acc = torch.zeros(2, dtype=torch.int64, device="cuda")
+        self.n = 0
+
+    def sample(self, stream):
+        from akili_bench_b200 import abi
+        rc = abi.load().akili_sm_clock_probe(self.acc.data_ptr(), self.spin, int(stream.cuda_stream))
+        if rc != abi.OK:
+            raise abi.AkiliError("sm_clock_probe", rc)
+        self.n += 1
+
+    def mhz(self):
+        cyc, ns = (int(v) for v in self.acc.cpu())
+        return 1e3 * cyc / ns if ns else None
+
+
+def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, barrier, mode):
+    """Time one workload: device value, e2e through the public API, the
+    verification gather, roofline and clocks.  Returns (line, inputs)."""
+    from akili_bench_b200 import shard
+    from akili_bench_b200.parity import parity
+    wl = W[name]
+    d = wl.make(Gens(torch, rank))
+    out = wl.call(d, None, None)  # allocates the output
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(2 * L2_BYTES // 4, device="cuda", dtype=torch.float32)
+    graph = None
+    if wl.graph:
+        # A launch-bound step (many short kernels) is timed as replays of
+        # its launches captured once in a CUDA graph.
+        l0 = ops.launch_count()
+        wl.call(d, out, stream)
+        torch.cuda.synchronize()
+        launches_per_step = ops.launch_count() - l0
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            wl.call(d, out, torch.cuda.current_stream())
+        torch.cuda.synchronize()
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            wl.call(d, out, stream)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    probe = ClockProbe(torch)
+
+    def soak(seconds):
+        # untimed repetitions so the clock sampler sees the GPU under this load
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end:
+            for _ in range(8):
+                step()
+            torch.cuda.synchronize()
+
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clk:
+        soak(args.soak)
+        torch.cuda.synchronize()
+        barrier()
+        l0 = ops.launch_count()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+            probe.sample(stream)
+        torch.cuda.synchronize()
+        launches = ops.launch_count() - l0 if graph is None else launches_per_step * args.steps
+        barrier()
+        soak(args.soak / 2)
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    dev_ms = float(sum(per_step))
+    t = torch.tensor([dev_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = wl.flops_total * args.steps / (max_ms * 1e-3) / wl.scale
+    status = ops.device_status()
+    del graph
+
+    # --- end to end through the public API with host buffers (pinned) ---
+    e_s = torch.cuda.Event(enable_timing=True)
+    e_e = torch.cuda.Event(enable_timing=True)
+    if wl.e2e_step is not None:
+        e2e_path = "per call: vector in from page-locked host memory, product back, synchronise"
+        host = wl.e2e_host(d)
+        for _ in range(max(1, args.warmup // 2)):
+            wl.e2e_step(d, host, stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_s.record(stream)
+        for _ in range(args.steps):
+            h2d, d2h = wl.e2e_step(d, host, stream)
+        e_e.record(stream)
+        torch.cuda.synchronize()
+        del host
+    elif wl.host_call:
+        e2e_path = "akili_host_call: copies and kernel pipelined over chunks inside one call per step"
+        hd = {k: (v.cpu().pin_memory() if k not in wl.scratch else v.cpu()) for k, v in d.items()}
+        hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        h2d = sum(v.numel() * v.element_size() for k, v in hd.items() if k not in wl.scratch)
+        d2h = hout.numel() * hout.element_size()
+        for _ in range(max(1, args.warmup // 2)):
+            wl.call(hd, hout, stream)
+        torch.cuda.synchronize()
+        barrier()
+        e_s.record(stream)
+        for _ in range(args.steps):
+            wl.call(hd, hout, stream)
+        e_e.record(stream)
+        torch.cuda.synchronize()
+        del hd
+    else:
+        e2e_path = "device call, copies in and out in series on the stream"
+        keys = wl.host or tuple(d)
+        host = {k: d[k].cpu().pin_memory() for k in keys}
+        host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        d2 = dict(d)
+        d2.update({k: torch.empty_like(d[k]) for k in keys})
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = out.numel() * out.element_size()
+        for _ in range(max(1, args.warmup // 2)):
+            for k in keys:
+                d2[k].copy_(host[k], non_blocking=True)
+            o2 = wl.call(d2, out, stream)
+            host_out.copy_(o2, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e_s.record(stream)
+        for _ in range(args.steps):
+            for k in keys:
+                d2[k].copy_(host[k], non_blocking=True)
+            o2 = wl.call(d2, out, stream)
+            host_out.copy_(o2, non_blocking=True)
+        e_e.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = e_s.elapsed_time(e_e)
+    t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_max_ms = float(t.item())
+    e2e_value = wl.flops_total * args.steps / (e2e_max_ms * 1e-3) / wl.scale
+    link = link_probe(torch) if args.link_probe else None
+
+    # --- verification: sampled rows all-gathered to rank 0, checked against the oracle ---
+    check = None
+    if name.startswith("llama2") and rank == 0:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle_py
+        _, _, K, ws, outs = d["calls"][-1]
+        rows = np.linspace(0, ws[0].shape[0] - 1, 256).astype(np.int64)
+        a = ws[0][torch.from_numpy(rows).cuda()].cpu().numpy()
+        x = d["x"][K].cpu().numpy().reshape(K, 1)
+        ref = oracle_py.llama2_matmul(a, x, len(rows), 1, K)[:, 0]
+        got = outs[0][torch.from_numpy(rows).cuda()].cpu().numpy()
+        lim = 4e-6 * K ** 0.5 * (np.abs(a) @ np.abs(x))[:, 0]
+        err = np.abs(got.astype(np.float64) - ref)
+        check = {"rows_checked": len(rows), "ok": bool((err <= lim).all()),
+                 "max_err_frac": float(err.max() / np.abs(ref).max()), "gather": "local"}
+    if name == "kbt_gemm_add_relu":
+        sample = torch.tensor(shard.sample_rows(out.shape[0]), device="cuda")
+        outs, ins = shard.gather_rows([out.index_select(0, sample).float(),
+                                       d["x"].index_select(0, sample).float()], world)
+        if rank == 0:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle_py
+            w_h = d["w"].float().cpu().numpy()
+            b_h = d["b"].float().cpu().numpy()
+            worst = shard.check_gathered(outs, ins, lambda xr: oracle_py.kbt_gemm_add_relu(
+                np.ascontiguousarray(xr), w_h, b_h, xr.shape[0], w_h.shape[1], w_h.shape[0], threads=4), parity)
+            check = {"rows_checked": len(sample) * world, "ok": worst["ok"], "max_err_frac": worst["err_frac"],
+                     "min_row_cos": worst["min_cos"], "gather": "all_gather" if world > 1 else "local"}
+
+    # --- roofline of the dominant kernel ---
+    mean_s = float(np.mean(per_step)) * 1e-3
+    if wl.bound == "tensor":
+        # Timed after a power-capped soak, so the sustained peak is the
+        # matching denominator; without a soak the burst figure is.
+        key = "bf16_tflops_sustained" if args.soak > 0 else "bf16_tflops"
+        peak = pk.get(key, FALLBACK_PEAKS[key])
+        ach = wl.flops / mean_s / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "peak_source": f"{pk_kind} {key}" + (" (kernel timed inside sustained load)" if args.soak > 0
+                                                    else " (burst)"),
+                "frac_of_burst_peak": ach / pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])}
+    else:
+        peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        ach = wl.io_bytes / mean_s / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                "peak_source": f"{pk_kind} hbm_gbs"}
+    roof["traffic"] = NCU_TRAFFIC.get((name, wl.desc.get("M", 0)))
+    roof["kernel"] = wl.kernel if wl.kernel != "gemm_kernel" or wl.desc.get("M", 0) <= 128 else "gemm_pair_kernel"
+
+    cl = clk.summary()
+    mhz = probe.mhz()
+    cl["sm_mhz_smi"] = cl["sm_mhz"]
+    if mhz:
+        cl["sm_mhz"] = round(mhz, 1)
+        cl["sm_mhz_source"] = ("device: SM cycles / globaltimer ns over a 40 us spin after each timed step "
+                               "(outside its events); sm_mhz_smi = nvidia-smi median over the soak around them")
+        roof["achieved_per_mhz"] = ach / mhz
+    e2e = {"value": e2e_value, "unit": wl.unit, "path": e2e_path, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h)}
+    if link:
+        moved = (h2d + d2h) * args.steps / (e2e_ms * 1e-3) / 1e9
+        e2e["link"] = link
+        e2e["host_link_gbs"] = moved
+        e2e["frac_of_duplex"] = moved / link["duplex_gbs"]
+    if getattr(args, "numa_node", None) is not None:
+        e2e["numa_node"] = args.numa_node
+    line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak" if wl.split == "replicas" or mode == "weak" else "strong",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+            "config": {"workload": f"{name} " + " ".join(f"{k}={v}" for k, v in wl.desc.items()) + " per GPU",
+                       "parallelism": (f"{world} independent replica(s)" if wl.split == "replicas" else
+                                       f"{wl.split} split over {world} GPU(s) ({mode} scaling), "
+                                       "no collective in the timed loop"),
+                       "l2": "flushed (512 MB write) before every timed step, outside the events",
+                       "inputs": "seeded synthetic, distributions of the configured workload"},
+            "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "device_status": status, "clocks": cl}
+    if check is not None:
+        line["check"] = check
+    del flush
+    return line, d
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
-    from akili_bench_b200 import ops, shard
-    from akili_bench_b200.parity import parity
+    from akili_bench_b200 import ops
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    args.numa_node = numa_bind(torch, local) if world > 1 else None
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
@@ -456,232 +856,41 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    W = workloads(torch, ops)
-    names = list(W) if args.op == "all" else [args.op]
     pk, pk_kind = peaks()
-    results = []
-    for name in names:
-        wl = W[name]
-        d = wl.make(Gens(torch, rank))
-        out = wl.call(d, None, None)  # allocates the output
-        torch.cuda.synchronize()
-        stream = torch.cuda.current_stream()
-        flush = torch.empty(2 * L2_BYTES // 4, device="cuda", dtype=torch.float32)
-        graph = None
-        if wl.graph:
-            # A launch-bound step (many short kernels) is timed as replays of
-            # its launches captured once in a CUDA graph.
-            l0 = ops.launch_count()
-            wl.call(d, out, stream)
-            torch.cuda.synchronize()
-            launches_per_step = ops.launch_count() - l0
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                wl.call(d, out, torch.cuda.current_stream())
-            torch.cuda.synchronize()
-
-        def step():
-            if graph is not None:
-                graph.replay()
+    names = None
+    modes = [args.scaling] + (["weak"] if world > 1 and args.scaling == "strong" and not args.no_weak else [])
+    results = {}
+    for mode in modes:
+        W = workloads(torch, ops, Part(world, rank, mode))
+        names = list(W) if args.op == "all" else [args.op]
+        for name in names:
+            if mode == "weak" and W[name].split == "replicas":
+                continue
+            line, d = measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, barrier, mode)
+            if mode == modes[0]:
+                results[name] = (line, d)
             else:
-                wl.call(d, out, stream)
-
-        for _ in range(args.warmup):
-            flush.zero_()
-            step()
-        torch.cuda.synchronize()
-        barrier()
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        def soak(seconds):
-            # untimed repetitions so the clock sampler sees the GPU under this load
-            t_end = time.perf_counter() + seconds
-            while time.perf_counter() < t_end:
-                for _ in range(8):
-                    step()
-                torch.cuda.synchronize()
-
-        try:
-            gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
-        except Exception:
-            gpu_id = str(local)
-        with ClockSampler(gpu_id) as clk:
-            soak(args.soak)
-            torch.cuda.synchronize()
-            barrier()
-            l0 = ops.launch_count()
-            for i in range(args.steps):
-                flush.zero_()
-                starts[i].record(stream)
-                step()
-                ends[i].record(stream)
-            torch.cuda.synchronize()
-            launches = ops.launch_count() - l0 if graph is None else launches_per_step * args.steps
-            barrier()
-            soak(args.soak / 2)
-        per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-        dev_ms = float(sum(per_step))
-        t = torch.tensor([dev_ms], device="cuda", dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        max_ms = float(t.item())
-        value = wl.flops * world * args.steps / (max_ms * 1e-3) / wl.scale
-        status = ops.device_status()
-        del graph
-
-        # --- end to end through the public API with host buffers (pinned) ---
-        e_s = torch.cuda.Event(enable_timing=True)
-        e_e = torch.cuda.Event(enable_timing=True)
-        if wl.e2e_step is not None:
-            e2e_path = "per call: vector in from page-locked host memory, product back, synchronise"
-            host = wl.e2e_host(d)
-            for _ in range(max(1, args.warmup // 2)):
-                wl.e2e_step(d, host, stream)
-            torch.cuda.synchronize()
-            barrier()
-            e_s.record(stream)
-            for _ in range(args.steps):
-                h2d, d2h = wl.e2e_step(d, host, stream)
-            e_e.record(stream)
-            torch.cuda.synchronize()
-            del host
-        elif wl.host_call:
-            e2e_path = "akili_host_call: copies and kernel pipelined over chunks inside one call per step"
-            # akili_host_call: the whole copy-in / run / copy-out in one call per
-            # step, copies and GEMM pipelined over row chunks inside it
-            hd = {k: (v.cpu().pin_memory() if k not in wl.scratch else v.cpu()) for k, v in d.items()}
-            hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-            h2d = sum(v.numel() * v.element_size() for k, v in hd.items() if k not in wl.scratch)
-            d2h = hout.numel() * hout.element_size()
-            for _ in range(max(1, args.warmup // 2)):
-                wl.call(hd, hout, stream)
-            torch.cuda.synchronize()
-            barrier()
-            e_s.record(stream)
-            for _ in range(args.steps):
-                wl.call(hd, hout, stream)
-            e_e.record(stream)
-            torch.cuda.synchronize()
-            del hd
-        else:
-            e2e_path = "device call, copies in and out in series on the stream"
-            # the step's inputs come from host memory; scratch buffers stay on the device
-            keys = wl.host or tuple(d)
-            host = {k: d[k].cpu().pin_memory() for k in keys}
-            host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-            d2 = dict(d)
-            d2.update({k: torch.empty_like(d[k]) for k in keys})
-            h2d = sum(v.numel() * v.element_size() for v in host.values())
-            d2h = out.numel() * out.element_size()
-            for _ in range(max(1, args.warmup // 2)):
-                for k in keys:
-                    d2[k].copy_(host[k], non_blocking=True)
-                o2 = wl.call(d2, out, stream)
-                host_out.copy_(o2, non_blocking=True)
-            torch.cuda.synchronize()
-            barrier()
-            e_s.record(stream)
-            for _ in range(args.steps):
-                for k in keys:
-                    d2[k].copy_(host[k], non_blocking=True)
-                o2 = wl.call(d2, out, stream)
-                host_out.copy_(o2, non_blocking=True)
-            e_e.record(stream)
-            torch.cuda.synchronize()
-        e2e_ms = e_s.elapsed_time(e_e)
-        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_value = wl.flops * world * args.steps / (float(t.item()) * 1e-3) / wl.scale
-
-        # --- verification: sampled rows all-gathered to rank 0, checked against the oracle ---
-        check = None
-        if name.startswith("llama2") and rank == 0:
-            # the classifier product of the last step against the oracle, sampled rows
-            sys.path.insert(0, os.path.join(ROOT, "oracle"))
-            import oracle_py
-            _, _, K, ws, outs = d["calls"][-1]
-            rows = np.linspace(0, ws[0].shape[0] - 1, 256).astype(np.int64)
-            a = ws[0][torch.from_numpy(rows).cuda()].cpu().numpy()
-            x = d["x"][K].cpu().numpy().reshape(K, 1)
-            ref = oracle_py.llama2_matmul(a, x, len(rows), 1, K)[:, 0]
-            got = outs[0][torch.from_numpy(rows).cuda()].cpu().numpy()
-            lim = 4e-6 * K ** 0.5 * (np.abs(a) @ np.abs(x))[:, 0]
-            err = np.abs(got.astype(np.float64) - ref)
-            check = {"rows_checked": len(rows), "ok": bool((err <= lim).all()),
-                     "max_err_frac": float(err.max() / np.abs(ref).max()), "gather": "local"}
-        if name == "kbt_gemm_add_relu":
-            sample = torch.tensor(shard.sample_rows(out.shape[0]), device="cuda")
-            outs, ins = shard.gather_rows([out.index_select(0, sample).float(),
-                                           d["x"].index_select(0, sample).float()], world)
-            if rank == 0:
-                sys.path.insert(0, os.path.join(ROOT, "oracle"))
-                import oracle_py
-                w_h = d["w"].float().cpu().numpy()
-                b_h = d["b"].float().cpu().numpy()
-                worst = shard.check_gathered(outs, ins, lambda xr: oracle_py.kbt_gemm_add_relu(
-                    np.ascontiguousarray(xr), w_h, b_h, xr.shape[0], w_h.shape[1], w_h.shape[0], threads=4), parity)
-                check = {"rows_checked": len(sample) * world, "ok": worst["ok"], "max_err_frac": worst["err_frac"],
-                         "min_row_cos": worst["min_cos"], "gather": "all_gather" if world > 1 else "local"}
-
-        # --- roofline of the dominant kernel ---
-        if wl.bound == "tensor":
-            # Timed after a power-capped soak, so the sustained peak is the
-            # matching denominator; without a soak the burst figure is.
-            key = "bf16_tflops_sustained" if args.soak > 0 else "bf16_tflops"
-            peak = pk.get(key, FALLBACK_PEAKS[key])
-            ach = wl.flops / (float(np.mean(per_step)) * 1e-3) / 1e12
-            roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                    "peak_source": f"{pk_kind} {key}" + (" (kernel timed inside sustained load)" if args.soak > 0
-                                                        else " (burst)"),
-                    "frac_of_burst_peak": ach / pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])}
-        else:
-            peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
-            ach = wl.io_bytes / (float(np.mean(per_step)) * 1e-3) / 1e9
-            roof = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                    "peak_source": f"{pk_kind} hbm_gbs"}
-        roof["traffic"] = NCU_TRAFFIC.get(name)
-        roof["kernel"] = wl.kernel if wl.kernel != "gemm_kernel" or wl.desc.get("M", 0) <= 128 else "gemm_pair_kernel"
-
-        line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-                "config": {"workload": f"{name} " + " ".join(f"{k}={v}" for k, v in wl.desc.items()) + " per GPU",
-                           "global_rows": (wl.desc.get("M", 0) * world) if "M" in wl.desc else None,
-                           "parallelism": (f"{world} independent replica(s), one token stream per GPU"
-                                           if name.startswith("llama2") else
-                                           f"rows sharded over {world} GPU(s), no collective in the timed loop"),
-                           "l2": "flushed (512 MB write) before every timed step, outside the events",
-                           "inputs": "seeded synthetic, distributions of the configured workload"},
-                "roofline": roof,
-                "e2e": {"value": e2e_value, "unit": wl.unit, "path": e2e_path, "h2d_bytes_per_step": int(h2d),
-                        "d2h_bytes_per_step": int(d2h)},
-                "gpu_launches": int(launches),
-                "device_status": status,
-                "clocks": clk.summary()}
-        if check is not None:
-            line["check"] = check
-        results.append((name, line, d))
-        del flush
+                main_line = results[name][0]
+                main_line["weak"] = {k: line[k] for k in ("value", "ms_per_step", "scaling")}
+                main_line["weak"]["workload"] = line["config"]["workload"]
+                main_line["weak"]["gpu_launches"] = line["gpu_launches"]
+                if "check" in line:
+                    main_line["weak"]["check"] = line["check"]
+                del d
 
     if rank == 0:
-        for name, line, d in results:
+        for name in names:
+            line, d = results[name]
             if world == 1 and name == "kbt_gemm_add_relu" and not args.no_cpu:
-                threads = host_threads()
-                rows = min(8192, max(8, threads * args.cpu_rows_per_thread))
-                dh = {"x": d["x"][:rows].float().cpu().numpy(), "w": d["w"].float().cpu().numpy(),
-                      "b": d["b"].float().cpu().numpy()}
-                _, dt, fl = cpu_sample(name, dh, rows, threads)
-                line["cpu_baseline"] = {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                                        "sample": f"{rows} of 8192 rows ({dt:.1f} s), rows split over {threads} "
-                                                  "threads; oracle restating kbt_gemm_add_relu/main.cpp:124-129"}
+                line["cpu_baseline"] = cpu_leg(d, host_threads(), args.cpu_rows_per_thread)
             elif world == 1 and not args.no_cpu and W[name].cpu_fn is not None:
                 line["cpu_baseline"] = W[name].cpu_fn(d)
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     # A throughput number over wrong results is not a result: fail loudly.
-    bad = [name for name, line, _ in results if line.get("check") and not line["check"]["ok"]]
+    bad = [n for n, (line, _) in results.items() if (line.get("check") and not line["check"]["ok"]) or
+           (line.get("weak", {}).get("check") and not line["weak"]["check"]["ok"])]
     if bad:
         print(f"verification failed for {bad}", file=sys.stderr)
         return 3
@@ -697,6 +906,12 @@ def main():
     ap.add_argument("--op", default="kbt_gemm_add_relu")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--cpu-rows-per-thread", type=int, default=48)
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong: the configured global problem split across the GPUs (default); weak: every GPU "
+                         "runs the full per-GPU workload.  With strong at N>1 a weak run follows as a second field")
+    ap.add_argument("--no-weak", action="store_true", help="skip the second (weak) run at N>1")
+    ap.add_argument("--no-link-probe", dest="link_probe", action="store_false",
+                    help="skip the host-link copy probe that states e2e against the link's ceiling")
     ap.add_argument("--soak", type=float, default=1.0,
                     help="seconds of untimed load before (and half after) the timed steps, for clock sampling")
     ap.add_argument("--flash-shape", type=int, nargs=4, metavar=("B", "H", "S", "D"), default=None,

@@ -476,6 +476,15 @@ int akili_selftest_wait_timeout(uint32_t limit_us, akili_stream_t stream);
  * (all devices).  For launch accounting in benchmarks. */
 uint64_t akili_launch_count(void);
 
+/* SM clock probe for benchmarks (no counterpart in the reference): launches
+ * one thread that spins for `spin_ns` nanoseconds of %globaltimer (1000 ..
+ * 10000000) and adds the SM cycles (clock64) and the nanoseconds it saw to
+ * the two uint64 counters at device address `acc_addr`.  cycles / ns * 1000
+ * is the SM clock in MHz over the spins; enqueued between timed launches it
+ * samples the clock of the load around them.  Not counted by
+ * akili_launch_count. */
+int akili_sm_clock_probe(uint64_t acc_addr, uint32_t spin_ns, akili_stream_t stream);
+
 /* ABI version compiled into the library. */
 uint32_t akili_abi_version(void);
 

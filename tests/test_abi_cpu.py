@@ -27,7 +27,7 @@ def exported(lib: str) -> set[str]:
 def test_libakili_exports_every_declared_entry():
     names = declared("akili.h", "akili_")
     # kbt+flash, kb2, attention (+ex), flash statistics, no-alloc LN, llama2 matmul + batch, helpers
-    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 7  # helpers: + akili_host_call
+    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 8  # helpers: + akili_host_call, akili_sm_clock_probe
     missing = names - exported(abi.LIB_PATH)
     assert not missing, missing
     L = abi.load()
@@ -157,3 +157,11 @@ def test_host_call_validates_before_cuda():
     assert L.akili_host_call(b"kb2_gemm_add_relu", C.byref(k2), C.byref(abi.make_ex()), None) == abi.E_DTYPE
     assert L.akili_host_call(b"kbt_gemm_add_relu", C.byref(arg), C.byref(abi.make_ex(batch=2)), None) == \
         abi.E_UNSUPPORTED
+
+
+def test_sm_clock_probe_validates_before_any_cuda_call():
+    L = abi.load()
+    assert L.akili_sm_clock_probe(0, 50000, None) == abi.E_NULL_ARG
+    assert L.akili_sm_clock_probe(0x1004, 50000, None) == abi.E_ALIGN
+    assert L.akili_sm_clock_probe(0x1000, 10, None) == abi.E_SHAPE
+    assert L.akili_sm_clock_probe(0x1000, 20_000_000, None) == abi.E_SHAPE
