@@ -32,7 +32,7 @@ E_DEVICE_TIMEOUT = -9
 E_ABI = -10
 E_WORKSPACE = -11
 E_SCRATCH_LIMIT = -12
-NOALLOC_SCRATCH_BYTES = 4 << 20
+NOALLOC_SCRATCH_BYTES = (4 << 20) + (64 << 10)
 
 _u32, _u64, _f = C.c_uint32, C.c_uint64, C.c_float
 _HDR = [("grid_dim", _u32 * 3), ("block_dim", _u32 * 3), ("M", _u32), ("N", _u32), ("K", _u32)]

@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -291,7 +292,16 @@ struct JobBuffers {
   __half* B0lo = nullptr;
   __half* B1lo = nullptr;
   float* stats = nullptr;
+  unsigned int* row_sync = nullptr;  // row-fused LayerNorm / softmax: one counter per 128-row block
 };
+
+// Row-fused LayerNorm / softmax candidates: the CTA-pair kernel (M > 128)
+// with a row-normalising epilogue.  Whether a launch fuses is decided at
+// launch (launch_gemm_pair); the counters are laid out either way.
+bool rownorm_candidate(const GemmJob& j) {
+  return epi_rownorm(j.epi) && !softmax_fused(j) && j.M > static_cast<uint32_t>(kBM);
+}
+size_t row_sync_count(const GemmJob& j) { return 2 * ((static_cast<size_t>(j.M) + 2 * kBM - 1) / (2 * kBM)); }
 
 size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
   const bool dual = epi_dual(j.epi);
@@ -328,20 +338,34 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
     if (j.stats_hint && j.stats_hint_bytes >= sb) jb->stats = static_cast<float*>(j.stats_hint);
     else jb->stats = static_cast<float*>(grab(sb));
   }
+  if (rownorm_candidate(j)) jb->row_sync = static_cast<unsigned int*>(grab(row_sync_count(j) * sizeof(unsigned int)));
   return cv.off;
+}
+
+// Row-fused LayerNorm / softmax switch: AKILI_ROWNORM=0 in the environment
+// selects the two-pass form (statistics, then a finaliser kernel).
+bool rownorm_enabled() {
+  const char* e = std::getenv("AKILI_ROWNORM");
+  return !(e && e[0] == '0');
 }
 
 // Persistent launch of the CTA-pair kernel: clusters of 2, as many pairs as
 // can be resident at once (cudaOccupancyMaxActiveClusters), at most one per tile.
+// With ea.row_sync set (a row-normalising epilogue) the launch is row-fused
+// when every column tile of a row block fits in one wave (num_n <= pairs):
+// the counters are zeroed on the stream and the kernel goes out as a
+// cooperative launch, so all its pairs are resident together.  Otherwise, or
+// if the cooperative launch is refused, it runs in the two-pass form and
+// *fused is false (the caller runs the finaliser).
 template <Epi E, typename OutT, bool BK, bool kSplit = false>
 int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMap& tmB0, const CUtensorMap& tmB1,
                      const CUtensorMap& tmC, const CUtensorMap& tmAlo, const CUtensorMap& tmB0lo,
-                     const CUtensorMap& tmB1lo, const EpiArgs& ea, cudaStream_t st) {
+                     const CUtensorMap& tmB1lo, EpiArgs ea, cudaStream_t st, bool* fused) {
   constexpr int BN = epi_bn(E);
   const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT), kSplit);
   auto kern = gemm_pair_kernel<E, OutT, BK, kSplit>;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -374,9 +398,30 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
     }
     pairs_cap = it->second;
   }
-  const int tiles = ((ea.M + 2 * kBM - 1) / (2 * kBM)) * ((ea.N + BN - 1) / BN);
+  const int num_n = (ea.N + BN - 1) / BN;
+  const int tiles = ((ea.M + 2 * kBM - 1) / (2 * kBM)) * num_n;
   const int pairs = tiles < pairs_cap ? tiles : pairs_cap;
   cfg.gridDim = dim3(2 * pairs);
+  if (fused) *fused = false;
+  if constexpr (epi_rownorm(E)) {
+    if (ea.row_sync && fused && num_n <= pairs && rownorm_enabled()) {
+      const size_t nsync = 2 * static_cast<size_t>((ea.M + 2 * kBM - 1) / (2 * kBM));
+      if (cudaMemsetAsync(ea.row_sync, 0, nsync * sizeof(unsigned int), st) != cudaSuccess) {
+        cudaGetLastError();
+        return AKILI_E_LAUNCH;
+      }
+      attr[1].id = cudaLaunchAttributeCooperative;
+      attr[1].val.cooperative = 1;
+      cfg.numAttrs = 2;
+      if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) == cudaSuccess) {
+        *fused = true;
+        return launch_status();
+      }
+      cudaGetLastError();  // refused: fall back to the two-pass form below
+      cfg.numAttrs = 1;
+    }
+  }
+  ea.row_sync = nullptr;
   if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) != cudaSuccess) {
     cudaGetLastError();
     return AKILI_E_LAUNCH;
@@ -385,7 +430,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
 }
 
 template <Epi E, typename OutT, bool BK, bool kSplit = false>
-int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaStream_t st) {
+int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaStream_t st, bool* fused) {
   constexpr bool kStore = epi_stores(E);
   constexpr int BN = epi_bn(E);
   CUtensorMap tmA, tmB0, tmB1, tmC;
@@ -430,6 +475,10 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.N = static_cast<int>(N);
   ea.K = static_cast<int>(K);
   ea.num_n_tiles = static_cast<int>(2 * ((N + BN - 1) / BN));  // statistics slots: two per tile
+  ea.row_sync = jb.row_sync;
+  ea.ln_w = j.ln_w;
+  ea.ln_b = j.ln_b;
+  ea.eps = j.eps;
 
   // the lo parts of the split mode: the same boxes over the lo copies
   CUtensorMap tmAlo = tmA, tmB0lo = tmB0, tmB1lo = tmB1;
@@ -443,7 +492,8 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
     if (!ok) return AKILI_E_LAUNCH;
   }
   if (pair)
-    return launch_gemm_pair<E, OutT, BK, kSplit>(di, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea, st);
+    return launch_gemm_pair<E, OutT, BK, kSplit>(di, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea, st, fused);
+  if (fused) *fused = false;
   const int smem = gemm_smem_bytes(kStore, sizeof(OutT), kSplit);
   static std::mutex mu;
   static std::map<int, bool> attr_done;
@@ -513,12 +563,14 @@ int launch_softmax_rows(const DevInfo& di, const GemmJob& j, const JobBuffers& j
 }
 
 template <Epi E, bool BK = false>
-int launch_gemm_out(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, bool out_f32, cudaStream_t st) {
-  if (j.split) return launch_gemm<E, float, BK, true>(di, j, jb, st);  // the kb2_* family: fp32 out
+int launch_gemm_out(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, bool out_f32, cudaStream_t st,
+                    bool* fused = nullptr) {
+  if (j.split) return launch_gemm<E, float, BK, true>(di, j, jb, st, fused);  // the kb2_* family: fp32 out
   if constexpr (!epi_stores(E)) {
-    return launch_gemm<E, float, BK>(di, j, jb, st);
+    return launch_gemm<E, float, BK>(di, j, jb, st, fused);
   } else {
-    return out_f32 ? launch_gemm<E, float, BK>(di, j, jb, st) : launch_gemm<E, __half, BK>(di, j, jb, st);
+    return out_f32 ? launch_gemm<E, float, BK>(di, j, jb, st, fused)
+                   : launch_gemm<E, __half, BK>(di, j, jb, st, fused);
   }
 }
 
@@ -577,22 +629,24 @@ int run_job(const GemmJob& j, const Mode& md, cudaStream_t st) {
     return j.b_kmajor ? launch_softmax_rows<__half, true>(di, j, jb, st)
                       : launch_softmax_rows<__half, false>(di, j, jb, st);
   }
+  bool rowfused = false;  // the row-normalising epilogue finished the rows in the GEMM kernel
   switch (j.epi) {
     case Epi::kPlain: rc = launch_gemm_out<Epi::kPlain>(di, j, jb, md.out_f32, st); break;
     case Epi::kBiasRelu: rc = launch_gemm_out<Epi::kBiasRelu>(di, j, jb, md.out_f32, st); break;
     case Epi::kBiasMulLeaky: rc = launch_gemm_out<Epi::kBiasMulLeaky>(di, j, jb, md.out_f32, st); break;
     case Epi::kRowSumHalf: rc = launch_gemm_out<Epi::kRowSumHalf>(di, j, jb, md.out_f32, st); break;
     case Epi::kRowSumBias: rc = launch_gemm_out<Epi::kRowSumBias>(di, j, jb, md.out_f32, st); break;
-    case Epi::kLnPre: rc = launch_gemm_out<Epi::kLnPre>(di, j, jb, md.out_f32, st); break;
+    case Epi::kLnPre: rc = launch_gemm_out<Epi::kLnPre>(di, j, jb, md.out_f32, st, &rowfused); break;
     case Epi::kSoftmaxPre:
-      rc = j.b_kmajor ? launch_gemm_out<Epi::kSoftmaxPre, true>(di, j, jb, md.out_f32, st)
-                      : launch_gemm_out<Epi::kSoftmaxPre, false>(di, j, jb, md.out_f32, st);
+      rc = j.b_kmajor ? launch_gemm_out<Epi::kSoftmaxPre, true>(di, j, jb, md.out_f32, st, &rowfused)
+                      : launch_gemm_out<Epi::kSoftmaxPre, false>(di, j, jb, md.out_f32, st, &rowfused);
       break;
     case Epi::kLseClamp: rc = launch_gemm_out<Epi::kLseClamp>(di, j, jb, md.out_f32, st); break;
     case Epi::kSiluMulBias: rc = launch_gemm_out<Epi::kSiluMulBias>(di, j, jb, md.out_f32, st); break;
     case Epi::kSwiglu: rc = launch_gemm_out<Epi::kSwiglu>(di, j, jb, md.out_f32, st); break;
   }
   if (rc) return rc;
+  if (rowfused) return AKILI_OK;
   // 3. finalisers
   const int M = static_cast<int>(j.M), N = static_cast<int>(j.N);
   const int nt = 2 * ((N + epi_bn(j.epi) - 1) / epi_bn(j.epi));  // statistics slots (half tiles)
@@ -1031,8 +1085,9 @@ cudaStream_t S(akili_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 // ------------------------------------------------- no-alloc LayerNorm scratch --
 // Fixed device scratch of akili_kbt_gemm_layernorm_noalloc: the per-(row,
 // 128-column half tile) (mean, M2) partials its GEMM epilogue writes and its
-// finaliser reads.  Every slot the finaliser reads is written earlier in the
-// same call, so nothing needs clearing between calls; concurrent calls race.
+// row merge (or finaliser) reads, and the row-fused epilogue's arrival
+// counters.  Every statistics slot read is written earlier in the same call;
+// the counters are zeroed on the stream before each GEMM.  Concurrent calls race.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[AKILI_NOALLOC_SCRATCH_BYTES];
 
 // Device address of g_noalloc_scratch for the current device.  In host code
@@ -1561,7 +1616,7 @@ int akili_kbt_gemm_layernorm_noalloc(const kbt_gemm_layernorm_arg_t* a, const ak
   GemmJob j;
   if ((rc = job_layernorm(a, j, a->M != 0))) return rc;
   if (j.M == 0) return AKILI_OK;
-  if (stats_bytes(j) > AKILI_NOALLOC_SCRATCH_BYTES) return AKILI_E_SCRATCH_LIMIT;
+  if (job_scratch_bytes(j, md) > AKILI_NOALLOC_SCRATCH_BYTES) return AKILI_E_SCRATCH_LIMIT;
   void* scratch = nullptr;
   if ((rc = noalloc_scratch_ptr(&scratch))) return rc;
   md.workspace = scratch;

@@ -71,7 +71,17 @@ struct EpiArgs {
   float* row_ws;      // partial stats: [stat][n_tile][M]
   int M, N, K;
   int num_n_tiles;
+  // Row-fused LayerNorm / softmax (CTA-pair kernel): one arrival counter per
+  // 128-row block, zeroed before the launch; nullptr = the two-pass form
+  // (statistics here, a finaliser kernel afterwards).
+  unsigned int* row_sync;
+  const float* ln_w;  // LayerNorm gamma / beta and eps (row-fused kLnPre)
+  const float* ln_b;
+  float eps;
 };
+
+// Epilogues that normalise whole rows (longer than one tile).
+__host__ __device__ constexpr bool epi_rownorm(Epi e) { return e == Epi::kLnPre || e == Epi::kSoftmaxPre; }
 
 // Split mode (fp32 operands as fp16 hi + lo parts, the kb2_* family): a
 // stage holds [A_hi][B_hi][A_lo][B_lo], twice the bytes, so the ring is two deep.
@@ -292,6 +302,136 @@ __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUten
     }
   }
   return st;
+}
+
+// ---- row-fused LayerNorm / softmax (the CTA-pair kernel with ea.row_sync) ----
+// Pass 1 reads a half tile's accumulator columns and returns the row's
+// statistics of the unrounded values y (LayerNorm: y = acc + b, (mean, M2)
+// merged chunk by chunk with Chan et al.'s update; softmax: y = acc * s0,
+// (max, sum of exp2) in the log2 domain).  Nothing is stored.
+template <Epi E>
+__device__ __forceinline__ RowState rowstats_half(const EpiArgs& ea, uint32_t tbase, int n0, int c_begin,
+                                                  int c_end) {
+  RowState st;
+  st.a = (E == Epi::kLnPre) ? 0.0f : -INFINITY;
+  st.b = 0.0f;
+  st.n = 0.0f;
+  float v2[64];
+  float u[32];
+  for (int c = c_begin; c < c_end; ++c) {
+    const bool odd = ((c - c_begin) & 1) != 0;
+    if (!odd) tmem_ld64(tbase + c * 32, v2);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = odd ? v2[32 + i] : v2[i];
+    const int col0 = n0 + c * 32;
+    epi_chunk<E, float>(ea, col0, min(32, ea.N - col0), v, u, st);
+  }
+  return st;
+}
+
+// A row's statistics merged over all its half-tile slots (written by the
+// CTAs of every tile of this row block): LayerNorm -> (mean, 1/sqrt(var +
+// eps)) with var = M2 / N; softmax -> (m2, 1/l) in the log2 domain.  The slots are read
+// through L2 (other SMs wrote them during this launch).
+template <Epi E>
+__device__ __forceinline__ void rowstats_merge(const EpiArgs& ea, int row, float& s0, float& s1) {
+  const int nslots = ea.num_n_tiles;
+  const size_t plane = static_cast<size_t>(nslots) * ea.M;
+  const int rr = min(row, ea.M - 1);
+  float a = (E == Epi::kLnPre) ? 0.0f : -INFINITY, b = 0.0f, n = 0.0f;
+  for (int t0 = 0; t0 < nslots; t0 += 8) {
+    float pa[8], pb[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int t = t0 + q;
+      pa[q] = t < nslots ? __ldcg(ea.row_ws + static_cast<size_t>(t) * ea.M + rr) : 0.0f;
+      pb[q] = t < nslots ? __ldcg(ea.row_ws + plane + static_cast<size_t>(t) * ea.M + rr) : 0.0f;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int t = t0 + q;
+      if (t >= nslots) break;
+      if constexpr (E == Epi::kLnPre) {
+        const float nb = static_cast<float>(max(0, min(kAccCols / 2, ea.N - t * (kAccCols / 2))));
+        if (nb > 0.0f) {
+          if (n == 0.0f) {
+            a = pa[q];
+            b = pb[q];
+            n = nb;
+          } else {
+            const float ntot = n + nb;
+            const float delta = pa[q] - a;
+            a += delta * (nb / ntot);
+            b += pb[q] + delta * delta * (n * nb / ntot);
+            n = ntot;
+          }
+        }
+      } else {
+        if (pa[q] != -INFINITY) {
+          if (a == -INFINITY) {
+            a = pa[q];
+            b = pb[q];
+          } else {
+            const float mn = fmaxf(a, pa[q]);
+            b = b * exp2f(a - mn) + pb[q] * exp2f(pa[q] - mn);
+            a = mn;
+          }
+        }
+      }
+    }
+  }
+  if constexpr (E == Epi::kLnPre) {
+    s0 = a;
+    s1 = 1.0f / sqrtf(b / static_cast<float>(ea.N) + ea.eps);
+  } else {
+    s0 = a;
+    s1 = 1.0f / b;
+  }
+}
+
+// Pass 2: the same half tile read again from TMEM, normalised with the row's
+// merged statistics (LayerNorm: ((y - mean) * inv_std) * gamma + beta;
+// softmax: exp2(y * log2 e - m2) * (1 / l)) and written once through the
+// staging buffers and TMA stores of the ordinary epilogue.
+template <Epi E, typename OutT>
+__device__ __forceinline__ void rownorm_half(const EpiArgs& ea, const CUtensorMap* tmC, uint32_t tbase, int n0,
+                                             int mrow0, int r, int c_begin, int c_end, uint8_t* staging,
+                                             uint32_t bar_id, bool issuer, int& chunk_ctr, float s0, float s1) {
+  constexpr int kStageOut = kBM * 32 * sizeof(OutT);
+  constexpr float kLog2e = 1.4426950408889634f;
+  float v2[64];
+  for (int c = c_begin; c < c_end; ++c) {
+    const bool odd = ((c - c_begin) & 1) != 0;
+    if (!odd) tmem_ld64(tbase + c * 32, v2);
+    const int col0 = n0 + c * 32;
+    const int nvalid = min(32, ea.N - col0);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float acc = odd ? v2[32 + j] : v2[j];
+      const bool ok = j < nvalid;
+      if constexpr (E == Epi::kLnPre) {
+        const float y = acc + (ok ? __ldg(ea.vec0 + col0 + j) : 0.0f);
+        const float g = ok ? __ldg(ea.ln_w + col0 + j) : 0.0f;
+        const float bb = ok ? __ldg(ea.ln_b + col0 + j) : 0.0f;
+        v[j] = ((y - s0) * s1) * g + bb;
+      } else {
+        v[j] = exp2f(fmaf(acc * ea.s0, kLog2e, -s0)) * s1;
+      }
+    }
+    uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
+    if (issuer) bulk_wait_read<1>();
+    named_bar_sync(bar_id, 128);
+    stage_row<OutT>(stg, r, v);
+    fence_async_shared();
+    named_bar_sync(bar_id, 128);
+    if (issuer) {
+      tma_store_2d(tmC, stg, col0, mrow0);
+      bulk_commit();
+    }
+    ++chunk_ctr;
+  }
 }
 
 // Per-row partial statistics of one half tile go to slot `slot` of the
@@ -562,6 +702,18 @@ __host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes, 
   return s;
 }
 
+// Tile order of the CTA-pair kernel: the grouped raster, or row-block-major
+// (every column tile of a row block in turn) for the row-fused epilogues.
+__device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n, bool row_major, int& m_blk,
+                                                 int& n_blk) {
+  if (row_major) {
+    m_blk = tile / num_n;
+    n_blk = tile - m_blk * num_n;
+  } else {
+    tile_coords(tile, num_m, num_n, m_blk, n_blk);
+  }
+}
+
 template <Epi E, typename OutT, bool kBKMajor, bool kSplit = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
@@ -602,6 +754,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int num_kb = (K + kBK - 1) / kBK;
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
+  // Row-fused LayerNorm / softmax: tiles in row-block-major order, so the
+  // tiles of one row block run in the same wave (see the epilogue).
+  const bool rowfused = epi_rownorm(E) && ea.row_sync != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
@@ -641,7 +796,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         int m_blk, n_blk;
-        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        pair_tile_coords(tile, num_m, num_n, rowfused, m_blk, n_blk);
         const int row0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
         const int col0 = n_blk * BN + static_cast<int>(rank) * BNH;
         for (int kb = 0; kb < num_kb && ok; ++kb) {
@@ -753,32 +908,86 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     constexpr int HC = BN / 64;  // chunks per half tile
     int it = 0;
     int chunk_ctr = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
-      int m_blk, n_blk;
-      tile_coords(tile, num_m, num_n, m_blk, n_blk);
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
-      // Each group reads only its own flag, after its own barrier, so all of
-      // its threads leave together.
-      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[grp] = 1;
-      named_bar_sync(bar_id, 128);
-      if (abort_flag[grp]) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
-      const int n0 = n_blk * BN;
-      const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
-      const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-      const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
-                                                 min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
-                                                 chunk_ctr);
-      // This warp has read its TMEM rows: release the accumulator to the even CTA's MMA.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (leader) mbar_arrive(&acc_empty[acc]);
-        else mbar_arrive_cluster(acc_empty_c + acc * 8);
+    if (rowfused) {
+      // Row-fused LayerNorm / softmax.  Per tile: pass 1 reads this CTA's
+      // accumulator and publishes each row's statistics of its half tile;
+      // the CTA then arrives on its 128-row block's counter and waits until
+      // the CTAs of all num_n tiles of the block have arrived; pass 2 merges
+      // the row's statistics, reads the accumulator again, normalises and
+      // stores the result once.  Both epilogue groups share one barrier (3)
+      // and one abort flag so that they leave together.
+      //
+      // Progress: tiles run row-block-major and num_n <= npairs, so the tile
+      // a pair handles before tile t of row block R (t - npairs) lies in an
+      // earlier row block, as does the tile whose accumulator tile t reuses
+      // (t - 2 npairs).  Pass 1 of every tile of R therefore depends only on
+      // earlier row blocks, and the wait in tile t ends once they are done.
+      // All pairs are resident at once (cooperative launch).
+      for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+        int m_blk, n_blk;
+        pair_tile_coords(tile, num_m, num_n, true, m_blk, n_blk);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[0] = 1;
+        named_bar_sync(3, 256);
+        if (abort_flag[0]) break;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
+        const int n0 = n_blk * BN;
+        const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
+        const int c0 = grp * HC, c1 = min((grp + 1) * HC, nchunks);
+        const RowState st = rowstats_half<E>(ea, tbase, n0, c0, c1);
+        write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
+        __threadfence();
+        named_bar_sync(3, 256);
+        if (threadIdx.x == 64) {
+          unsigned int* cnt = ea.row_sync + mrow0 / kBM;
+          atomicAdd(cnt, 1u);
+          if (!counter_wait_geq(cnt, static_cast<unsigned int>(num_n), kSiteRowSync)) abort_flag[0] = 1;
+        }
+        named_bar_sync(3, 256);
+        if (abort_flag[0]) break;
+        __threadfence();
+        float s0, s1;
+        rowstats_merge<E>(ea, mrow0 + r, s0, s1);
+        rownorm_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, c0, c1, gstaging, bar_id, gtid == 0, chunk_ctr, s0,
+                              s1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&acc_empty[acc]);
+          else mbar_arrive_cluster(acc_empty_c + acc * 8);
+        }
       }
-      write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
+    } else {
+      for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+        int m_blk, n_blk;
+        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        // Each group reads only its own flag, after its own barrier, so all of
+        // its threads leave together.
+        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[grp] = 1;
+        named_bar_sync(bar_id, 128);
+        if (abort_flag[grp]) break;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
+        const int n0 = n_blk * BN;
+        const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
+        const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
+                                                   min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
+                                                   chunk_ctr);
+        // This warp has read its TMEM rows: release the accumulator to the even CTA's MMA.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&acc_empty[acc]);
+          else mbar_arrive_cluster(acc_empty_c + acc * 8);
+        }
+        write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
+      }
     }
     if constexpr (kStore) {
       if (gtid == 0) bulk_wait<0>();

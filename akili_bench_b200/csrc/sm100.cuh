@@ -37,6 +37,7 @@ enum WaitSite : uint32_t {
   kSiteDrain = 11,
   kSiteSelfTest = 12,
   kSiteExchange = 13,
+  kSiteRowSync = 14,
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -97,6 +98,25 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, ui
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site) {
   return mbar_wait_for(bar, parity, site, kWaitTimeoutNs);
+}
+
+// Wait until the global counter at `p` reaches `target` (acquire at GPU
+// scope, so what the arriving CTAs wrote before their release is visible).
+// Returns false (and records `site`) after kWaitTimeoutNs.
+__device__ __forceinline__ bool counter_wait_geq(const unsigned int* p, unsigned int target, uint32_t site) {
+  uint64_t t0 = 0;
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    if (t0 == 0) {
+      t0 = globaltimer();
+    } else if (globaltimer() - t0 > kWaitTimeoutNs) {
+      record_timeout(site);
+      return false;
+    }
+    __nanosleep(32);
+  }
 }
 
 // Wait for up to three barrier phases at once: the try_waits are issued back

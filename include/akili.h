@@ -316,16 +316,19 @@ int akili_kbt_gemm_layernorm_ex(const kbt_gemm_layernorm_arg_t* arg, const akili
  * The caller passes inputs and outputs as for akili_kbt_gemm_layernorm_ex;
  * operands must be fp16 (ex->in_dtype = AKILI_DTYPE_F16, output fp16 or
  * fp32) and ex->workspace must be 0.  The only scratch, the per-row LayerNorm
- * partial statistics, lives in a fixed device array of
- * AKILI_NOALLOC_SCRATCH_BYTES inside the library (held by every GPU that
- * loads it until exit); a problem needing more, i.e.
- * 16 * M * ceil(N / 256) bytes > AKILI_NOALLOC_SCRATCH_BYTES, returns
- * AKILI_E_SCRATCH_LIMIT.  The first call on a device looks up that array's
- * device address (once per device, with the device current); make that first
- * call before any stream capture.  All calls share the array: calls that
- * overlap on the GPU (different streams, or different host threads on one
- * device) race on it and must be serialised by the caller. */
-#define AKILI_NOALLOC_SCRATCH_BYTES (4u << 20)
+ * partial statistics and (for M > 128) one arrival counter per 128-row
+ * block, lives in a fixed device array of AKILI_NOALLOC_SCRATCH_BYTES inside
+ * the library (held by every GPU that loads it until exit); a problem needing
+ * more, i.e. 16 * M * ceil(N / 256) bytes of statistics plus
+ * 8 * ceil(M / 256) bytes of counters (each rounded up to 256 bytes)
+ * > AKILI_NOALLOC_SCRATCH_BYTES, returns AKILI_E_SCRATCH_LIMIT (M = 16384 at
+ * N = 4096 fits).  Each call zeroes the counters on its stream before its
+ * GEMM.  The first call on a device looks up that array's device address
+ * (once per device, with the device current); make that first call before
+ * any stream capture.  All calls share the array: calls that overlap on the
+ * GPU (different streams, or different host threads on one device) race on
+ * it and must be serialised by the caller. */
+#define AKILI_NOALLOC_SCRATCH_BYTES ((4u << 20) + (64u << 10))
 int akili_kbt_gemm_layernorm_noalloc(const kbt_gemm_layernorm_arg_t* arg, const akili_ex_t* ex,
                                      akili_stream_t stream);
 

@@ -225,3 +225,54 @@ def test_workspace_too_small_is_rejected_and_exact_fit_works(oracle):
     got = ops.kbt_gemm_layernorm(dev(x, torch.float16), dev(w, torch.float16), dev(b, f32), dev(g, f32),
                                  dev(beta, f32), workspace=ws).float().cpu().numpy()
     assert_parity(got, oracle.kbt_gemm_layernorm(x, w, b, g, beta, M, N, K, 1e-5))
+
+
+# Row-fused LayerNorm / softmax (CTA-pair kernel, M > 128): the epilogue merges
+# each row's statistics across the CTAs of the row block and stores the
+# normalised row once, one launch.  AKILI_ROWNORM=0 selects the two-pass form
+# (GEMM with statistics, then a finaliser: two launches).  Shapes: ragged M and
+# N, several row blocks whose tiles straddle a wave, N of 33 tiles, and N of 75
+# tiles (more than one wave of CTA pairs holds: the two-pass form either way).
+ROWFUSED = [(264, 4104, 136), (200, 264, 136), (520, 8200, 264), (2056, 4096, 256), (1032, 1048, 520),
+            (264, 18952, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", ROWFUSED)
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_layernorm_row_fused_and_two_pass(oracle, monkeypatch, M, N, K, mode):
+    monkeypatch.setenv("AKILI_ROWNORM", mode)
+    rng = np.random.default_rng(23 * M + N)
+    x, w = f16(rng, (M, K)), f16(rng, (K, N), K ** -0.5)
+    b = rng.standard_normal(N).astype(np.float32) * 0.02
+    g = (1 + rng.standard_normal(N) * 0.02).astype(np.float32)
+    beta = rng.standard_normal(N).astype(np.float32) * 0.02
+    ref = oracle.kbt_gemm_layernorm(x, w, b, g, beta, M, N, K, 1e-5, threads=8)
+    f16t, f32 = torch.float16, torch.float32
+    args = (dev(x, f16t), dev(w, f16t), dev(b, f32), dev(g, f32), dev(beta, f32))
+    for odt in (f16t, f32):
+        torch.cuda.synchronize()
+        l0 = ops.launch_count()
+        got = ops.kbt_gemm_layernorm(*args, 1e-5, out_dtype=odt).float().cpu().numpy()
+        launches = ops.launch_count() - l0
+        assert ops.device_status() == 0
+        assert_parity(got, ref, what=f"layernorm rownorm={mode} {odt}")
+        assert launches == (1 if mode == "1" and N <= 74 * 256 else 2)
+
+
+@pytest.mark.parametrize("M,N,K", [(264, 1040, 320), (1032, 4096, 512), (2056, 2056, 264), (520, 8200, 264)])
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_matmul_softmax_row_fused_and_two_pass(oracle, monkeypatch, M, N, K, mode):
+    monkeypatch.setenv("AKILI_ROWNORM", mode)
+    rng = np.random.default_rng(29 * M + N)
+    a, b = f16(rng, (M, K)), f16(rng, (K, N), K ** -0.5 * 3)
+    ref = oracle.kbt_matmul_softmax(a, b, M, N, K, threads=8)
+    f16t = torch.float16
+    for odt in (f16t, torch.float32):
+        torch.cuda.synchronize()
+        l0 = ops.launch_count()
+        got = ops.kbt_matmul_softmax(dev(a, f16t), dev(b, f16t), out_dtype=odt).float().cpu().numpy()
+        launches = ops.launch_count() - l0
+        assert ops.device_status() == 0
+        assert_parity(got, ref, what=f"softmax rownorm={mode} {odt}")
+        np.testing.assert_allclose(got.sum(1), 1.0, rtol=2e-3)
+        assert launches == (1 if mode == "1" else 2)

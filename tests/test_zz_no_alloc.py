@@ -46,6 +46,17 @@ def test_noalloc_rejects_what_it_cannot_hold_without_touching_the_gpu():
     ex_ws = abi.make_ex(abi.DTYPE_F16, abi.DTYPE_F16, workspace=0x10000, workspace_bytes=1 << 20)
     assert _noalloc(_arg(64, 256, 64), ex_ws) == abi.E_UNSUPPORTED
     assert abi.load().akili_kbt_gemm_layernorm_noalloc(C.byref(_arg(64, 256, 64)), None, None) == abi.E_NULL_ARG
+    # the documented example fits: 4 MiB of statistics plus 512 bytes of counters at M = 16384, N = 4096
+    # (checked only where no GPU would go on to launch on these placeholder addresses)
+    try:
+        import torch
+        have_gpu = torch.cuda.is_available()
+    except Exception:
+        have_gpu = False
+    if not have_gpu:
+        assert 16 * 16384 * 16 + 512 <= abi.NOALLOC_SCRATCH_BYTES
+        assert _noalloc(_arg(16384, 4096, 64), ex) not in (abi.OK, abi.E_SCRATCH_LIMIT)  # no device here
+        assert _noalloc(_arg(16384, 4608, 64), ex) == abi.E_SCRATCH_LIMIT
 
 
 @pytest.mark.gpu
