@@ -293,7 +293,31 @@ struct JobBuffers {
   __half* B1lo = nullptr;
   float* stats = nullptr;
   unsigned int* row_sync = nullptr;  // row-fused LayerNorm / softmax: one counter per 128-row block
+  unsigned int* sk_flags = nullptr;  // stream-K: a ready flag and a partial slot per (pair, CTA)
+  float* sk_part = nullptr;
 };
+
+// ---- stream-K ----
+// The CTA-pair kernel runs whole tiles per pair unless the tiles fill its
+// waves poorly: with efficiency tiles / (ceil(tiles / P) * P) below
+// kSkMinWaveEff over P pairs (the small per-GPU M of a row-split GEMM), the
+// (tile, K-block) units are split evenly over the pairs (stream-K).
+// AKILI_STREAMK=0 in the environment keeps whole tiles.
+constexpr int kSkMaxPairs = 74;          // partial slots laid out for a B200's 148 SMs
+constexpr double kSkMinWaveEff = 0.96;
+constexpr int kSkMinUnitsPerPair = 8;    // K-blocks per pair below which splitting does not pay
+
+bool streamk_enabled() {
+  const char* e = std::getenv("AKILI_STREAMK");
+  return !(e && e[0] == '0');
+}
+
+bool streamk_wanted(long long tiles, long long num_kb, int pairs) {
+  if (pairs < 1 || pairs > kSkMaxPairs || tiles < 1) return false;
+  const long long waves = (tiles + pairs - 1) / pairs;
+  const double eff = static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+  return eff < kSkMinWaveEff && tiles * num_kb >= static_cast<long long>(kSkMinUnitsPerPair) * pairs;
+}
 
 // Row-fused LayerNorm / softmax candidates: the CTA-pair kernel (M > 128)
 // with a row-normalising epilogue.  Whether a launch fuses is decided at
@@ -302,6 +326,15 @@ bool rownorm_candidate(const GemmJob& j) {
   return epi_rownorm(j.epi) && !softmax_fused(j) && j.M > static_cast<uint32_t>(kBM);
 }
 size_t row_sync_count(const GemmJob& j) { return 2 * ((static_cast<size_t>(j.M) + 2 * kBM - 1) / (2 * kBM)); }
+
+// Stream-K candidates: the CTA-pair kernel with an epilogue other than the
+// row-normalising ones, when whole tiles would fill B200's pairs poorly.
+bool streamk_candidate(const GemmJob& j) {
+  if (j.M <= static_cast<uint32_t>(kBM) || epi_rownorm(j.epi) || !streamk_enabled()) return false;
+  const long long bn = epi_bn(j.epi);
+  const long long tiles = ((j.M + 2LL * kBM - 1) / (2 * kBM)) * ((j.N + bn - 1) / bn);
+  return streamk_wanted(tiles, (j.K + kBK - 1) / kBK, kSkMaxPairs);
+}
 
 size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
   const bool dual = epi_dual(j.epi);
@@ -339,13 +372,25 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
     else jb->stats = static_cast<float*>(grab(sb));
   }
   if (rownorm_candidate(j)) jb->row_sync = static_cast<unsigned int*>(grab(row_sync_count(j) * sizeof(unsigned int)));
+  if (streamk_candidate(j)) {
+    jb->sk_flags = static_cast<unsigned int*>(grab(2 * kSkMaxPairs * sizeof(unsigned int)));
+    jb->sk_part = static_cast<float*>(grab(static_cast<size_t>(2 * kSkMaxPairs) * kSkPartFloats * sizeof(float)));
+  }
   return cv.off;
 }
 
-// Row-fused LayerNorm / softmax switch: AKILI_ROWNORM=0 in the environment
-// selects the two-pass form (statistics, then a finaliser kernel).
-bool rownorm_enabled() {
+// Row-fused LayerNorm / softmax switch (environment AKILI_ROWNORM): unset or
+// 1 = deferred in-place normalise, 2 = normalise from TMEM after a row-block
+// wait, 0 = the two-pass form (statistics, then a finaliser kernel).
+// AKILI_COOP=0 launches the row-fused kernel without the cooperative
+// attribute (profilers that cannot replay cooperative cluster launches).
+int rownorm_mode() {
   const char* e = std::getenv("AKILI_ROWNORM");
+  if (!e || !e[0]) return 1;
+  return e[0] == '0' ? 0 : (e[0] == '2' ? 2 : 1);
+}
+bool coop_enabled() {
+  const char* e = std::getenv("AKILI_COOP");
   return !(e && e[0] == '0');
 }
 
@@ -362,7 +407,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
                      const CUtensorMap& tmC, const CUtensorMap& tmAlo, const CUtensorMap& tmB0lo,
                      const CUtensorMap& tmB1lo, EpiArgs ea, cudaStream_t st, bool* fused) {
   constexpr int BN = epi_bn(E);
-  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT), kSplit);
+  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT), kSplit, epi_rownorm(E));
   auto kern = gemm_pair_kernel<E, OutT, BK, kSplit>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -404,7 +449,9 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
   cfg.gridDim = dim3(2 * pairs);
   if (fused) *fused = false;
   if constexpr (epi_rownorm(E)) {
-    if (ea.row_sync && fused && num_n <= pairs && rownorm_enabled()) {
+    const int mode = rownorm_mode();
+    if (ea.row_sync && fused && num_n <= pairs && mode != 0) {
+      ea.rowfuse_mode = mode;
       const size_t nsync = 2 * static_cast<size_t>((ea.M + 2 * kBM - 1) / (2 * kBM));
       if (cudaMemsetAsync(ea.row_sync, 0, nsync * sizeof(unsigned int), st) != cudaSuccess) {
         cudaGetLastError();
@@ -412,7 +459,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
       }
       attr[1].id = cudaLaunchAttributeCooperative;
       attr[1].val.cooperative = 1;
-      cfg.numAttrs = 2;
+      cfg.numAttrs = coop_enabled() ? 2 : 1;
       if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) == cudaSuccess) {
         *fused = true;
         return launch_status();
@@ -422,6 +469,29 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
     }
   }
   ea.row_sync = nullptr;
+  if (ea.sk_flags) {
+    const int kbs = (ea.K + kBK - 1) / kBK;
+    if (pairs_cap <= kSkMaxPairs && streamk_enabled() && streamk_wanted(tiles, kbs, pairs_cap)) {
+      // every pair takes an equal share of the (tile, K-block) units; the
+      // owners wait only for lower pairs, and the cooperative launch keeps
+      // the grid resident
+      if (cudaMemsetAsync(ea.sk_flags, 0, 2 * static_cast<size_t>(pairs_cap) * sizeof(unsigned int), st) !=
+          cudaSuccess) {
+        cudaGetLastError();
+        return AKILI_E_LAUNCH;
+      }
+      cfg.gridDim = dim3(2 * pairs_cap);
+      attr[1].id = cudaLaunchAttributeCooperative;
+      attr[1].val.cooperative = 1;
+      cfg.numAttrs = coop_enabled() ? 2 : 1;
+      if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) == cudaSuccess)
+        return launch_status();
+      cudaGetLastError();  // refused: whole tiles below
+      cfg.numAttrs = 1;
+      cfg.gridDim = dim3(2 * pairs);
+    }
+    ea.sk_flags = nullptr;
+  }
   if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) != cudaSuccess) {
     cudaGetLastError();
     return AKILI_E_LAUNCH;
@@ -479,6 +549,10 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.ln_w = j.ln_w;
   ea.ln_b = j.ln_b;
   ea.eps = j.eps;
+  ea.c_out = j.C;
+  ea.rowfuse_mode = 0;
+  ea.sk_flags = jb.sk_flags;
+  ea.sk_part = jb.sk_part;
 
   // the lo parts of the split mode: the same boxes over the lo copies
   CUtensorMap tmAlo = tmA, tmB0lo = tmB0, tmB1lo = tmB1;

@@ -21,6 +21,7 @@
 #pragma once
 #include <cuda_fp16.h>
 
+#include "aux.cuh"
 #include "sm100.cuh"
 
 namespace akili {
@@ -78,6 +79,62 @@ struct EpiArgs {
   const float* ln_w;  // LayerNorm gamma / beta and eps (row-fused kLnPre)
   const float* ln_b;
   float eps;
+  void* c_out;        // the output (row-fused: normalised in place)
+  int rowfuse_mode;   // 1 = deferred in-place normalise, 2 = normalise from TMEM after a row-block wait
+  // Stream-K mode of the CTA-pair kernel (nullptr = one whole tile per work
+  // item): a ready flag per (pair, CTA), zeroed before the launch, and a
+  // 128 x 256 fp32 partial accumulator per (pair, CTA).
+  unsigned int* sk_flags;
+  float* sk_part;
+};
+
+// ---- stream-K work split of the CTA-pair kernel ----
+// The grid's npairs pairs share the num_tiles * num_kb (tile, K-block) units:
+// pair p takes the contiguous range [U p / P, U (p + 1) / P) and walks it from
+// its last unit down, one segment per tile it touches.  A tile's segment
+// holding its last K-block is its owner's: the owner adds the partial
+// accumulators of the lower pairs that hold the tile's earlier K-blocks and
+// runs the epilogue.  Every other partial segment is a contribution: its
+// accumulator goes to the pair's partial slot and the pair's flag is raised.
+// A pair contributes at most once, in its first segment, and an owner only
+// waits for lower pairs' first segments, so the waits never form a cycle.
+// Without stream-K each pair takes whole tiles pair, pair + npairs, ...
+constexpr int kSkFull = 0, kSkOwner = 1, kSkContrib = 2;
+constexpr int kSkPartFloats = kBM * 256;  // one CTA's partial: 128 rows x 256 TMEM columns
+
+struct PairWork {
+  long long U, u0, u;
+  int num_tiles, num_kb, npairs, next_tile;
+  bool sk;
+  __device__ PairWork(int tiles, int kbs, int pair, int pairs, bool stream_k)
+      : U(static_cast<long long>(tiles) * kbs), num_tiles(tiles), num_kb(kbs), npairs(pairs), next_tile(pair),
+        sk(stream_k) {
+    u0 = U * pair / pairs;
+    u = U * (pair + 1) / pairs;
+  }
+  // The pair whose range holds unit x.
+  __device__ int pair_of(long long x) const { return static_cast<int>(((x + 1) * npairs + U - 1) / U) - 1; }
+  __device__ bool next(int& tile, int& kb0, int& kb1, int& role, int& c_first) {
+    if (!sk) {
+      if (next_tile >= num_tiles) return false;
+      tile = next_tile;
+      next_tile += npairs;
+      kb0 = 0;
+      kb1 = num_kb;
+      role = kSkFull;
+      c_first = 0;
+      return true;
+    }
+    if (u <= u0) return false;
+    const long long t = (u - 1) / num_kb, lo = t * num_kb, s0 = u0 > lo ? u0 : lo;
+    tile = static_cast<int>(t);
+    kb0 = static_cast<int>(s0 - lo);
+    kb1 = static_cast<int>(u - lo);
+    role = kb1 == num_kb ? (kb0 == 0 ? kSkFull : kSkOwner) : kSkContrib;
+    c_first = role == kSkOwner ? pair_of(lo) : 0;
+    u = s0;
+    return true;
+  }
 };
 
 // Epilogues that normalise whole rows (longer than one tile).
@@ -256,10 +313,44 @@ __device__ __forceinline__ void stage_row(uint8_t* stage, int r, const float (&v
 // buffers) for TMA stores issued by `issuer`, or reduced to the row's
 // statistics, which are returned.  `bar_id` is the named barrier of these
 // 128 threads.
+// Stream-K owners pass the partial accumulators of their tile's `nskp`
+// contributors (`skp`: the first one's slot for this CTA, later ones
+// 2 * kSkPartFloats apart); they are added to each 64-column TMEM load.
+__device__ __forceinline__ void sk_add_partials(const float* skp, int nskp, int col, int r, float (&v)[64]) {
+  for (int ci = 0; ci < nskp; ++ci) {
+    const float4* p = reinterpret_cast<const float4*>(skp + static_cast<size_t>(ci) * 2 * kSkPartFloats);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const float4 f = __ldcg(p + (col / 4 + q) * kBM + r);
+      v[4 * q] += f.x;
+      v[4 * q + 1] += f.y;
+      v[4 * q + 2] += f.z;
+      v[4 * q + 3] += f.w;
+    }
+  }
+}
+
+// A stream-K contribution: this thread's row of TMEM columns [col0, col0 +
+// 128) into the partial slot `dst`, in the layout sk_add_partials reads
+// (4-column groups, row-minor, so a warp's 16-byte stores are contiguous).
+__device__ __forceinline__ void sk_write_partial(uint32_t tbase, int col0, int r, float* dst) {
+  float v[64];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int col = col0 + 64 * h;
+    tmem_ld64(tbase + col, v);
+    float4* p = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      __stcg(p + (col / 4 + q) * kBM + r, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+  }
+}
+
 template <Epi E, typename OutT>
 __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUtensorMap* tmC, uint32_t tbase, int n0,
                                                   int mrow0, int r, int c_begin, int c_end, uint8_t* staging,
-                                                  uint32_t bar_id, bool issuer, int& chunk_ctr) {
+                                                  uint32_t bar_id, bool issuer, int& chunk_ctr,
+                                                  const float* skp = nullptr, int nskp = 0) {
   constexpr bool kDual = epi_dual(E);
   constexpr bool kStore = epi_stores(E);
   constexpr int kStats = epi_stats(E);
@@ -276,6 +367,10 @@ __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUten
     if (!odd) {
       tmem_ld64(tbase + c * 32, v2);
       if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
+      if (nskp) {
+        sk_add_partials(skp, nskp, c * 32, r, v2);
+        if constexpr (kDual) sk_add_partials(skp, nskp, 128 + c * 32, r, reinterpret_cast<float(&)[64]>(u2));
+      }
     }
     float v[32];
     float u[32];
@@ -432,6 +527,72 @@ __device__ __forceinline__ void rownorm_half(const EpiArgs& ea, const CUtensorMa
     }
     ++chunk_ctr;
   }
+}
+
+// Deferred row-fused form: the CTA normalises its own 128 x 256 slice of a
+// tile in place, once every tile of the slice's row block has published its
+// statistics.  y was stored (rounded to OutT) by this CTA's TMA stores, which
+// have completed; the statistics are those of the stored values, as in the
+// two-pass form.  Threads 0..127 (of the 256 epilogue threads, ep) merge one
+// row each into shared memory; then warp w streams rows w, w + 8, ..., each
+// lane 8 columns, 16 (fp16) or 32 (fp32) bytes per row.  Reads bypass L1.
+template <Epi E, typename OutT>
+__device__ __forceinline__ void rownorm_slice(const EpiArgs& ea, int mrow0, int n0, int ep, float* s_a, float* s_b) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  if (ep < kBM) {
+    float a, b;
+    rowstats_merge<E>(ea, mrow0 + ep, a, b);
+    s_a[ep] = a;
+    s_b[ep] = b;
+  }
+  named_bar_sync(3, 256);
+  const int w = ep >> 5, lane = ep & 31;
+  const int col = n0 + lane * 8;
+  OutT* __restrict__ c = static_cast<OutT*>(ea.c_out);
+  if (col < ea.N) {
+    float g[8], bb[8];
+    if constexpr (E == Epi::kLnPre) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        g[i] = __ldg(ea.ln_w + col + i);
+        bb[i] = __ldg(ea.ln_b + col + i);
+      }
+    }
+    const int rows = min(kBM, ea.M - mrow0);
+    for (int r0 = w; r0 < rows; r0 += 32) {
+      Raw8<OutT> raw[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = r0 + 8 * q;
+        if (r < rows) {
+          const OutT* src = c + static_cast<size_t>(mrow0 + r) * ea.N + col;
+#pragma unroll
+          for (int k = 0; k < static_cast<int>(sizeof(OutT) / 2); ++k)
+            raw[q].v[k] = __ldcg(reinterpret_cast<const uint4*>(src) + k);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = r0 + 8 * q;
+        if (r < rows) {
+          float f[8];
+          raw8_to_float(raw[q], f);
+          const float sa = s_a[r], sb = s_b[r];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if constexpr (E == Epi::kLnPre) f[i] = ((f[i] - sa) * sb) * g[i] + bb[i];
+            else f[i] = exp2f(fmaf(f[i], kLog2e, -sa)) * sb;
+          }
+          store8(c + static_cast<size_t>(mrow0 + r) * ea.N + col, f);
+        }
+      }
+    }
+  }
+  named_bar_sync(3, 256);  // s_a / s_b are free again
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // Per-row partial statistics of one half tile go to slot `slot` of the
@@ -695,10 +856,12 @@ __host__ __device__ constexpr int pair_stages(bool stores, int out_bytes, bool s
   return split ? (stores && out_bytes == 4 ? 2 : 3) : (stores && out_bytes == 4 ? 5 : 6);
 }
 
-__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes, bool split = false) {
+__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes, bool split = false,
+                                                    bool rownorm = false) {
   int s = pair_stages(stores, out_bytes, split) * pair_stage_bytes(split);
   if (stores) s += 2 * 2 * kBM * 32 * out_bytes;
   s += 256 + 1024;
+  if (rownorm) s += 2 * kBM * sizeof(float);  // per-row statistics of the in-place normaliser
   return s;
 }
 
@@ -742,6 +905,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);  // one per epilogue group
+  volatile int* ready_flag = abort_flag + 2;  // deferred row-fused form: the oldest pending slice is ready
+  float* row_a = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [kBM] (row-fused only)
+  float* row_b = row_a + kBM;
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -757,6 +923,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   // Row-fused LayerNorm / softmax: tiles in row-block-major order, so the
   // tiles of one row block run in the same wave (see the epilogue).
   const bool rowfused = epi_rownorm(E) && ea.row_sync != nullptr;
+  const bool stream_k = !rowfused && ea.sk_flags != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
@@ -794,12 +961,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      PairWork work(num_tiles, num_kb, pair, npairs, stream_k);
+      int tile, kb0, kb1, role, c_first;
+      while (ok && work.next(tile, kb0, kb1, role, c_first)) {
         int m_blk, n_blk;
         pair_tile_coords(tile, num_m, num_n, rowfused, m_blk, n_blk);
         const int row0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
         const int col0 = n_blk * BN + static_cast<int>(rank) * BNH;
-        for (int kb = 0; kb < num_kb && ok; ++kb) {
+        for (int kb = kb0; kb < kb1 && ok; ++kb) {
           ok = mbar_wait_cluster(&empty[stage], phase ^ 1, kSiteProducerEmpty);
           if (!ok) break;
           uint8_t* sa = ring + stage * kSB;
@@ -854,14 +1023,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++it) {
+      PairWork work(num_tiles, num_kb, pair, npairs, stream_k);
+      int tile, kb0, kb1, role, c_first;
+      for (; ok && work.next(tile, kb0, kb1, role, c_first); ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         ok = mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
         if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccCols;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           ok = mbar_wait_cluster(&full[stage], phase, kSiteMmaFull);
           if (!ok) break;
           tc_fence_after();
@@ -870,7 +1041,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
-            const uint32_t accum = (kb | k) != 0;
+            const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
             const uint64_t bd = kBKMajor ? make_sdesc(sb + k * 32, 16, 1024, kSw128)
                                          : make_sdesc(sb + k * 2048, 8192, 1024, kSw128);
             umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
@@ -908,7 +1079,96 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     constexpr int HC = BN / 64;  // chunks per half tile
     int it = 0;
     int chunk_ctr = 0;
-    if (rowfused) {
+    if (rowfused && ea.rowfuse_mode == 1) {
+      // Deferred row-fused LayerNorm / softmax.  Per tile, as the two-pass
+      // form: y (rounded to OutT) goes out through the TMA stores and each
+      // row's statistics of its half tile to the workspace; the accumulator
+      // is released at once.  When this CTA's stores have completed it
+      // arrives on its 128-row block's counter.  A slice whose row block has
+      // all num_n arrivals is normalised in place by this CTA (rownorm_slice)
+      // while y is still in L2: the oldest pending slice is tried after each
+      // tile, and the rest are waited for after the last tile.  No wait holds
+      // an accumulator, and the waits after the last tile depend only on
+      // other CTAs' tiles, which never wait; the cooperative launch keeps
+      // those CTAs resident.  Both epilogue groups share barrier 3 and
+      // abort_flag[0].
+      constexpr int kMaxPend = 4;
+      int pend_m[kMaxPend], pend_n[kMaxPend];
+      int npend = 0;
+      const int ep = threadIdx.x - 64;  // 0..255
+      auto slice_ready = [&](int m_blk, bool block) -> bool {
+        if (threadIdx.x == 64) {
+          const unsigned int* cnt = ea.row_sync + m_blk * 2 + rank;
+          bool ok;
+          if (block) {
+            ok = counter_wait_geq(cnt, static_cast<unsigned int>(num_n), kSiteRowSync);
+            if (!ok) abort_flag[0] = 1;
+          } else {
+            unsigned int v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+            ok = v >= static_cast<unsigned int>(num_n);
+          }
+          *ready_flag = ok ? 1 : 0;
+        }
+        named_bar_sync(3, 256);
+        const bool ok = *ready_flag != 0 && !abort_flag[0];
+        named_bar_sync(3, 256);  // everyone has read ready_flag before it is written again
+        return ok;
+      };
+      auto pop_slice = [&]() {
+        __threadfence();
+        rownorm_slice<E, OutT>(ea, pend_m[0] * 2 * kBM + static_cast<int>(rank) * kBM, pend_n[0] * BN, ep, row_a,
+                               row_b);
+        for (int q = 1; q < npend; ++q) {
+          pend_m[q - 1] = pend_m[q];
+          pend_n[q - 1] = pend_n[q];
+        }
+        --npend;
+      };
+      for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+        int m_blk, n_blk;
+        pair_tile_coords(tile, num_m, num_n, true, m_blk, n_blk);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[0] = 1;
+        named_bar_sync(3, 256);
+        if (abort_flag[0]) break;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
+        const int n0 = n_blk * BN;
+        const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
+        const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
+                                                   min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
+                                                   chunk_ctr);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&acc_empty[acc]);
+          else mbar_arrive_cluster(acc_empty_c + acc * 8);
+        }
+        write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
+        if (gtid == 0) {
+          bulk_wait<0>();  // this group's y has reached memory
+          fence_proxy_async_global();
+        }
+        __threadfence();
+        named_bar_sync(3, 256);
+        if (threadIdx.x == 64) atomicAdd(ea.row_sync + mrow0 / kBM, 1u);
+        if (npend == kMaxPend) {
+          if (!slice_ready(pend_m[0], true)) break;
+          pop_slice();
+        }
+        pend_m[npend] = m_blk;
+        pend_n[npend] = n_blk;
+        ++npend;
+        if (slice_ready(pend_m[0], false)) pop_slice();
+      }
+      while (npend > 0 && !abort_flag[0]) {
+        if (!slice_ready(pend_m[0], true)) break;
+        pop_slice();
+      }
+    } else if (rowfused) {
       // Row-fused LayerNorm / softmax.  Per tile: pass 1 reads this CTA's
       // accumulator and publishes each row's statistics of its half tile;
       // the CTA then arrives on its 128-row block's counter and waits until
@@ -959,6 +1219,57 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if (leader) mbar_arrive(&acc_empty[acc]);
           else mbar_arrive_cluster(acc_empty_c + acc * 8);
         }
+      }
+    } else if (stream_k) {
+      // Stream-K: as below, per segment of PairWork.  A contribution writes
+      // the CTA's accumulator to this pair's partial slot and raises the
+      // pair's flag; an owner first waits for the flags of the lower pairs
+      // that contributed to its tile (bounded), then adds their partials in
+      // the epilogue.  Both groups share barrier 3 and abort_flag[0].
+      PairWork work(num_tiles, num_kb, pair, npairs, true);
+      int tile, kb0, kb1, role, c_first;
+      for (; work.next(tile, kb0, kb1, role, c_first); ++it) {
+        int m_blk, n_blk;
+        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[0] = 1;
+        if (role == kSkOwner && threadIdx.x == 64) {
+          for (int c = c_first; c < pair; ++c)
+            if (!counter_wait_geq(ea.sk_flags + 2 * c + rank, 1u, kSiteStreamK)) abort_flag[0] = 1;
+        }
+        named_bar_sync(3, 256);
+        if (abort_flag[0]) break;
+        if (role == kSkOwner) __threadfence();
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
+        if (role == kSkContrib) {
+          sk_write_partial(tbase, grp * 128, r, ea.sk_part + static_cast<size_t>(2 * pair + rank) * kSkPartFloats);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) mbar_arrive(&acc_empty[acc]);
+            else mbar_arrive_cluster(acc_empty_c + acc * 8);
+          }
+          __threadfence();
+          named_bar_sync(3, 256);
+          if (threadIdx.x == 64) atomicExch(ea.sk_flags + 2 * pair + rank, 1u);
+          continue;
+        }
+        const int n0 = n_blk * BN;
+        const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
+        const float* skp = ea.sk_part + static_cast<size_t>(2 * c_first + rank) * kSkPartFloats;
+        const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
+                                                   min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
+                                                   chunk_ctr, skp, role == kSkOwner ? pair - c_first : 0);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(&acc_empty[acc]);
+          else mbar_arrive_cluster(acc_empty_c + acc * 8);
+        }
+        write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
       }
     } else {
       for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {

@@ -38,6 +38,7 @@ enum WaitSite : uint32_t {
   kSiteSelfTest = 12,
   kSiteExchange = 13,
   kSiteRowSync = 14,
+  kSiteStreamK = 15,
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {

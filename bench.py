@@ -861,7 +861,14 @@ def run_ours(args):
     modes = [args.scaling] + (["weak"] if world > 1 and args.scaling == "strong" and not args.no_weak else [])
     results = {}
     for mode in modes:
-        W = workloads(torch, ops, Part(world, rank, mode))
+        if args.shard_of > 1:
+            # one rank's share of an N-way row split, measured alone on this GPU
+            W = workloads(torch, ops, Part(args.shard_of, 0, "strong"))
+            for wl in W.values():
+                wl.flops_total = wl.flops * world
+                wl.desc["shard"] = f"rank 0 of {args.shard_of}"
+        else:
+            W = workloads(torch, ops, Part(world, rank, mode))
         names = list(W) if args.op == "all" else [args.op]
         for name in names:
             if mode == "weak" and W[name].split == "replicas":
@@ -910,6 +917,9 @@ def main():
                     help="strong: the configured global problem split across the GPUs (default); weak: every GPU "
                          "runs the full per-GPU workload.  With strong at N>1 a weak run follows as a second field")
     ap.add_argument("--no-weak", action="store_true", help="skip the second (weak) run at N>1")
+    ap.add_argument("--shard-of", type=int, default=1, metavar="G",
+                    help="measure rank 0's share of a G-way strong split on this GPU alone (profiling the small "
+                         "per-GPU problems of the multi-GPU split); value is then this GPU's work")
     ap.add_argument("--no-link-probe", dest="link_probe", action="store_false",
                     help="skip the host-link copy probe that states e2e against the link's ceiling")
     ap.add_argument("--soak", type=float, default=1.0,
