@@ -379,16 +379,29 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
   return cv.off;
 }
 
-// Row-fused LayerNorm / softmax switch (environment AKILI_ROWNORM): unset or
-// 1 = deferred in-place normalise, 2 = normalise from TMEM after a row-block
-// wait, 0 = the two-pass form (statistics, then a finaliser kernel).
-// AKILI_COOP=0 launches the row-fused kernel without the cooperative
-// attribute (profilers that cannot replay cooperative cluster launches).
-int rownorm_mode() {
+// Row-fused LayerNorm / softmax switch: AKILI_ROWNORM=0 in the environment
+// selects the two-pass form (statistics, then a finaliser kernel).
+// AKILI_COOP=0 launches the row-fused (and stream-K) kernel without the
+// cooperative attribute, for profilers that cannot replay cooperative
+// cluster launches.
+bool rownorm_enabled() {
   const char* e = std::getenv("AKILI_ROWNORM");
-  if (!e || !e[0]) return 1;
-  return e[0] == '0' ? 0 : (e[0] == '2' ? 2 : 1);
+  return !(e && e[0] == '0');
 }
+// Tile order of the CTA-pair kernel: row-block-major when the B operand
+// (K x N fp16, both weights for the dual GEMMs) fits well inside L2, so each
+// A row block is read from HBM once while B stays resident (C2: 115 against
+// 167 MB of DRAM reads per launch, same time); groups of row blocks otherwise
+// (C4's 172 MB of weights: row-major re-reads them and ran 26% slower).
+// AKILI_RASTER=row / group in the environment forces one.
+constexpr uint64_t kRowMajorMaxB = 48ull << 20;
+bool raster_row_major(uint64_t b_bytes) {
+  const char* e = std::getenv("AKILI_RASTER");
+  if (e && e[0] == 'r') return true;
+  if (e && e[0] == 'g') return false;
+  return b_bytes <= kRowMajorMaxB;
+}
+
 bool coop_enabled() {
   const char* e = std::getenv("AKILI_COOP");
   return !(e && e[0] == '0');
@@ -407,7 +420,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
                      const CUtensorMap& tmC, const CUtensorMap& tmAlo, const CUtensorMap& tmB0lo,
                      const CUtensorMap& tmB1lo, EpiArgs ea, cudaStream_t st, bool* fused) {
   constexpr int BN = epi_bn(E);
-  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT), kSplit, epi_rownorm(E));
+  const int smem = gemm_pair_smem_bytes(epi_stores(E), sizeof(OutT), kSplit);
   auto kern = gemm_pair_kernel<E, OutT, BK, kSplit>;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -449,9 +462,7 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
   cfg.gridDim = dim3(2 * pairs);
   if (fused) *fused = false;
   if constexpr (epi_rownorm(E)) {
-    const int mode = rownorm_mode();
-    if (ea.row_sync && fused && num_n <= pairs && mode != 0) {
-      ea.rowfuse_mode = mode;
+    if (ea.row_sync && fused && num_n <= pairs && rownorm_enabled()) {
       const size_t nsync = 2 * static_cast<size_t>((ea.M + 2 * kBM - 1) / (2 * kBM));
       if (cudaMemsetAsync(ea.row_sync, 0, nsync * sizeof(unsigned int), st) != cudaSuccess) {
         cudaGetLastError();
@@ -549,10 +560,9 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.ln_w = j.ln_w;
   ea.ln_b = j.ln_b;
   ea.eps = j.eps;
-  ea.c_out = j.C;
-  ea.rowfuse_mode = 0;
   ea.sk_flags = jb.sk_flags;
   ea.sk_part = jb.sk_part;
+  ea.row_major = raster_row_major(K * N * 2 * (epi_dual(E) ? 2 : 1) * (kSplit ? 2 : 1)) ? 1 : 0;
 
   // the lo parts of the split mode: the same boxes over the lo copies
   CUtensorMap tmAlo = tmA, tmB0lo = tmB0, tmB1lo = tmB1;
@@ -1146,6 +1156,10 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
   fa.causal = md.causal ? 1 : 0;
   fa.m_out = j.m_out;
   fa.l_out = j.l_out;
+  {
+    const char* e = std::getenv("AKILI_FLASH_PINGPONG");
+    fa.pingpong = (e && e[0] == '1') ? 1 : 0;
+  }
   dim3 grid((j.seq_len + kFlashBM * kFlashQTiles - 1) / (kFlashBM * kFlashQTiles), bh);
   if (split) rc = launch_flash<64, true>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
   else if (dpad == 64) rc = launch_flash<64, false>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);

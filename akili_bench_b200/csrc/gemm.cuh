@@ -21,7 +21,6 @@
 #pragma once
 #include <cuda_fp16.h>
 
-#include "aux.cuh"
 #include "sm100.cuh"
 
 namespace akili {
@@ -79,13 +78,15 @@ struct EpiArgs {
   const float* ln_w;  // LayerNorm gamma / beta and eps (row-fused kLnPre)
   const float* ln_b;
   float eps;
-  void* c_out;        // the output (row-fused: normalised in place)
-  int rowfuse_mode;   // 1 = deferred in-place normalise, 2 = normalise from TMEM after a row-block wait
   // Stream-K mode of the CTA-pair kernel (nullptr = one whole tile per work
   // item): a ready flag per (pair, CTA), zeroed before the launch, and a
   // 128 x 256 fp32 partial accumulator per (pair, CTA).
   unsigned int* sk_flags;
   float* sk_part;
+  // CTA-pair tile order: 1 = row-block-major (every column tile of a row
+  // block in turn; the B panels stay in L2 when B fits there), 0 = groups of
+  // kGroupM row blocks walked row-block-fastest.
+  int row_major;
 };
 
 // ---- stream-K work split of the CTA-pair kernel ----
@@ -529,72 +530,6 @@ __device__ __forceinline__ void rownorm_half(const EpiArgs& ea, const CUtensorMa
   }
 }
 
-// Deferred row-fused form: the CTA normalises its own 128 x 256 slice of a
-// tile in place, once every tile of the slice's row block has published its
-// statistics.  y was stored (rounded to OutT) by this CTA's TMA stores, which
-// have completed; the statistics are those of the stored values, as in the
-// two-pass form.  Threads 0..127 (of the 256 epilogue threads, ep) merge one
-// row each into shared memory; then warp w streams rows w, w + 8, ..., each
-// lane 8 columns, 16 (fp16) or 32 (fp32) bytes per row.  Reads bypass L1.
-template <Epi E, typename OutT>
-__device__ __forceinline__ void rownorm_slice(const EpiArgs& ea, int mrow0, int n0, int ep, float* s_a, float* s_b) {
-  constexpr float kLog2e = 1.4426950408889634f;
-  if (ep < kBM) {
-    float a, b;
-    rowstats_merge<E>(ea, mrow0 + ep, a, b);
-    s_a[ep] = a;
-    s_b[ep] = b;
-  }
-  named_bar_sync(3, 256);
-  const int w = ep >> 5, lane = ep & 31;
-  const int col = n0 + lane * 8;
-  OutT* __restrict__ c = static_cast<OutT*>(ea.c_out);
-  if (col < ea.N) {
-    float g[8], bb[8];
-    if constexpr (E == Epi::kLnPre) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        g[i] = __ldg(ea.ln_w + col + i);
-        bb[i] = __ldg(ea.ln_b + col + i);
-      }
-    }
-    const int rows = min(kBM, ea.M - mrow0);
-    for (int r0 = w; r0 < rows; r0 += 32) {
-      Raw8<OutT> raw[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = r0 + 8 * q;
-        if (r < rows) {
-          const OutT* src = c + static_cast<size_t>(mrow0 + r) * ea.N + col;
-#pragma unroll
-          for (int k = 0; k < static_cast<int>(sizeof(OutT) / 2); ++k)
-            raw[q].v[k] = __ldcg(reinterpret_cast<const uint4*>(src) + k);
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = r0 + 8 * q;
-        if (r < rows) {
-          float f[8];
-          raw8_to_float(raw[q], f);
-          const float sa = s_a[r], sb = s_b[r];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if constexpr (E == Epi::kLnPre) f[i] = ((f[i] - sa) * sb) * g[i] + bb[i];
-            else f[i] = exp2f(fmaf(f[i], kLog2e, -sa)) * sb;
-          }
-          store8(c + static_cast<size_t>(mrow0 + r) * ea.N + col, f);
-        }
-      }
-    }
-  }
-  named_bar_sync(3, 256);  // s_a / s_b are free again
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // Per-row partial statistics of one half tile go to slot `slot` of the
 // [stat][slot][M] workspace (two slots per BN-column tile).
 template <Epi E>
@@ -856,12 +791,10 @@ __host__ __device__ constexpr int pair_stages(bool stores, int out_bytes, bool s
   return split ? (stores && out_bytes == 4 ? 2 : 3) : (stores && out_bytes == 4 ? 5 : 6);
 }
 
-__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes, bool split = false,
-                                                    bool rownorm = false) {
+__host__ __device__ inline int gemm_pair_smem_bytes(bool stores, int out_bytes, bool split = false) {
   int s = pair_stages(stores, out_bytes, split) * pair_stage_bytes(split);
   if (stores) s += 2 * 2 * kBM * 32 * out_bytes;
   s += 256 + 1024;
-  if (rownorm) s += 2 * kBM * sizeof(float);  // per-row statistics of the in-place normaliser
   return s;
 }
 
@@ -905,9 +838,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);  // one per epilogue group
-  volatile int* ready_flag = abort_flag + 2;  // deferred row-fused form: the oldest pending slice is ready
-  float* row_a = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [kBM] (row-fused only)
-  float* row_b = row_a + kBM;
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -924,6 +854,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   // tiles of one row block run in the same wave (see the epilogue).
   const bool rowfused = epi_rownorm(E) && ea.row_sync != nullptr;
   const bool stream_k = !rowfused && ea.sk_flags != nullptr;
+  const bool row_major = rowfused || ea.row_major != 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
@@ -965,7 +896,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int tile, kb0, kb1, role, c_first;
       while (ok && work.next(tile, kb0, kb1, role, c_first)) {
         int m_blk, n_blk;
-        pair_tile_coords(tile, num_m, num_n, rowfused, m_blk, n_blk);
+        pair_tile_coords(tile, num_m, num_n, row_major, m_blk, n_blk);
         const int row0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
         const int col0 = n_blk * BN + static_cast<int>(rank) * BNH;
         for (int kb = kb0; kb < kb1 && ok; ++kb) {
@@ -1079,96 +1010,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     constexpr int HC = BN / 64;  // chunks per half tile
     int it = 0;
     int chunk_ctr = 0;
-    if (rowfused && ea.rowfuse_mode == 1) {
-      // Deferred row-fused LayerNorm / softmax.  Per tile, as the two-pass
-      // form: y (rounded to OutT) goes out through the TMA stores and each
-      // row's statistics of its half tile to the workspace; the accumulator
-      // is released at once.  When this CTA's stores have completed it
-      // arrives on its 128-row block's counter.  A slice whose row block has
-      // all num_n arrivals is normalised in place by this CTA (rownorm_slice)
-      // while y is still in L2: the oldest pending slice is tried after each
-      // tile, and the rest are waited for after the last tile.  No wait holds
-      // an accumulator, and the waits after the last tile depend only on
-      // other CTAs' tiles, which never wait; the cooperative launch keeps
-      // those CTAs resident.  Both epilogue groups share barrier 3 and
-      // abort_flag[0].
-      constexpr int kMaxPend = 4;
-      int pend_m[kMaxPend], pend_n[kMaxPend];
-      int npend = 0;
-      const int ep = threadIdx.x - 64;  // 0..255
-      auto slice_ready = [&](int m_blk, bool block) -> bool {
-        if (threadIdx.x == 64) {
-          const unsigned int* cnt = ea.row_sync + m_blk * 2 + rank;
-          bool ok;
-          if (block) {
-            ok = counter_wait_geq(cnt, static_cast<unsigned int>(num_n), kSiteRowSync);
-            if (!ok) abort_flag[0] = 1;
-          } else {
-            unsigned int v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
-            ok = v >= static_cast<unsigned int>(num_n);
-          }
-          *ready_flag = ok ? 1 : 0;
-        }
-        named_bar_sync(3, 256);
-        const bool ok = *ready_flag != 0 && !abort_flag[0];
-        named_bar_sync(3, 256);  // everyone has read ready_flag before it is written again
-        return ok;
-      };
-      auto pop_slice = [&]() {
-        __threadfence();
-        rownorm_slice<E, OutT>(ea, pend_m[0] * 2 * kBM + static_cast<int>(rank) * kBM, pend_n[0] * BN, ep, row_a,
-                               row_b);
-        for (int q = 1; q < npend; ++q) {
-          pend_m[q - 1] = pend_m[q];
-          pend_n[q - 1] = pend_n[q];
-        }
-        --npend;
-      };
-      for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
-        int m_blk, n_blk;
-        pair_tile_coords(tile, num_m, num_n, true, m_blk, n_blk);
-        const int acc = it & 1;
-        const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[0] = 1;
-        named_bar_sync(3, 256);
-        if (abort_flag[0]) break;
-        tc_fence_after();
-        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
-        const int n0 = n_blk * BN;
-        const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-        const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
-                                                   min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
-                                                   chunk_ctr);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) mbar_arrive(&acc_empty[acc]);
-          else mbar_arrive_cluster(acc_empty_c + acc * 8);
-        }
-        write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
-        if (gtid == 0) {
-          bulk_wait<0>();  // this group's y has reached memory
-          fence_proxy_async_global();
-        }
-        __threadfence();
-        named_bar_sync(3, 256);
-        if (threadIdx.x == 64) atomicAdd(ea.row_sync + mrow0 / kBM, 1u);
-        if (npend == kMaxPend) {
-          if (!slice_ready(pend_m[0], true)) break;
-          pop_slice();
-        }
-        pend_m[npend] = m_blk;
-        pend_n[npend] = n_blk;
-        ++npend;
-        if (slice_ready(pend_m[0], false)) pop_slice();
-      }
-      while (npend > 0 && !abort_flag[0]) {
-        if (!slice_ready(pend_m[0], true)) break;
-        pop_slice();
-      }
-    } else if (rowfused) {
+    if (rowfused) {
       // Row-fused LayerNorm / softmax.  Per tile: pass 1 reads this CTA's
       // accumulator and publishes each row's statistics of its half tile;
       // the CTA then arrives on its 128-row block's counter and waits until
@@ -1230,7 +1072,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int tile, kb0, kb1, role, c_first;
       for (; work.next(tile, kb0, kb1, role, c_first); ++it) {
         int m_blk, n_blk;
-        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        pair_tile_coords(tile, num_m, num_n, row_major, m_blk, n_blk);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[0] = 1;
@@ -1274,7 +1116,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     } else {
       for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
         int m_blk, n_blk;
-        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        pair_tile_coords(tile, num_m, num_n, row_major, m_blk, n_blk);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         // Each group reads only its own flag, after its own barrier, so all of

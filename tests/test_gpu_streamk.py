@@ -143,7 +143,7 @@ def test_streamk_kb2_split_mode(oracle, monkeypatch):
     b = rng.standard_normal(N).astype(np.float32) * 0.1
     f32 = torch.float32
     sk, dp = both_modes(monkeypatch, lambda: ops.kb2_gemm_add_relu(dev(x, f32), dev(w, f32), dev(b, f32)))
-    close(sk, dp, 1e-5)
+    close(sk, dp, 1e-4)  # the split mode's own bar (about 2^-21 per product)
     rows = sample_rows(M)
     ref = oracle.kb2_gemm_add_relu(np.ascontiguousarray(x[rows]), w, b, len(rows), N, K, threads=8)
     scale = np.abs(ref).max()
