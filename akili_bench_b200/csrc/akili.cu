@@ -1156,10 +1156,6 @@ int run_flash(const FlashJob& j, const Mode& md, cudaStream_t st) {
   fa.causal = md.causal ? 1 : 0;
   fa.m_out = j.m_out;
   fa.l_out = j.l_out;
-  {
-    const char* e = std::getenv("AKILI_FLASH_PINGPONG");
-    fa.pingpong = (e && e[0] == '1') ? 1 : 0;
-  }
   dim3 grid((j.seq_len + kFlashBM * kFlashQTiles - 1) / (kFlashBM * kFlashQTiles), bh);
   if (split) rc = launch_flash<64, true>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);
   else if (dpad == 64) rc = launch_flash<64, false>(grid, md.out_f32, tq, tk, tv, to, tql, tkl, fa, st);

@@ -61,7 +61,6 @@ struct FlashArgs {
   int causal;        // 1: query i sees keys j <= i only
   float* m_out;      // optional [bh][seq_len]: row max of the scaled scores
   float* l_out;      // optional [bh][seq_len]: sum_j exp(score_j - m)
-  int pingpong;      // 1: the two Q tiles take turns for their exponentials (see the softmax loop)
 };
 
 // kSplit: Q and K also carry their fp16 low parts (x - fp16(x)), doubling
@@ -114,9 +113,6 @@ __global__ void __maxnreg__(96)
   // [tile][parity]: a wait that gave up in block j sets slot j & 1, read by
   // the whole tile after block j's barrier (the next block's slot is apart)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
-  // [tile]: a phase completes when the other tile's softmax warps have
-  // written their P of a key block (ping-pong of the exponential passes)
-  uint64_t* turn = bars + 20;
 
   const int N = fa.seq_len;
   // Causal: the CTA of query tile pair x visits 2x + 2 key blocks, so the
@@ -149,8 +145,6 @@ __global__ void __maxnreg__(96)
       mbar_init(&o_done[s], 1);
     }
     mbar_init(drain, 1);
-    mbar_init(&turn[0], 8);  // one arrive per softmax warp of the other tile
-    mbar_init(&turn[1], 8);
     for (int i = 0; i < 2 * kFlashQTiles; ++i) abort_flag[i] = 0;
     fence_mbar_init();
   }
@@ -331,17 +325,6 @@ __global__ void __maxnreg__(96)
         ok = false;
         break;
       }
-      // Ping-pong: the tiles' exponential passes take turns, tile 0 for
-      // block j after tile 1's block j - 1, tile 1 for block j after tile
-      // 0's block j (when tile 0 has one; under causal masking it may stop a
-      // block early), so the two do not share the MUFU while the tensor core
-      // waits for both.
-      if (fa.pingpong) {
-        const bool need = grp == 0 ? j >= 1 : j < nkv_t0;
-        if (need && !mbar_wait(&turn[grp], grp == 0 ? ((j - 1) & 1) : (j & 1), kSiteFlashTurn)) {
-          abort_flag[2 * grp + (j & 1)] = 1;
-        }
-      }
       const float rmax = sl * fmaxf(pmax, xs[(half ^ 1) * kFlashBM + r]);
       m_true = fmaxf(m_true, rmax);
       const bool grow = rmax > m_use + kRescaleThreshold;
@@ -371,11 +354,6 @@ __global__ void __maxnreg__(96)
         pk[i] = __uint_as_float(pack_half2(p0, p1));
       }
       tmem_st32(tP, pk);
-      if (fa.pingpong) {
-        // this warp's exponentials are done: the other tile may start its turn
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&turn[grp ^ 1]);
-      }
       float sv[8];
 #pragma unroll
       for (int a = 0; a < 4; ++a) f2_unpack(sm2[a], sv[2 * a], sv[2 * a + 1]);

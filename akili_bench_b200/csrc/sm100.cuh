@@ -39,7 +39,6 @@ enum WaitSite : uint32_t {
   kSiteExchange = 13,
   kSiteRowSync = 14,
   kSiteStreamK = 15,
-  kSiteFlashTurn = 16,
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
