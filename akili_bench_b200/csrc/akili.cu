@@ -298,18 +298,19 @@ struct JobBuffers {
 };
 
 // ---- stream-K ----
-// The CTA-pair kernel runs whole tiles per pair unless the tiles fill its
-// waves poorly: with efficiency tiles / (ceil(tiles / P) * P) below
-// kSkMinWaveEff over P pairs (the small per-GPU M of a row-split GEMM), the
-// (tile, K-block) units are split evenly over the pairs (stream-K).
-// AKILI_STREAMK=0 in the environment keeps whole tiles.
+// With AKILI_STREAMK=1 in the environment, a CTA-pair GEMM whose tiles fill
+// the pairs' waves poorly (efficiency tiles / (ceil(tiles / P) * P) below
+// kSkMinWaveEff over P pairs: the small per-GPU M of a row-split GEMM) splits
+// its (tile, K-block) units evenly over the pairs.  Whole tiles are the
+// default: on a B200 the split measured slower at every per-GPU share of C2
+// (1024 rows: 50.0 against 40.8 us a step).
 constexpr int kSkMaxPairs = 74;          // partial slots laid out for a B200's 148 SMs
 constexpr double kSkMinWaveEff = 0.96;
 constexpr int kSkMinUnitsPerPair = 8;    // K-blocks per pair below which splitting does not pay
 
 bool streamk_enabled() {
   const char* e = std::getenv("AKILI_STREAMK");
-  return !(e && e[0] == '0');
+  return e && e[0] == '1';
 }
 
 bool streamk_wanted(long long tiles, long long num_kb, int pairs) {

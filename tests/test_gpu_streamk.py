@@ -5,7 +5,8 @@ When a GEMM's 256-row tiles fill the CTA pairs' waves poorly (the small
 per-GPU M of a row-split GEMM: C2's 8192 rows over 8 GPUs leave 64 tiles for
 74 pairs), the (tile, K-block) units are split evenly over the pairs; a
 tile's owner adds the partial accumulators of the pairs that computed its
-earlier K-blocks before the epilogue.  AKILI_STREAMK=0 keeps whole tiles.
+earlier K-blocks before the epilogue.  AKILI_STREAMK=1 selects it (whole
+tiles are the default).
 Each case checks the stream-K output against the oracle on sampled rows
 (the parity bar) and against the whole-tile output on every element (the
 two differ only in the order of the fp32 K-block sums), and the launch
