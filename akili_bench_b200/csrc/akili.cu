@@ -293,32 +293,7 @@ struct JobBuffers {
   __half* B1lo = nullptr;
   float* stats = nullptr;
   unsigned int* row_sync = nullptr;  // row-fused LayerNorm / softmax: one counter per 128-row block
-  unsigned int* sk_flags = nullptr;  // stream-K: a ready flag and a partial slot per (pair, CTA)
-  float* sk_part = nullptr;
 };
-
-// ---- stream-K ----
-// With AKILI_STREAMK=1 in the environment, a CTA-pair GEMM whose tiles fill
-// the pairs' waves poorly (efficiency tiles / (ceil(tiles / P) * P) below
-// kSkMinWaveEff over P pairs: the small per-GPU M of a row-split GEMM) splits
-// its (tile, K-block) units evenly over the pairs.  Whole tiles are the
-// default: on a B200 the split measured slower at every per-GPU share of C2
-// (1024 rows: 50.0 against 40.8 us a step).
-constexpr int kSkMaxPairs = 74;          // partial slots laid out for a B200's 148 SMs
-constexpr double kSkMinWaveEff = 0.96;
-constexpr int kSkMinUnitsPerPair = 8;    // K-blocks per pair below which splitting does not pay
-
-bool streamk_enabled() {
-  const char* e = std::getenv("AKILI_STREAMK");
-  return e && e[0] == '1';
-}
-
-bool streamk_wanted(long long tiles, long long num_kb, int pairs) {
-  if (pairs < 1 || pairs > kSkMaxPairs || tiles < 1) return false;
-  const long long waves = (tiles + pairs - 1) / pairs;
-  const double eff = static_cast<double>(tiles) / static_cast<double>(waves * pairs);
-  return eff < kSkMinWaveEff && tiles * num_kb >= static_cast<long long>(kSkMinUnitsPerPair) * pairs;
-}
 
 // Row-fused LayerNorm / softmax candidates: the CTA-pair kernel (M > 128)
 // with a row-normalising epilogue.  Whether a launch fuses is decided at
@@ -327,15 +302,6 @@ bool rownorm_candidate(const GemmJob& j) {
   return epi_rownorm(j.epi) && !softmax_fused(j) && j.M > static_cast<uint32_t>(kBM);
 }
 size_t row_sync_count(const GemmJob& j) { return 2 * ((static_cast<size_t>(j.M) + 2 * kBM - 1) / (2 * kBM)); }
-
-// Stream-K candidates: the CTA-pair kernel with an epilogue other than the
-// row-normalising ones, when whole tiles would fill B200's pairs poorly.
-bool streamk_candidate(const GemmJob& j) {
-  if (j.M <= static_cast<uint32_t>(kBM) || epi_rownorm(j.epi) || !streamk_enabled()) return false;
-  const long long bn = epi_bn(j.epi);
-  const long long tiles = ((j.M + 2LL * kBM - 1) / (2 * kBM)) * ((j.N + bn - 1) / bn);
-  return streamk_wanted(tiles, (j.K + kBK - 1) / kBK, kSkMaxPairs);
-}
 
 size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
   const bool dual = epi_dual(j.epi);
@@ -373,18 +339,13 @@ size_t layout_job(const GemmJob& j, const Mode& md, Carve& cv, JobBuffers* jb) {
     else jb->stats = static_cast<float*>(grab(sb));
   }
   if (rownorm_candidate(j)) jb->row_sync = static_cast<unsigned int*>(grab(row_sync_count(j) * sizeof(unsigned int)));
-  if (streamk_candidate(j)) {
-    jb->sk_flags = static_cast<unsigned int*>(grab(2 * kSkMaxPairs * sizeof(unsigned int)));
-    jb->sk_part = static_cast<float*>(grab(static_cast<size_t>(2 * kSkMaxPairs) * kSkPartFloats * sizeof(float)));
-  }
   return cv.off;
 }
 
 // Row-fused LayerNorm / softmax switch: AKILI_ROWNORM=0 in the environment
 // selects the two-pass form (statistics, then a finaliser kernel).
-// AKILI_COOP=0 launches the row-fused (and stream-K) kernel without the
-// cooperative attribute, for profilers that cannot replay cooperative
-// cluster launches.
+// AKILI_COOP=0 launches the row-fused kernel without the cooperative
+// attribute, for profilers that cannot replay cooperative cluster launches.
 bool rownorm_enabled() {
   const char* e = std::getenv("AKILI_ROWNORM");
   return !(e && e[0] == '0');
@@ -401,6 +362,15 @@ bool raster_row_major(uint64_t b_bytes) {
   if (e && e[0] == 'r') return true;
   if (e && e[0] == 'g') return false;
   return b_bytes <= kRowMajorMaxB;
+}
+
+// K-blocks of L2 prefetch the CTA-pair producer issues beyond its ring
+// (AKILI_PREFETCH in the environment; 0 turns it off).
+int prefetch_ahead() {
+  const char* e = std::getenv("AKILI_PREFETCH");
+  if (!e || !e[0]) return 8;
+  const int v = std::atoi(e);
+  return v < 0 ? 0 : (v > 64 ? 64 : v);
 }
 
 bool coop_enabled() {
@@ -481,29 +451,6 @@ int launch_gemm_pair(const DevInfo& di, const CUtensorMap& tmA, const CUtensorMa
     }
   }
   ea.row_sync = nullptr;
-  if (ea.sk_flags) {
-    const int kbs = (ea.K + kBK - 1) / kBK;
-    if (pairs_cap <= kSkMaxPairs && streamk_enabled() && streamk_wanted(tiles, kbs, pairs_cap)) {
-      // every pair takes an equal share of the (tile, K-block) units; the
-      // owners wait only for lower pairs, and the cooperative launch keeps
-      // the grid resident
-      if (cudaMemsetAsync(ea.sk_flags, 0, 2 * static_cast<size_t>(pairs_cap) * sizeof(unsigned int), st) !=
-          cudaSuccess) {
-        cudaGetLastError();
-        return AKILI_E_LAUNCH;
-      }
-      cfg.gridDim = dim3(2 * pairs_cap);
-      attr[1].id = cudaLaunchAttributeCooperative;
-      attr[1].val.cooperative = 1;
-      cfg.numAttrs = coop_enabled() ? 2 : 1;
-      if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) == cudaSuccess)
-        return launch_status();
-      cudaGetLastError();  // refused: whole tiles below
-      cfg.numAttrs = 1;
-      cfg.gridDim = dim3(2 * pairs);
-    }
-    ea.sk_flags = nullptr;
-  }
   if (cudaLaunchKernelEx(&cfg, kern, tmA, tmB0, tmB1, tmC, tmAlo, tmB0lo, tmB1lo, ea) != cudaSuccess) {
     cudaGetLastError();
     return AKILI_E_LAUNCH;
@@ -561,8 +508,7 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.ln_w = j.ln_w;
   ea.ln_b = j.ln_b;
   ea.eps = j.eps;
-  ea.sk_flags = jb.sk_flags;
-  ea.sk_part = jb.sk_part;
+  ea.prefetch_ahead = prefetch_ahead();
   ea.row_major = raster_row_major(K * N * 2 * (epi_dual(E) ? 2 : 1) * (kSplit ? 2 : 1)) ? 1 : 0;
 
   // the lo parts of the split mode: the same boxes over the lo copies

@@ -78,64 +78,11 @@ struct EpiArgs {
   const float* ln_w;  // LayerNorm gamma / beta and eps (row-fused kLnPre)
   const float* ln_b;
   float eps;
-  // Stream-K mode of the CTA-pair kernel (nullptr = one whole tile per work
-  // item): a ready flag per (pair, CTA), zeroed before the launch, and a
-  // 128 x 256 fp32 partial accumulator per (pair, CTA).
-  unsigned int* sk_flags;
-  float* sk_part;
   // CTA-pair tile order: 1 = row-block-major (every column tile of a row
   // block in turn; the B panels stay in L2 when B fits there), 0 = groups of
   // kGroupM row blocks walked row-block-fastest.
   int row_major;
-};
-
-// ---- stream-K work split of the CTA-pair kernel ----
-// The grid's npairs pairs share the num_tiles * num_kb (tile, K-block) units:
-// pair p takes the contiguous range [U p / P, U (p + 1) / P) and walks it from
-// its last unit down, one segment per tile it touches.  A tile's segment
-// holding its last K-block is its owner's: the owner adds the partial
-// accumulators of the lower pairs that hold the tile's earlier K-blocks and
-// runs the epilogue.  Every other partial segment is a contribution: its
-// accumulator goes to the pair's partial slot and the pair's flag is raised.
-// A pair contributes at most once, in its first segment, and an owner only
-// waits for lower pairs' first segments, so the waits never form a cycle.
-// Without stream-K each pair takes whole tiles pair, pair + npairs, ...
-constexpr int kSkFull = 0, kSkOwner = 1, kSkContrib = 2;
-constexpr int kSkPartFloats = kBM * 256;  // one CTA's partial: 128 rows x 256 TMEM columns
-
-struct PairWork {
-  long long U, u0, u;
-  int num_tiles, num_kb, npairs, next_tile;
-  bool sk;
-  __device__ PairWork(int tiles, int kbs, int pair, int pairs, bool stream_k)
-      : U(static_cast<long long>(tiles) * kbs), num_tiles(tiles), num_kb(kbs), npairs(pairs), next_tile(pair),
-        sk(stream_k) {
-    u0 = U * pair / pairs;
-    u = U * (pair + 1) / pairs;
-  }
-  // The pair whose range holds unit x.
-  __device__ int pair_of(long long x) const { return static_cast<int>(((x + 1) * npairs + U - 1) / U) - 1; }
-  __device__ bool next(int& tile, int& kb0, int& kb1, int& role, int& c_first) {
-    if (!sk) {
-      if (next_tile >= num_tiles) return false;
-      tile = next_tile;
-      next_tile += npairs;
-      kb0 = 0;
-      kb1 = num_kb;
-      role = kSkFull;
-      c_first = 0;
-      return true;
-    }
-    if (u <= u0) return false;
-    const long long t = (u - 1) / num_kb, lo = t * num_kb, s0 = u0 > lo ? u0 : lo;
-    tile = static_cast<int>(t);
-    kb0 = static_cast<int>(s0 - lo);
-    kb1 = static_cast<int>(u - lo);
-    role = kb1 == num_kb ? (kb0 == 0 ? kSkFull : kSkOwner) : kSkContrib;
-    c_first = role == kSkOwner ? pair_of(lo) : 0;
-    u = s0;
-    return true;
-  }
+  int prefetch_ahead;  // K-blocks the producer prefetches into L2 beyond its ring (0: none)
 };
 
 // Epilogues that normalise whole rows (longer than one tile).
@@ -182,22 +129,55 @@ struct RowState {
   float a, b, n;
 };
 
+// Epilogues that read the per-column vectors vec0 (bias, ba) / vec1 (bb).
+__host__ __device__ constexpr bool epi_vec0(Epi e) {
+  return e == Epi::kBiasRelu || e == Epi::kBiasMulLeaky || e == Epi::kRowSumBias || e == Epi::kLnPre ||
+         e == Epi::kLseClamp || e == Epi::kSiluMulBias;
+}
+__host__ __device__ constexpr bool epi_vec1(Epi e) { return e == Epi::kSiluMulBias; }
+
+// This lane's share of a per-column vector for up to four 32-column chunks of
+// a tile: lane l holds vec[n0 + (c_begin + i) * 32 + l] (0 past c_end, past N
+// or without a vector).  Loaded once per tile with one coalesced load per
+// chunk; the epilogue broadcasts column j of chunk i with a warp shuffle
+// (lane_pick + __shfl_sync) instead of 32 dependent scalar loads per chunk.
+struct LaneVec {
+  float v[4];
+};
+__device__ __forceinline__ LaneVec lane_vec(const float* vec, int n0, int c_begin, int c_end, int N) {
+  LaneVec r;
+  const int lane = static_cast<int>(threadIdx.x & 31);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int col = n0 + (c_begin + i) * 32 + lane;
+    r.v[i] = (vec != nullptr && c_begin + i < c_end && col < N) ? __ldg(vec + col) : 0.0f;
+  }
+  return r;
+}
+__device__ __forceinline__ float lane_pick(const LaneVec& lv, int i) {
+  return i == 0 ? lv.v[0] : (i == 1 ? lv.v[1] : (i == 2 ? lv.v[2] : lv.v[3]));
+}
+__device__ __forceinline__ float col_of(float lane_val, int j) { return __shfl_sync(0xffffffffu, lane_val, j); }
+
+// One 32-column chunk of the epilogue: b0 / b1 are this lane's values of
+// vec0 / vec1 for the chunk (lane_vec), column j is col_of(b0, j).
 template <Epi E, typename OutT>
 __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvalid, float (&v)[32],
-                                          const float (&u)[32], RowState& st) {
+                                          const float (&u)[32], RowState& st, float b0 = 0.0f, float b1 = 0.0f) {
+  (void)col0;
   if constexpr (E == Epi::kPlain) {
     (void)u;
   } else if constexpr (E == Epi::kBiasRelu) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+      const float b = col_of(b0, j);
       const float s = v[j] + b;
       v[j] = s > 0.0f ? s : 0.0f;
     }
   } else if constexpr (E == Epi::kBiasMulLeaky) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+      const float b = col_of(b0, j);
       const float val = (v[j] + b) * ea.s0;
       v[j] = val >= 0.0f ? val : val * ea.s1;
     }
@@ -209,7 +189,10 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
   } else if constexpr (E == Epi::kRowSumBias) {
     float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int j = 0; j < 32; ++j) s[j & 3] += (j < nvalid) ? (v[j] + __ldg(ea.vec0 + col0 + j)) : 0.0f;
+    for (int j = 0; j < 32; ++j) {
+      const float b = col_of(b0, j);
+      s[j & 3] += (j < nvalid) ? (v[j] + b) : 0.0f;
+    }
     st.a += sum4(s);
   } else if constexpr (E == Epi::kLnPre) {
     // y = acc + b, rounded to the stored precision; chunk mean/M2 merged into
@@ -217,7 +200,7 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
     float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float b = (j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+      const float b = col_of(b0, j);
       v[j] = round_out<OutT>(v[j] + b);
       sum[j & 3] += (j < nvalid) ? v[j] : 0.0f;
     }
@@ -249,7 +232,7 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
         y = round_out<OutT>(v[j] * ea.s0);
       } else {
         // kb2_matmul_scale_residadd_clamp adds a bias first (vec0); kbt has none
-        const float b = (ea.vec0 != nullptr && j < nvalid) ? __ldg(ea.vec0 + col0 + j) : 0.0f;
+        const float b = col_of(b0, j);
         const float scaled = (v[j] + b) * ea.s0;
         float t = scaled + scaled;
         if (t < ea.s1) t = ea.s1;
@@ -270,9 +253,8 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
   } else if constexpr (E == Epi::kSiluMulBias) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const bool ok = j < nvalid;
-      const float g = v[j] + (ok ? __ldg(ea.vec0 + col0 + j) : 0.0f);
-      const float uu = u[j] + (ok ? __ldg(ea.vec1 + col0 + j) : 0.0f);
+      const float g = v[j] + col_of(b0, j);
+      const float uu = u[j] + col_of(b1, j);
       v[j] = silu(g) * uu;
     }
   } else if constexpr (E == Epi::kSwiglu) {
@@ -314,44 +296,10 @@ __device__ __forceinline__ void stage_row(uint8_t* stage, int r, const float (&v
 // buffers) for TMA stores issued by `issuer`, or reduced to the row's
 // statistics, which are returned.  `bar_id` is the named barrier of these
 // 128 threads.
-// Stream-K owners pass the partial accumulators of their tile's `nskp`
-// contributors (`skp`: the first one's slot for this CTA, later ones
-// 2 * kSkPartFloats apart); they are added to each 64-column TMEM load.
-__device__ __forceinline__ void sk_add_partials(const float* skp, int nskp, int col, int r, float (&v)[64]) {
-  for (int ci = 0; ci < nskp; ++ci) {
-    const float4* p = reinterpret_cast<const float4*>(skp + static_cast<size_t>(ci) * 2 * kSkPartFloats);
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const float4 f = __ldcg(p + (col / 4 + q) * kBM + r);
-      v[4 * q] += f.x;
-      v[4 * q + 1] += f.y;
-      v[4 * q + 2] += f.z;
-      v[4 * q + 3] += f.w;
-    }
-  }
-}
-
-// A stream-K contribution: this thread's row of TMEM columns [col0, col0 +
-// 128) into the partial slot `dst`, in the layout sk_add_partials reads
-// (4-column groups, row-minor, so a warp's 16-byte stores are contiguous).
-__device__ __forceinline__ void sk_write_partial(uint32_t tbase, int col0, int r, float* dst) {
-  float v[64];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int col = col0 + 64 * h;
-    tmem_ld64(tbase + col, v);
-    float4* p = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int q = 0; q < 16; ++q)
-      __stcg(p + (col / 4 + q) * kBM + r, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
-  }
-}
-
 template <Epi E, typename OutT>
 __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUtensorMap* tmC, uint32_t tbase, int n0,
                                                   int mrow0, int r, int c_begin, int c_end, uint8_t* staging,
-                                                  uint32_t bar_id, bool issuer, int& chunk_ctr,
-                                                  const float* skp = nullptr, int nskp = 0) {
+                                                  uint32_t bar_id, bool issuer, int& chunk_ctr) {
   constexpr bool kDual = epi_dual(E);
   constexpr bool kStore = epi_stores(E);
   constexpr int kStats = epi_stats(E);
@@ -362,16 +310,14 @@ __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUten
   st.n = 0.0f;
   float v2[64];
   float u2[kDual ? 64 : 1];
+  const LaneVec lv0 = lane_vec(epi_vec0(E) ? ea.vec0 : nullptr, n0, c_begin, c_end, ea.N);
+  const LaneVec lv1 = lane_vec(epi_vec1(E) ? ea.vec1 : nullptr, n0, c_begin, c_end, ea.N);
   for (int c = c_begin; c < c_end; ++c) {
     const bool odd = ((c - c_begin) & 1) != 0;
     // TMEM is read 64 columns at a time: one load + wait per chunk pair.
     if (!odd) {
       tmem_ld64(tbase + c * 32, v2);
       if constexpr (kDual) tmem_ld64(tbase + 128 + c * 32, reinterpret_cast<float(&)[64]>(u2));
-      if (nskp) {
-        sk_add_partials(skp, nskp, c * 32, r, v2);
-        if constexpr (kDual) sk_add_partials(skp, nskp, 128 + c * 32, r, reinterpret_cast<float(&)[64]>(u2));
-      }
     }
     float v[32];
     float u[32];
@@ -382,7 +328,7 @@ __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUten
     }
     const int col0 = n0 + c * 32;
     const int nvalid = min(32, ea.N - col0);
-    epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st);
+    epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st, lane_pick(lv0, c - c_begin), lane_pick(lv1, c - c_begin));
     if constexpr (kStore) {
       uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
       if (issuer) bulk_wait_read<1>();
@@ -414,6 +360,7 @@ __device__ __forceinline__ RowState rowstats_half(const EpiArgs& ea, uint32_t tb
   st.n = 0.0f;
   float v2[64];
   float u[32];
+  const LaneVec lv0 = lane_vec(epi_vec0(E) ? ea.vec0 : nullptr, n0, c_begin, c_end, ea.N);
   for (int c = c_begin; c < c_end; ++c) {
     const bool odd = ((c - c_begin) & 1) != 0;
     if (!odd) tmem_ld64(tbase + c * 32, v2);
@@ -421,7 +368,7 @@ __device__ __forceinline__ RowState rowstats_half(const EpiArgs& ea, uint32_t tb
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = odd ? v2[32 + i] : v2[i];
     const int col0 = n0 + c * 32;
-    epi_chunk<E, float>(ea, col0, min(32, ea.N - col0), v, u, st);
+    epi_chunk<E, float>(ea, col0, min(32, ea.N - col0), v, u, st, lane_pick(lv0, c - c_begin));
   }
   return st;
 }
@@ -497,21 +444,22 @@ __device__ __forceinline__ void rownorm_half(const EpiArgs& ea, const CUtensorMa
   constexpr int kStageOut = kBM * 32 * sizeof(OutT);
   constexpr float kLog2e = 1.4426950408889634f;
   float v2[64];
+  const bool ln = E == Epi::kLnPre;
+  const LaneVec lb = lane_vec(ln ? ea.vec0 : nullptr, n0, c_begin, c_end, ea.N);
+  const LaneVec lg = lane_vec(ln ? ea.ln_w : nullptr, n0, c_begin, c_end, ea.N);
+  const LaneVec lbeta = lane_vec(ln ? ea.ln_b : nullptr, n0, c_begin, c_end, ea.N);
   for (int c = c_begin; c < c_end; ++c) {
     const bool odd = ((c - c_begin) & 1) != 0;
     if (!odd) tmem_ld64(tbase + c * 32, v2);
     const int col0 = n0 + c * 32;
-    const int nvalid = min(32, ea.N - col0);
+    const float pb = lane_pick(lb, c - c_begin), pg = lane_pick(lg, c - c_begin), pbeta = lane_pick(lbeta, c - c_begin);
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float acc = odd ? v2[32 + j] : v2[j];
-      const bool ok = j < nvalid;
       if constexpr (E == Epi::kLnPre) {
-        const float y = acc + (ok ? __ldg(ea.vec0 + col0 + j) : 0.0f);
-        const float g = ok ? __ldg(ea.ln_w + col0 + j) : 0.0f;
-        const float bb = ok ? __ldg(ea.ln_b + col0 + j) : 0.0f;
-        v[j] = ((y - s0) * s1) * g + bb;
+        const float y = acc + col_of(pb, j);
+        v[j] = ((y - s0) * s1) * col_of(pg, j) + col_of(pbeta, j);
       } else {
         v[j] = exp2f(fmaf(acc * ea.s0, kLog2e, -s0)) * s1;
       }
@@ -853,7 +801,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   // Row-fused LayerNorm / softmax: tiles in row-block-major order, so the
   // tiles of one row block run in the same wave (see the epilogue).
   const bool rowfused = epi_rownorm(E) && ea.row_sync != nullptr;
-  const bool stream_k = !rowfused && ea.sk_flags != nullptr;
   const bool row_major = rowfused || ea.row_major != 0;
 
   if (threadIdx.x == 0) {
@@ -892,20 +839,38 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      PairWork work(num_tiles, num_kb, pair, npairs, stream_k);
-      int tile, kb0, kb1, role, c_first;
-      while (ok && work.next(tile, kb0, kb1, role, c_first)) {
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         int m_blk, n_blk;
         pair_tile_coords(tile, num_m, num_n, row_major, m_blk, n_blk);
         const int row0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
         const int col0 = n_blk * BN + static_cast<int>(rank) * BNH;
-        for (int kb = kb0; kb < kb1 && ok; ++kb) {
+        for (int kb = 0; kb < num_kb && ok; ++kb) {
           ok = mbar_wait_cluster(&empty[stage], phase ^ 1, kSiteProducerEmpty);
           if (!ok) break;
           uint8_t* sa = ring + stage * kSB;
           uint8_t* sb = sa + kATileBytes;
           const uint32_t fb = full_c + stage * 8;
           if (leader) mbar_expect_tx(&full[stage], 2 * kSB);
+          // L2 prefetch ea.prefetch_ahead K-blocks beyond the ring's reach
+          // (the tile's first K-block covers the blocks in between), so a
+          // cold panel's DRAM latency is not left to the ring's depth.
+          if (!kSplit && ea.prefetch_ahead > 0) {
+            const int p0 = kb == 0 ? kPairStages : kb + kPairStages + ea.prefetch_ahead - 1;
+            const int p1 = min(num_kb, kb + kPairStages + ea.prefetch_ahead);
+            for (int pk = p0; pk < p1; ++pk) {
+              tma_prefetch_l2_2d(&tmA, pk * kBK, row0);
+              if constexpr (kBKMajor) {
+                tma_prefetch_l2_2d(&tmB0, pk * kBK, col0);
+              } else if constexpr (kDual) {
+                const CUtensorMap* tb = leader ? &tmB0 : &tmB1;
+                tma_prefetch_l2_2d(tb, n_blk * BN, pk * kBK);
+                tma_prefetch_l2_2d(tb, n_blk * BN + 64, pk * kBK);
+              } else {
+                tma_prefetch_l2_2d(&tmB0, col0, pk * kBK);
+                tma_prefetch_l2_2d(&tmB0, col0 + 64, pk * kBK);
+              }
+            }
+          }
           tma_load_2d_pair(sa, &tmA, fb, kb * kBK, row0);
           if constexpr (kBKMajor) {
             tma_load_2d_pair(sb, &tmB0, fb, kb * kBK, col0);
@@ -954,16 +919,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      PairWork work(num_tiles, num_kb, pair, npairs, stream_k);
-      int tile, kb0, kb1, role, c_first;
-      for (; ok && work.next(tile, kb0, kb1, role, c_first); ++it) {
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         ok = mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
         if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccCols;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb) {
           ok = mbar_wait_cluster(&full[stage], phase, kSiteMmaFull);
           if (!ok) break;
           tc_fence_after();
@@ -972,7 +935,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
-            const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
+            const uint32_t accum = (kb | k) != 0;
             const uint64_t bd = kBKMajor ? make_sdesc(sb + k * 32, 16, 1024, kSw128)
                                          : make_sdesc(sb + k * 2048, 8192, 1024, kSw128);
             umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
@@ -1061,57 +1024,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if (leader) mbar_arrive(&acc_empty[acc]);
           else mbar_arrive_cluster(acc_empty_c + acc * 8);
         }
-      }
-    } else if (stream_k) {
-      // Stream-K: as below, per segment of PairWork.  A contribution writes
-      // the CTA's accumulator to this pair's partial slot and raises the
-      // pair's flag; an owner first waits for the flags of the lower pairs
-      // that contributed to its tile (bounded), then adds their partials in
-      // the epilogue.  Both groups share barrier 3 and abort_flag[0].
-      PairWork work(num_tiles, num_kb, pair, npairs, true);
-      int tile, kb0, kb1, role, c_first;
-      for (; work.next(tile, kb0, kb1, role, c_first); ++it) {
-        int m_blk, n_blk;
-        pair_tile_coords(tile, num_m, num_n, row_major, m_blk, n_blk);
-        const int acc = it & 1;
-        const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, kSiteEpiAccFull)) abort_flag[0] = 1;
-        if (role == kSkOwner && threadIdx.x == 64) {
-          for (int c = c_first; c < pair; ++c)
-            if (!counter_wait_geq(ea.sk_flags + 2 * c + rank, 1u, kSiteStreamK)) abort_flag[0] = 1;
-        }
-        named_bar_sync(3, 256);
-        if (abort_flag[0]) break;
-        if (role == kSkOwner) __threadfence();
-        tc_fence_after();
-        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(wq * 32) << 16) + acc * kAccCols;
-        if (role == kSkContrib) {
-          sk_write_partial(tbase, grp * 128, r, ea.sk_part + static_cast<size_t>(2 * pair + rank) * kSkPartFloats);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (leader) mbar_arrive(&acc_empty[acc]);
-            else mbar_arrive_cluster(acc_empty_c + acc * 8);
-          }
-          __threadfence();
-          named_bar_sync(3, 256);
-          if (threadIdx.x == 64) atomicExch(ea.sk_flags + 2 * pair + rank, 1u);
-          continue;
-        }
-        const int n0 = n_blk * BN;
-        const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-        const float* skp = ea.sk_part + static_cast<size_t>(2 * c_first + rank) * kSkPartFloats;
-        const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
-                                                   min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
-                                                   chunk_ctr, skp, role == kSkOwner ? pair - c_first : 0);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) mbar_arrive(&acc_empty[acc]);
-          else mbar_arrive_cluster(acc_empty_c + acc * 8);
-        }
-        write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
       }
     } else {
       for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {

@@ -21,8 +21,9 @@ seeded synthetic data with the configured shapes and distributions.
              host threads as "all_cores".
 * --impl reference  times that reference CPU path alone (all host threads).
 * clocks     sm_mhz of the timed steps measured on the device (SM cycles
-             over globaltimer nanoseconds in a short spin after each step);
-             throttle reasons from nvidia-smi sampled over the soak around them.
+             over globaltimer nanoseconds of a one-thread spin running beside
+             each step); throttle reasons from nvidia-smi sampled over the soak
+             around them.
 
 Multi-GPU (torchrun, one rank per GPU): by default (--scaling strong) the
 configured global problem is split across the ranks -- GEMM rows in
@@ -593,18 +594,24 @@ def cpu_leg(d, threads: int, rows_per_thread: int) -> dict:
 
 
 class ClockProbe:
-    """SM clock of the timed steps, measured on the device: after each timed
-    step (outside its events) one thread spins for `spin_ns` and counts SM
-    cycles (akili_sm_clock_probe); cycles / ns over all steps is the clock."""
+    """SM clock of the timed steps, measured on the device while they run:
+    with each timed step, a one-thread kernel (akili_sm_clock_probe) on a side
+    stream starts at the step's start event and spins for `spin_ns`, about
+    half the step, counting SM cycles (clock64) against globaltimer
+    nanoseconds.  It fits beside the step's CTAs on an SM (one thread, no
+    shared memory), so it samples the clock the step's kernels run at.
+    cycles / ns over all steps is the clock."""
 
     def __init__(self, torch, spin_ns: int = 40000):
-        self.torch, self.spin = torch, spin_ns
+        self.torch, self.spin = torch, int(min(10_000_000, max(2000, spin_ns)))
         self.acc = torch.zeros(2, dtype=torch.int64, device="cuda")
+        self.side = torch.cuda.Stream()
         self.n = 0
 
-    def sample(self, stream):
+    def sample(self, start_event):
         from akili_bench_b200 import abi
-        rc = abi.load().akili_sm_clock_probe(self.acc.data_ptr(), self.spin, int(stream.cuda_stream))
+        self.side.wait_event(start_event)
+        rc = abi.load().akili_sm_clock_probe(self.acc.data_ptr(), self.spin, int(self.side.cuda_stream))
         if rc != abi.OK:
             raise abi.AkiliError("sm_clock_probe", rc)
         self.n += 1
@@ -626,16 +633,23 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
     stream = torch.cuda.current_stream()
     flush = torch.empty(2 * L2_BYTES // 4, device="cuda", dtype=torch.float32)
     graph = None
-    if wl.graph:
-        # A launch-bound step (many short kernels) is timed as replays of
-        # its launches captured once in a CUDA graph.
+    if wl.graph or args.graph:
+        # The timed steps replay the step's launches, captured once in a CUDA
+        # graph: a C-ABI call spends tens of microseconds on the host (argument
+        # checks, tensor maps, launch), longer than the L2 flush before it, and
+        # eager launches would let that host time show up as device idle time
+        # inside the events.  The capture stream runs one call first, so any
+        # scratch the library keeps per stream exists before the capture.
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
         l0 = ops.launch_count()
-        wl.call(d, out, stream)
+        with torch.cuda.stream(cap):
+            wl.call(d, out, cap)
         torch.cuda.synchronize()
         launches_per_step = ops.launch_count() - l0
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            wl.call(d, out, torch.cuda.current_stream())
+        with torch.cuda.graph(graph, stream=cap):
+            wl.call(d, out, cap)
         torch.cuda.synchronize()
 
     def step():
@@ -651,7 +665,14 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    probe = ClockProbe(torch)
+    # one untimed step to size the clock probe's spin to half a step
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    flush.zero_()
+    e0.record(stream)
+    step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    probe = ClockProbe(torch, int(e0.elapsed_time(e1) * 1e6 * 0.5))
 
     def soak(seconds):
         # untimed repetitions so the clock sampler sees the GPU under this load
@@ -673,14 +694,15 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
+            probe.sample(starts[i])
             step()
             ends[i].record(stream)
-            probe.sample(stream)
         torch.cuda.synchronize()
         launches = ops.launch_count() - l0 if graph is None else launches_per_step * args.steps
         barrier()
         soak(args.soak / 2)
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    graph_used = graph is not None
     dev_ms = float(sum(per_step))
     t = torch.tensor([dev_ms], device="cuda", dtype=torch.float64)
     if world > 1:
@@ -808,8 +830,9 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
     cl["sm_mhz_smi"] = cl["sm_mhz"]
     if mhz:
         cl["sm_mhz"] = round(mhz, 1)
-        cl["sm_mhz_source"] = ("device: SM cycles / globaltimer ns over a 40 us spin after each timed step "
-                               "(outside its events); sm_mhz_smi = nvidia-smi median over the soak around them")
+        cl["sm_mhz_source"] = ("device: SM cycles / globaltimer ns of a one-thread spin beside each timed step, "
+                               f"{probe.spin / 1e3:.0f} us from its start; sm_mhz_smi = nvidia-smi median over the "
+                               "soak around the steps")
         roof["achieved_per_mhz"] = ach / mhz
     e2e = {"value": e2e_value, "unit": wl.unit, "path": e2e_path, "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h)}
@@ -828,7 +851,9 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
                        "parallelism": (f"{world} independent replica(s)" if wl.split == "replicas" else
                                        f"{wl.split} split over {world} GPU(s) ({mode} scaling), "
                                        "no collective in the timed loop"),
-                       "l2": "flushed (512 MB write) before every timed step, outside the events",
+                       "l2": "flushed (a 252 MiB write, twice L2) before every timed step, outside the events",
+                       "launch": ("each timed step replays the step's launches from a CUDA graph" if graph_used
+                                  else "eager launches"),
                        "inputs": "seeded synthetic, distributions of the configured workload"},
             "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "device_status": status, "clocks": cl}
     if check is not None:
@@ -920,6 +945,8 @@ def main():
     ap.add_argument("--shard-of", type=int, default=1, metavar="G",
                     help="measure rank 0's share of a G-way strong split on this GPU alone (profiling the small "
                          "per-GPU problems of the multi-GPU split); value is then this GPU's work")
+    ap.add_argument("--eager", dest="graph", action="store_false",
+                    help="launch the timed steps eagerly instead of replaying a captured CUDA graph")
     ap.add_argument("--no-link-probe", dest="link_probe", action="store_false",
                     help="skip the host-link copy probe that states e2e against the link's ceiling")
     ap.add_argument("--soak", type=float, default=1.0,
