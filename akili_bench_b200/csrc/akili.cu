@@ -364,15 +364,6 @@ bool raster_row_major(uint64_t b_bytes) {
   return b_bytes <= kRowMajorMaxB;
 }
 
-// K-blocks of L2 prefetch the CTA-pair producer issues beyond its ring
-// (AKILI_PREFETCH in the environment; 0 turns it off).
-int prefetch_ahead() {
-  const char* e = std::getenv("AKILI_PREFETCH");
-  if (!e || !e[0]) return 8;
-  const int v = std::atoi(e);
-  return v < 0 ? 0 : (v > 64 ? 64 : v);
-}
-
 bool coop_enabled() {
   const char* e = std::getenv("AKILI_COOP");
   return !(e && e[0] == '0');
@@ -508,7 +499,6 @@ int launch_gemm(const DevInfo& di, const GemmJob& j, const JobBuffers& jb, cudaS
   ea.ln_w = j.ln_w;
   ea.ln_b = j.ln_b;
   ea.eps = j.eps;
-  ea.prefetch_ahead = prefetch_ahead();
   ea.row_major = raster_row_major(K * N * 2 * (epi_dual(E) ? 2 : 1) * (kSplit ? 2 : 1)) ? 1 : 0;
 
   // the lo parts of the split mode: the same boxes over the lo copies

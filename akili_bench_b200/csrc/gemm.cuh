@@ -82,7 +82,6 @@ struct EpiArgs {
   // block in turn; the B panels stay in L2 when B fits there), 0 = groups of
   // kGroupM row blocks walked row-block-fastest.
   int row_major;
-  int prefetch_ahead;  // K-blocks the producer prefetches into L2 beyond its ring (0: none)
 };
 
 // Epilogues that normalise whole rows (longer than one tile).
@@ -851,26 +850,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           uint8_t* sb = sa + kATileBytes;
           const uint32_t fb = full_c + stage * 8;
           if (leader) mbar_expect_tx(&full[stage], 2 * kSB);
-          // L2 prefetch ea.prefetch_ahead K-blocks beyond the ring's reach
-          // (the tile's first K-block covers the blocks in between), so a
-          // cold panel's DRAM latency is not left to the ring's depth.
-          if (!kSplit && ea.prefetch_ahead > 0) {
-            const int p0 = kb == 0 ? kPairStages : kb + kPairStages + ea.prefetch_ahead - 1;
-            const int p1 = min(num_kb, kb + kPairStages + ea.prefetch_ahead);
-            for (int pk = p0; pk < p1; ++pk) {
-              tma_prefetch_l2_2d(&tmA, pk * kBK, row0);
-              if constexpr (kBKMajor) {
-                tma_prefetch_l2_2d(&tmB0, pk * kBK, col0);
-              } else if constexpr (kDual) {
-                const CUtensorMap* tb = leader ? &tmB0 : &tmB1;
-                tma_prefetch_l2_2d(tb, n_blk * BN, pk * kBK);
-                tma_prefetch_l2_2d(tb, n_blk * BN + 64, pk * kBK);
-              } else {
-                tma_prefetch_l2_2d(&tmB0, col0, pk * kBK);
-                tma_prefetch_l2_2d(&tmB0, col0 + 64, pk * kBK);
-              }
-            }
-          }
           tma_load_2d_pair(sa, &tmA, fb, kb * kBK, row0);
           if constexpr (kBKMajor) {
             tma_load_2d_pair(sb, &tmB0, fb, kb * kBK, col0);
