@@ -232,8 +232,8 @@ def load(path: str = LIB_PATH) -> C.CDLL:
     L.akili_selftest_wait_timeout.restype = C.c_int
     L.akili_launch_count.argtypes = []
     L.akili_launch_count.restype = C.c_uint64
-    L.akili_sm_clock_probe.argtypes = [C.c_uint64, C.c_uint32, C.c_void_p]
-    L.akili_sm_clock_probe.restype = C.c_int
+    L.akili_sm_clock_read.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.c_int]
+    L.akili_sm_clock_read.restype = C.c_int
     L.akili_abi_version.argtypes = []
     L.akili_abi_version.restype = C.c_uint32
     _LIB = L

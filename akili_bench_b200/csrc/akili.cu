@@ -1164,18 +1164,6 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
   __syncthreads();
 }
 
-// One thread spins for spin_ns of %globaltimer and adds the SM cycles and
-// nanoseconds it saw to acc[0] / acc[1].
-__global__ void sm_clock_probe_kernel(unsigned long long* acc, uint64_t spin_ns) {
-  const uint64_t t0 = globaltimer();
-  const long long c0 = clock64();
-  uint64_t t1 = t0;
-  while (t1 - t0 < spin_ns) t1 = globaltimer();
-  const long long c1 = clock64();
-  acc[0] += static_cast<unsigned long long>(c1 - c0);
-  acc[1] += t1 - t0;
-}
-
 // kb2_* entries: fp32 in, fp32 out; an akili_ex_t may only add a workspace.
 template <class Arg, int (*Build)(const Arg*, GemmJob&, bool)>
 int entry_kb2(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
@@ -1900,16 +1888,26 @@ int akili_selftest_wait_timeout(uint32_t limit_us, akili_stream_t s) {
 
 uint64_t akili_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-int akili_sm_clock_probe(uint64_t acc_addr, uint32_t spin_ns, akili_stream_t s) {
-  if (acc_addr == 0) return AKILI_E_NULL_ARG;
-  if (acc_addr % 8) return AKILI_E_ALIGN;
-  if (spin_ns < 1000u || spin_ns > 10000000u) return AKILI_E_SHAPE;
+int akili_sm_clock_read(uint64_t* cycles, uint64_t* ns, int clear) {
+  if (!cycles || !ns) return AKILI_E_NULL_ARG;
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  sm_clock_probe_kernel<<<1, 1, 0, S(s)>>>(reinterpret_cast<unsigned long long*>(acc_addr), spin_ns);
-  return cudaGetLastError() == cudaSuccess ? AKILI_OK : AKILI_E_LAUNCH;
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
+  unsigned long long v[2] = {0, 0};
+  if (cudaMemcpyFromSymbol(v, g_clock_acc, sizeof(v)) != cudaSuccess) return AKILI_E_LAUNCH;
+  *cycles = v[0];
+  *ns = v[1];
+  if (clear) {
+    const unsigned long long z[2] = {0, 0};
+    if (cudaMemcpyToSymbol(g_clock_acc, z, sizeof(z)) != cudaSuccess) return AKILI_E_LAUNCH;
+  }
+  return AKILI_OK;
 }
+
 uint32_t akili_abi_version(void) { return AKILI_ABI_VERSION; }
 
 }  // extern "C"

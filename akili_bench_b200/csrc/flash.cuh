@@ -95,6 +95,7 @@ __global__ void __maxnreg__(96)
   constexpr int kStageOut = kFlashBM * 32 * sizeof(OutT);
   constexpr uint32_t kColO = 256;   // O_t at 256 + 128 t; S_t / P_t at 128 t
 
+  const KClock kclk = kclock_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::kQOff;
@@ -428,6 +429,7 @@ __global__ void __maxnreg__(96)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  kclock_end(kclk);
 }
 
 template <int DP, bool kSplit>

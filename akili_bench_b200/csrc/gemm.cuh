@@ -509,6 +509,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int kOutBytes = sizeof(OutT);
   constexpr int kStageOut = kBM * 32 * kOutBytes;
 
+  const KClock kclk = kclock_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
@@ -709,6 +710,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  kclock_end(kclk);
 }
 
 }  // namespace akili
@@ -773,6 +775,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   constexpr int kPairStages = pair_stages(kStore, kOutBytes, kSplit);
   constexpr int kSB = pair_stage_bytes(kSplit);
 
+  const KClock kclk = kclock_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
@@ -1044,6 +1047,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+  kclock_end(kclk);
 }
 
 }  // namespace akili

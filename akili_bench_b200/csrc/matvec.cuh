@@ -19,6 +19,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include "sm100.cuh"
+
 namespace akili {
 
 constexpr int kMatvecMaxSegs = 4;
@@ -43,6 +45,7 @@ struct MatvecArgs {
 // kSmemX: x fits in shared memory (else it is read through L1).
 template <bool kVec, bool kSmemX>
 __global__ void __launch_bounds__(kMatvecThreads) matvec_kernel(const __grid_constant__ MatvecArgs a) {
+  const KClock kclk = kclock_begin();
   extern __shared__ float4 xs4[];
   float* xs = reinterpret_cast<float*>(xs4);
   const int K = a.K;
@@ -89,6 +92,7 @@ __global__ void __launch_bounds__(kMatvecThreads) matvec_kernel(const __grid_con
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) a.seg[s].C[r] = acc;
   }
+  kclock_end(kclk);
 }
 
 }  // namespace akili

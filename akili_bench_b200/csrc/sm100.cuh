@@ -46,8 +46,38 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// SM clock of the library's main kernels, for benchmarks: CTA 0's thread 0
+// of each gemm / flash / softmax-rows / matrix-vector launch adds the SM
+// cycles (clock64) and the globaltimer nanoseconds from its entry to its exit.
+// cycles / ns * 1000 is the SM clock in MHz those launches ran at
+// (akili_sm_clock_read).  The cost is four register reads and two atomics a launch.
+__device__ unsigned long long g_clock_acc[2];
+struct KClock {
+  long long c;
+  unsigned long long t;
+};
+__device__ __forceinline__ bool kclock_thread() {
+  return blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0;
+}
 __device__ __forceinline__ void record_timeout(uint32_t site) {
   atomicCAS(&g_status, 0u, 0x1000u | site);
+}
+
+__device__ __forceinline__ KClock kclock_begin() {
+  KClock k{0, 0};
+  if (kclock_thread()) {
+    k.t = globaltimer();
+    k.c = clock64();
+  }
+  return k;
+}
+__device__ __forceinline__ void kclock_end(const KClock& k) {
+  if (kclock_thread()) {
+    const long long c = clock64();
+    const unsigned long long t = globaltimer();
+    atomicAdd(&g_clock_acc[0], static_cast<unsigned long long>(c - k.c));
+    atomicAdd(&g_clock_acc[1], t - k.t);
+  }
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

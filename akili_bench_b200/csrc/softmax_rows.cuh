@@ -194,6 +194,7 @@ template <typename OutT, bool kBKMajor>
 __global__ void __launch_bounds__(kSmThreads, 1)
     softmax_rows_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const SoftmaxRowsArgs p) {
+  const KClock kclk = kclock_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_smem = smem + p.L.a_off;
@@ -415,6 +416,7 @@ __global__ void __launch_bounds__(kSmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  kclock_end(kclk);
 }
 
 }  // namespace akili

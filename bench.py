@@ -20,10 +20,10 @@ seeded synthetic data with the configured shapes and distributions.
              (the reference's serial loop), plus a row-parallel run on all
              host threads as "all_cores".
 * --impl reference  times that reference CPU path alone (all host threads).
-* clocks     sm_mhz of the timed steps measured on the device (SM cycles
-             over globaltimer nanoseconds of a one-thread spin running beside
-             each step); throttle reasons from nvidia-smi sampled over the soak
-             around them.
+* clocks     sm_mhz of the timed steps measured on the device: the SM
+             cycles over the globaltimer nanoseconds of the steps' own kernels
+             (their CTA 0 counts both); throttle reasons from nvidia-smi
+             sampled over the soak around them.
 
 Multi-GPU (torchrun, one rank per GPU): by default (--scaling strong) the
 configured global problem is split across the ranks -- GEMM rows in
@@ -593,31 +593,28 @@ def cpu_leg(d, threads: int, rows_per_thread: int) -> dict:
                                     "(a labelled row-parallel run; the reference's loop is serial)"}}
 
 
-class ClockProbe:
-    """SM clock of the timed steps, measured on the device while they run:
-    with each timed step, a one-thread kernel (akili_sm_clock_probe) on a side
-    stream starts at the step's start event and spins for `spin_ns`, about
-    half the step, counting SM cycles (clock64) against globaltimer
-    nanoseconds.  It fits beside the step's CTAs on an SM (one thread, no
-    shared memory), so it samples the clock the step's kernels run at.
-    cycles / ns over all steps is the clock."""
+class KernelClock:
+    """SM clock the timed steps' own kernels ran at: the library's GEMM,
+    flash, fused-softmax and matrix-vector kernels each add, from CTA 0, the
+    SM cycles (clock64) and globaltimer nanoseconds of their run to two device
+    counters (akili_sm_clock_read); read over the timed steps alone, cycles /
+    ns is the clock under that load, with nothing running beside them."""
 
-    def __init__(self, torch, spin_ns: int = 40000):
-        self.torch, self.spin = torch, int(min(10_000_000, max(2000, spin_ns)))
-        self.acc = torch.zeros(2, dtype=torch.int64, device="cuda")
-        self.side = torch.cuda.Stream()
-        self.n = 0
-
-    def sample(self, start_event):
+    def __init__(self):
         from akili_bench_b200 import abi
-        self.side.wait_event(start_event)
-        rc = abi.load().akili_sm_clock_probe(self.acc.data_ptr(), self.spin, int(self.side.cuda_stream))
-        if rc != abi.OK:
-            raise abi.AkiliError("sm_clock_probe", rc)
-        self.n += 1
+        self.L = abi.load()
+
+    def _read(self, clear):
+        import ctypes as C
+        cyc, ns = C.c_uint64(0), C.c_uint64(0)
+        rc = self.L.akili_sm_clock_read(C.byref(cyc), C.byref(ns), 1 if clear else 0)
+        return (int(cyc.value), int(ns.value)) if rc == 0 else (0, 0)
+
+    def reset(self):
+        self._read(True)
 
     def mhz(self):
-        cyc, ns = (int(v) for v in self.acc.cpu())
+        cyc, ns = self._read(False)
         return 1e3 * cyc / ns if ns else None
 
 
@@ -665,14 +662,7 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    # one untimed step to size the clock probe's spin to half a step
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    flush.zero_()
-    e0.record(stream)
-    step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    probe = ClockProbe(torch, int(e0.elapsed_time(e1) * 1e6 * 0.5))
+    kclock = KernelClock()
 
     def soak(seconds):
         # untimed repetitions so the clock sampler sees the GPU under this load
@@ -690,14 +680,15 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
         soak(args.soak)
         torch.cuda.synchronize()
         barrier()
+        kclock.reset()
         l0 = ops.launch_count()
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            probe.sample(starts[i])
             step()
             ends[i].record(stream)
         torch.cuda.synchronize()
+        mhz = kclock.mhz()
         launches = ops.launch_count() - l0 if graph is None else launches_per_step * args.steps
         barrier()
         soak(args.soak / 2)
@@ -826,13 +817,12 @@ def measure(torch, dist, ops, W, name, args, rank, world, local, pk, pk_kind, ba
     roof["kernel"] = wl.kernel if wl.kernel != "gemm_kernel" or wl.desc.get("M", 0) <= 128 else "gemm_pair_kernel"
 
     cl = clk.summary()
-    mhz = probe.mhz()
     cl["sm_mhz_smi"] = cl["sm_mhz"]
     if mhz:
         cl["sm_mhz"] = round(mhz, 1)
-        cl["sm_mhz_source"] = ("device: SM cycles / globaltimer ns of a one-thread spin beside each timed step, "
-                               f"{probe.spin / 1e3:.0f} us from its start; sm_mhz_smi = nvidia-smi median over the "
-                               "soak around the steps")
+        cl["sm_mhz_source"] = ("device: SM cycles / globaltimer ns of the timed steps' own kernels (CTA 0 of each "
+                               "launch, akili_sm_clock_read); sm_mhz_smi = nvidia-smi median over the soak around "
+                               "the steps")
         roof["achieved_per_mhz"] = ach / mhz
     e2e = {"value": e2e_value, "unit": wl.unit, "path": e2e_path, "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h)}

@@ -479,14 +479,14 @@ int akili_selftest_wait_timeout(uint32_t limit_us, akili_stream_t stream);
  * (all devices).  For launch accounting in benchmarks. */
 uint64_t akili_launch_count(void);
 
-/* SM clock probe for benchmarks (no counterpart in the reference): launches
- * one thread that spins for `spin_ns` nanoseconds of %globaltimer (1000 ..
- * 10000000) and adds the SM cycles (clock64) and the nanoseconds it saw to
- * the two uint64 counters at device address `acc_addr`.  cycles / ns * 1000
- * is the SM clock in MHz over the spins; enqueued between timed launches it
- * samples the clock of the load around them.  Not counted by
- * akili_launch_count. */
-int akili_sm_clock_probe(uint64_t acc_addr, uint32_t spin_ns, akili_stream_t stream);
+/* SM clock of the library's own kernels, for benchmarks (no counterpart in
+ * the reference).  CTA 0 of every GEMM, flash, fused-softmax and
+ * matrix-vector launch adds the SM cycles and globaltimer nanoseconds from
+ * its entry to its exit to two device counters of the current device.
+ * Returns them in *cycles / *ns; cycles / ns * 1000 is the SM clock in MHz
+ * those launches ran at.  Synchronises the device; `clear` != 0 resets the
+ * counters. */
+int akili_sm_clock_read(uint64_t* cycles, uint64_t* ns, int clear);
 
 /* ABI version compiled into the library. */
 uint32_t akili_abi_version(void);

@@ -27,7 +27,7 @@ def exported(lib: str) -> set[str]:
 def test_libakili_exports_every_declared_entry():
     names = declared("akili.h", "akili_")
     # kbt+flash, kb2, attention (+ex), flash statistics, no-alloc LN, llama2 matmul + batch, helpers
-    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 8  # helpers: + akili_host_call, akili_sm_clock_probe
+    assert len(names) == 24 + 20 + 2 + 1 + 1 + 2 + 8  # helpers: + akili_host_call, akili_sm_clock_read
     missing = names - exported(abi.LIB_PATH)
     assert not missing, missing
     L = abi.load()
@@ -159,9 +159,8 @@ def test_host_call_validates_before_cuda():
         abi.E_UNSUPPORTED
 
 
-def test_sm_clock_probe_validates_before_any_cuda_call():
+def test_sm_clock_read_validates_before_any_cuda_call():
     L = abi.load()
-    assert L.akili_sm_clock_probe(0, 50000, None) == abi.E_NULL_ARG
-    assert L.akili_sm_clock_probe(0x1004, 50000, None) == abi.E_ALIGN
-    assert L.akili_sm_clock_probe(0x1000, 10, None) == abi.E_SHAPE
-    assert L.akili_sm_clock_probe(0x1000, 20_000_000, None) == abi.E_SHAPE
+    v = C.c_uint64(0)
+    assert L.akili_sm_clock_read(None, C.byref(v), 0) == abi.E_NULL_ARG
+    assert L.akili_sm_clock_read(C.byref(v), None, 0) == abi.E_NULL_ARG
