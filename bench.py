@@ -59,11 +59,27 @@ FLASH_SHAPE = [8, 32, 4096, 128]  # batch, heads, seq, head_dim; --
 # cache flush, so every operand is read cold).  Workloads or shapes without
 # a capture report null.
 NCU_TRAFFIC = {
-    # gemm_pair_kernel, C2: 171.7 MB read + 49.7 MB written
-    ("kbt_gemm_add_relu", 8192): 221.4e6,
-    # softmax_rows_kernel: 5.5 MB read + 74.5 MB written (part of the output
-    # is still in L2 when the kernel ends)
-    ("kbt_attention_score", 16384): 80.0e6,
+    # gemm_pair_kernel (row-block-major tiles): 111.52 MB read + 49.44 MB written
+    ("kbt_gemm_add_relu", 8192): 160.96e6,
+    ("kbt_gemm_mul_leakyrelu", 8192): 164.05e6,  # 114.00 + 50.05
+    ("kbt_gemm_div_sum_scale", 8192): 104.84e6,  # 101.00 + 3.84 (row partials only)
+    ("kbt_matmul_scale_residadd_clamp", 8192): 106.45e6,  # 101.04 + 5.41
+    ("kbt_matmul_sum_max_avgpool", 8192): 104.93e6,  # 101.01 + 3.92
+    ("kbt_matmul_softmax", 8192): 158.83e6,  # row-fused: 111.48 + 47.35
+    ("kbt_gemm_layernorm", 16384): 302.36e6,  # row-fused: 186.20 + 116.16
+    # the dual GEMM (groups of row blocks: its 172 MB of weights exceed L2);
+    # the RMSNorm pre-pass before it moves another 167.01 + 88.17 MB
+    ("kbt_gemm_rmsnorm_swiglu", 16384): 1592.65e6,  # 1240 + 352.65
+    ("kbt_gemm_silu_mul", 16384): 1612.56e6,  # 1260 + 352.56
+    ("kb2_gemm_add_relu", 8192): 806.58e6,  # split mode, fp32 in and out: 687.75 + 118.83
+    # softmax_rows_kernel: 5.52 MB read + 74.69 MB written (part of the
+    # output is still in L2 when the kernel ends)
+    ("kbt_attention_score", 16384): 80.21e6,
+    ("kbt_sgemm", 128): 0.0876e6,  # gemm_kernel, one tile: 87.55 KB read
+    # flash_fwd_kernel at B8 H32 S4096 d128: 805.35 / 805.44 MB read (Q, K, V
+    # once) + 247.40 / 251.13 MB written
+    ("flash", 0): 1052.75e6,
+    ("flash_causal", 0): 1056.57e6,
     # matvec_kernel: the QKV launch moved 207.33 MB for 201.39 MB of
     # algorithmic bytes; scaled by that ratio to one token's 26.43 GB (the
     # whole token's 26 GB of weights is too large for a multi-pass capture)
