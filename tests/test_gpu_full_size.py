@@ -6,7 +6,13 @@ Every output is checked against properties that hold at any size.  Sampled
 rows are also checked against the oracle, to the parity bar
 (max|err| <= 1e-2 * max|ref|, row cosine >= 0.9999), on the same
 fp16-rounded operands.  Rows are independent for every op, so the oracle
-runs on the sampled rows alone.
+runs on the sampled rows alone.  The samples include the rows either side of
+a CTA (128 rows) and a CTA-pair tile (256 rows) boundary, and the last rows.
+
+The column tiles are never ragged at these shapes (4096 = 16 x 256 and
+11008 = 43 x 256): the ragged-N paths (the TMA store clipping the last tile,
+partial statistics slots) are covered in test_gpu_kbt.py, e.g. N = 4104,
+8200 and 18952.
 """
 import numpy as np
 import pytest
@@ -20,7 +26,7 @@ pytestmark = pytest.mark.gpu
 
 
 def rows_of(M):
-    return sorted({0, 1, M // 3, M // 2, (2 * M) // 3, M - 2, M - 1})
+    return sorted({0, 1, 127, 128, 255, 256, M // 3, M // 2, (2 * M) // 3, M - 129, M - 128, M - 2, M - 1})
 
 
 def gen(seed):
@@ -45,7 +51,7 @@ def test_add_relu_c2(oracle):
     assert torch.isfinite(out).all() and (out >= 0).all()  # ReLU
     assert (out > 0).float().mean().item() > 0.3
     r = rows_of(M)
-    ref = oracle.kbt_gemm_add_relu(host(x[r]), host(w), host(b), len(r), N, K)
+    ref = oracle.kbt_gemm_add_relu(host(x[r]), host(w), host(b), len(r), N, K, threads=8)
     assert_parity(host(out[r]), ref, what="add_relu C2")
 
 
@@ -62,7 +68,8 @@ def test_layernorm_c3(oracle):
     assert z.mean(dim=1).abs().max().item() < 1e-2
     assert (z.var(dim=1, unbiased=False) - 1).abs().max().item() < 2e-2
     r = rows_of(M)
-    ref = oracle.kbt_gemm_layernorm(host(x[r]), host(w), host(b), host(gam), host(bet), len(r), N, K, 1e-5)
+    ref = oracle.kbt_gemm_layernorm(host(x[r]), host(w), host(b), host(gam), host(bet), len(r), N, K, 1e-5,
+                                    threads=8)
     assert_parity(host(out[r]), ref, what="layernorm C3")
 
 
@@ -75,9 +82,24 @@ def test_rmsnorm_swiglu_c4(oracle):
     out = ops.kbt_gemm_rmsnorm_swiglu(x, rw, wg, wu, 1e-6)
     torch.cuda.synchronize()
     assert torch.isfinite(out).all()
-    r = rows_of(M)[:4]
-    ref = oracle.kbt_gemm_rmsnorm_swiglu(host(x[r]), host(rw), host(wg), host(wu), len(r), N, K, 1e-6)
+    r = rows_of(M)
+    ref = oracle.kbt_gemm_rmsnorm_swiglu(host(x[r]), host(rw), host(wg), host(wu), len(r), N, K, 1e-6, threads=8)
     assert_parity(host(out[r]), ref, what="rmsnorm_swiglu C4")
+
+
+def test_matmul_softmax_c2_row_fused(oracle):
+    """kbt_matmul_softmax at the C2 shape: the row-fused epilogue (row
+    statistics merged across the 16 tiles of each row) in one launch."""
+    M, N, K = 8192, 4096, 4096
+    g = gen(5)
+    a, b = randn(g, (M, K)), randn(g, (K, N), 3 * K ** -0.5)
+    out = ops.kbt_matmul_softmax(a, b)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and (out >= 0).all()
+    assert (out.float().sum(dim=1) - 1).abs().max().item() < 5e-3  # every row sums to one
+    r = rows_of(M)
+    ref = oracle.kbt_matmul_softmax(host(a[r]), host(b), len(r), N, K, threads=8)
+    assert_parity(host(out[r]), ref, what="matmul_softmax C2")
 
 
 def test_flash_c5(oracle):
