@@ -84,6 +84,10 @@ NCU_TRAFFIC = {
     # algorithmic bytes; scaled by that ratio to one token's 26.43 GB (the
     # whole token's 26 GB of weights is too large for a multi-pass capture)
     ("llama2_7b_decode", 0): 27.21e9,
+    # matvec_kernel, the 25 launches of one stories15M token captured with
+    # --cache-control none (its 61 MB of weights mostly stay in L2):
+    # 23.20 MB read + 4.16 MB written
+    ("llama2_stories15m_decode", 0): 27.36e6,
 }
 
 
