@@ -21,6 +21,8 @@
 #include <map>
 #include <string>
 #include <mutex>
+#include <thread>
+#include <tuple>
 #include <utility>
 
 #include "../../include/akili.h"
@@ -158,10 +160,60 @@ bool map3d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, uint64_t d0,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// ------------------------------------------------------------- contexts --
+// Identity of the calling thread's current CUDA context: the current
+// device's primary context under the runtime API.  A device reset destroys
+// that context and every device address it handed out; the next runtime call
+// creates a new one with a new identity.  Caches of device addresses are keyed
+// by it, so none outlives its context.  Without the driver entry points (a
+// driver older than CUDA 12.0) the device ordinal stands in.
+int current_context_id(unsigned long long* id) {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(p);
+    cudaGetLastError();
+  });
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return AKILI_E_NO_DEVICE;
+  }
+  constexpr unsigned long long kOrdinalTag = 1ull << 63;  // context ids count up from 1
+  if (!get_current || !get_id) {
+    *id = kOrdinalTag | static_cast<unsigned long long>(dev);
+    return AKILI_OK;
+  }
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+    // no context current on this thread yet: cudaSetDevice makes the
+    // device's primary context current, creating it if need be
+    if (cudaSetDevice(dev) != cudaSuccess || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+      cudaGetLastError();
+      return AKILI_E_NO_DEVICE;
+    }
+  }
+  if (get_id(ctx, id) != CUDA_SUCCESS) return AKILI_E_NO_DEVICE;
+  return AKILI_OK;
+}
+
 // --------------------------------------------------------------- scratch --
-// Internal scratch, one grow-only buffer per (device, stream): calls on one
+// Internal scratch, one grow-only buffer per (context, stream): calls on one
 // stream are ordered, so they can share it.  Used when the caller gives no
 // akili_ex_t workspace.  Growing it frees the old buffer (a device sync).
+// cudaStreamPerThread names a different stream in every host thread, so for
+// it the calling thread is part of the key.
 struct Pool {
   void* ptr = nullptr;
   size_t bytes = 0;
@@ -169,11 +221,13 @@ struct Pool {
 
 int pool_get(cudaStream_t st, size_t bytes, void** out) {
   static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, Pool> pools;
-  int dev = 0;
-  cudaGetDevice(&dev);
+  static std::map<std::tuple<unsigned long long, cudaStream_t, std::thread::id>, Pool> pools;
+  unsigned long long ctx = 0;
+  int rc = current_context_id(&ctx);
+  if (rc) return rc;
+  const std::thread::id owner = st == cudaStreamPerThread ? std::this_thread::get_id() : std::thread::id();
   std::lock_guard<std::mutex> g(mu);
-  Pool& p = pools[{dev, st}];
+  Pool& p = pools[{ctx, st, owner}];
   if (p.bytes < bytes) {
     if (p.ptr) cudaFree(p.ptr);
     p.ptr = nullptr;
@@ -1113,15 +1167,14 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[AKILI_NOALLOC_S
 
 // Device address of g_noalloc_scratch for the current device.  In host code
 // the array's name is only a host-side stand-in; the kernel must be given the
-// address cudaGetSymbolAddress returns, looked up once per device.
+// address cudaGetSymbolAddress returns, looked up once per device (per
+// context: a device reset reloads the module at a new address).
 int noalloc_scratch_ptr(void** out) {
   static std::mutex mu;
-  static std::map<int, void*> addr;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return AKILI_E_NO_DEVICE;
-  }
+  static std::map<unsigned long long, void*> addr;
+  unsigned long long dev = 0;
+  int rc = current_context_id(&dev);
+  if (rc) return rc;
   std::lock_guard<std::mutex> g(mu);
   auto it = addr.find(dev);
   if (it == addr.end()) {

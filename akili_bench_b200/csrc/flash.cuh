@@ -16,12 +16,15 @@
 //                While one tile's softmax runs, the tensor core works on the
 //                other tile.  Per block: read the half's 64 scores of S_t,j
 //                from TMEM (scores never leave the chip), swap the halves'
-//                maxima through shared memory (one barrier per tile), write
+//                maxima through shared memory (one barrier per tile), rescale
+//                O_t in TMEM only when the running max grows by more than 2^8
+//                (the stale max cancels in O / l), then write
 //                P = exp2(scale*log2e*s - m) as packed fp16 over the first 64
-//                columns of S_t, and rescale O_t in TMEM only when the running
-//                max grows by more than 2^8 (the stale max cancels in O / l).
-//                S_t,j being complete implies O_t += P_t,j-1 V_j-1 is
-//                complete, so the rescale never races the accumulation.
+//                columns of S_t in two parts, announcing each: the P.V
+//                K-steps over the first part's keys start while the second
+//                part is computed.  S_t,j being complete implies
+//                O_t += P_t,j-1 V_j-1 is complete, and the next P.V waits for
+//                the first part, so the rescale never races the accumulation.
 // Finally the halves add their row sums, and each divides its O columns by l,
 // stages them through swizzled shared memory (the drained K/V rings) and
 // TMA-stores them.  Head dims up to 64 use a 64-column tile, up to 128 a
@@ -53,6 +56,36 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #define AKILI_FLASH_EXP_GROUP 0
 #endif
 constexpr int kExpGroup = AKILI_FLASH_EXP_GROUP;
+
+// The softmax writes each block's P in kPParts parts and announces each one,
+// so the P.V MMAs over the keys of the first parts run while the later parts'
+// exponentials are computed.  Each half of a row holds 64 keys, four P.V
+// K-steps of 16 keys (8 packed P columns each); part p covers K-steps
+// [p * kPSteps, (p + 1) * kPSteps) of both halves.  At B8 H32 S4096 d128 two
+// parts measured +4% over one (full mask and causal); four parts, or two
+// uneven ones (1 + 3 or 3 + 1 K-steps), gained less.
+#ifndef AKILI_FLASH_P_PARTS
+#define AKILI_FLASH_P_PARTS 2
+#endif
+constexpr int kPParts = AKILI_FLASH_P_PARTS;
+static_assert(kPParts == 1 || kPParts == 2 || kPParts == 4, "P is announced in 1, 2 or 4 parts");
+constexpr int kPSteps = 4 / kPParts;  // P.V K-steps per part and half
+constexpr int kPPairs = 8 * kPSteps;  // packed P columns (score pairs) per part and half
+
+// Store one part's n = kPPairs packed P columns (8, 16 or 32); waits for it.
+template <int n>
+__device__ __forceinline__ void tmem_st_p(uint32_t taddr, const uint32_t (&v)[n]) {
+  if constexpr (n == 32) {
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+    tmem_st32(taddr, f);
+  } else if constexpr (n == 16) {
+    tmem_st16(taddr, v);
+  } else {
+    tmem_st8(taddr, v);
+  }
+}
 
 struct FlashArgs {
   int seq_len;
@@ -114,6 +147,9 @@ __global__ void __maxnreg__(96)
   // [tile][parity]: a wait that gave up in block j sets slot j & 1, read by
   // the whole tile after block j's barrier (the next block's slot is apart)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+  uint64_t* p_part = bars + 19;   // [kPParts - 1][2]: parts before the last of P_t
+  // the barrier that announces part p of tile t's P (the last is p_full)
+  auto p_bar = [&](int p, int t) { return p == kPParts - 1 ? &p_full[t] : &p_part[2 * p + t]; };
 
   const int N = fa.seq_len;
   // Causal: the CTA of query tile pair x visits 2x + 2 key blocks, so the
@@ -143,6 +179,7 @@ __global__ void __maxnreg__(96)
       mbar_init(&rel[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 8);  // one arrive per softmax warp of the tile
+      for (int p = 0; p + 1 < kPParts; ++p) mbar_init(&p_part[2 * p + s], 8);
       mbar_init(&o_done[s], 1);
     }
     mbar_init(drain, 1);
@@ -196,24 +233,28 @@ __global__ void __maxnreg__(96)
     // ------------------------------------------------------------- MMA
     constexpr uint32_t idesc_s = make_idesc_f16(kFlashBM, kFlashBN, false, false);  // K-major K
     constexpr uint32_t idesc_o = make_idesc_f16(kFlashBM, DP, false, true);         // MN-major V
-    bool ok = true;
-    if (lane == 0) {
-      ok = mbar_wait(q_full, 0, kSiteFlashQ);
-      // Shared-memory descriptors are built once; the start-address field is
-      // (address >> 4) in the low bits, so an operand at byte offset `off`
-      // from a base is base descriptor + (off >> 4).  One MMA here is only
-      // 64 tensor cycles and the MMA queue is shallow, so the issuing thread
-      // keeps its own work between MMAs small: an add per operand, one
-      // batched wait at the top of each iteration and three commits.
+    // The whole warp runs the issue loop, converged: every lane waits, each
+    // wait's outcome is made warp-uniform, and one elected lane (lane 0, so
+    // the commits track its MMAs) issues each MMA and commit.  One MMA here
+    // is only 64 tensor cycles; issued from a single diverged lane the loop
+    // fell behind the tensor pipe (at most 0.80 TFLOP/s per MHz even with no
+    // softmax at all).  Shared-memory descriptors are built once; the
+    // start-address field is (address >> 4) in the low bits, so an operand at
+    // byte offset `off` from a base is base descriptor + (off >> 4).
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, kSiteFlashQ));
+    {
       const uint64_t qd0 = make_sdesc(smem_u32(sQ), 16, 1024, kSw128);
       const uint64_t kd0 = make_sdesc(smem_u32(sK), 16, 1024, kSw128);
       const uint64_t vd0 = make_sdesc(smem_u32(sV), 16384, 1024, kSw128);
       for (int j = 0; j <= nkv && ok; ++j) {
         const int st = j & 1;
         const int jj = j - 1;  // the block whose P.V this iteration issues
-        // K_j, V_j-1 and P_0,j-1 in one wait; P_1,j-1 before its P.V.
-        ok = mbar_wait3(j < nkv ? &k_full[st] : nullptr, (j >> 1) & 1, j >= 1 ? &v_full[jj & 1] : nullptr,
-                        (jj >> 1) & 1, (j >= 1 && j <= nkv_t0) ? &p_full[0] : nullptr, jj & 1, kSiteFlashKV);
+        // K_j, V_j-1 and the first part of P_0,j-1 in one wait; every other
+        // part of P just before the P.V K-steps that read it.
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait3(j < nkv ? &k_full[st] : nullptr, (j >> 1) & 1, j >= 1 ? &v_full[jj & 1] : nullptr,
+                                   (jj >> 1) & 1, (j >= 1 && j <= nkv_t0) ? p_bar(0, 0) : nullptr, jj & 1,
+                                   kSiteFlashKV));
         const uint64_t kd = kd0 + static_cast<uint64_t>((st * L::kKV) >> 4);
         const uint64_t vd = vd0 + static_cast<uint64_t>(((jj & 1) * L::kKV) >> 4);
 #pragma unroll
@@ -221,21 +262,30 @@ __global__ void __maxnreg__(96)
           if (!ok) break;
           const int nkv_t = t == 0 ? nkv_t0 : nkv;
           if (j >= 1 && j <= nkv_t) {
-            // O_t += P_t,j-1 . V_j-1
-            if (t > 0) ok = mbar_wait(&p_full[t], jj & 1, kSiteFlashP);
-            if (!ok) break;
-            tc_fence_after();
+            // O_t += P_t,j-1 . V_j-1, part by part as the softmax announces P.
+            // K-step 0 goes first, so it alone starts a fresh accumulator.
             const uint32_t o_tmem = tmem + kColO + t * 128;
             const uint32_t p_tmem = tmem + t * 128;
 #pragma unroll
-            for (int k = 0; k < kFlashBN / 16; ++k)
-              umma_f16_ts(o_tmem, p_tmem + k * 8, vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_o,
-                          (jj | k) != 0);
+            for (int p = 0; p < kPParts; ++p) {
+              if (t > 0 || p > 0) ok = __all_sync(0xffffffffu, mbar_wait(p_bar(p, t), jj & 1, kSiteFlashP));
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int q = 0; q < kPSteps; ++q) {
+                  const int k = 4 * h + p * kPSteps + q;
+                  umma_f16_ts_warp(o_tmem, p_tmem + k * 8, vd + static_cast<uint64_t>((k * 2048) >> 4), idesc_o,
+                                   (jj | k) != 0);
+                }
+            }
+            if (!ok) break;
           }
           // O_t is final once every MMA issued so far completes; both tiles
           // commit in the last iteration, when the K/V rings that the output
           // staging reuses are drained.
-          if (j == nkv) umma_commit(&o_done[t]);
+          if (j == nkv) umma_commit_warp(&o_done[t]);
           if (j < nkv_t) {
             // S_t,j = Q_t . K_j^T
             tc_fence_after();
@@ -246,21 +296,22 @@ __global__ void __maxnreg__(96)
               const uint64_t off = static_cast<uint64_t>(((k >> 2) * 16384 + (k & 3) * 32) >> 4);
               const uint64_t qh = qd + off;
               const uint64_t kh = kd + off;
-              umma_f16_ss(s_tmem, qh, kh, idesc_s, k != 0);
+              umma_f16_ss_warp(s_tmem, qh, kh, idesc_s, k != 0);
               if constexpr (kSplit) {
-                umma_f16_ss(s_tmem, qh, kh + static_cast<uint64_t>((2 * L::kKV) >> 4), idesc_s, 1);
-                umma_f16_ss(s_tmem, qh + static_cast<uint64_t>((kFlashQTiles * L::kQ) >> 4), kh, idesc_s, 1);
+                umma_f16_ss_warp(s_tmem, qh, kh + static_cast<uint64_t>((2 * L::kKV) >> 4), idesc_s, 1);
+                umma_f16_ss_warp(s_tmem, qh + static_cast<uint64_t>((kFlashQTiles * L::kQ) >> 4), kh, idesc_s,
+                                 1);
               }
             }
-            umma_commit(&s_full[t]);
+            umma_commit_warp(&s_full[t]);
           }
         }
         if (!ok) break;
         // K_j (read by S_t,j) and V_j-1 (read by P_t,j-1 . V_j-1) are free once
         // this iteration's MMAs complete.
-        umma_commit(&rel[st]);
+        umma_commit_warp(&rel[st]);
       }
-      umma_commit(drain);
+      umma_commit_warp(drain);
       mbar_wait(drain, 0, kSiteDrain);
     }
     __syncwarp();
@@ -331,51 +382,57 @@ __global__ void __maxnreg__(96)
       const bool grow = rmax > m_use + kRescaleThreshold;
       const float m_new = grow ? rmax : m_use;
       const float alpha = grow ? exp2f(m_use - m_new) : 1.0f;  // 0 on the first block
+      // Rescale this half's O columns when the running max grew (rare after
+      // the first blocks), before any part of P is announced: S_t,j being
+      // complete implies O_t += P_t,j-1 V_j-1 is, and the next P.V waits for
+      // this warp's first arrive below.
+      // The scores are live here, so O goes through in 8-column chunks.
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+        for (int c = 0; c < DP / 16; ++c) {
+          uint32_t o[8];
+          tmem_ld8(tO + c * 8, o);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st8(tO + c * 8, o);
+        }
+      }
       // P = exp2(s * sl - m) as packed fp16: per score pair one packed FFMA,
       // two exponentials (MUFU, or the FMA pipe for one pair in kExpGroup),
-      // one packed add into the row sum and one pack; one TMEM store.
+      // one packed add into the row sum and one pack.  Each part is one TMEM
+      // store and one arrive per warp (the store has completed when it returns).
       const uint64_t sl2 = f2_pack(sl, sl);
       const uint64_t nm2 = f2_pack(-m_new, -m_new);
       uint64_t sm2[4];
 #pragma unroll
       for (int a = 0; a < 4; ++a) sm2[a] = 0ull;
-      float pk[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const bool fma_pipe = kExpGroup > 0 && (i % (kExpGroup > 0 ? kExpGroup : 1)) == kExpGroup - 1;
-        float x0, x1, p0, p1;
-        f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2, nm2), x0, x1);
-        if (fma_pipe) {
-          exp2_fma3_pair(x0, x1, p0, p1);
-        } else {
-          p0 = ex2_mufu(x0);
-          p1 = ex2_mufu(x1);
+      for (int p = 0; p < kPParts; ++p) {
+        uint32_t pk[kPPairs];
+#pragma unroll
+        for (int ii = 0; ii < kPPairs; ++ii) {
+          const int i = p * kPPairs + ii;
+          const bool fma_pipe = kExpGroup > 0 && (i % (kExpGroup > 0 ? kExpGroup : 1)) == kExpGroup - 1;
+          float x0, x1, p0, p1;
+          f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sl2, nm2), x0, x1);
+          if (fma_pipe) {
+            exp2_fma3_pair(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_mufu(x0);
+            p1 = ex2_mufu(x1);
+          }
+          sm2[i & 3] = f2_add(sm2[i & 3], f2_pack(p0, p1));
+          pk[ii] = pack_half2(p0, p1);
         }
-        sm2[i & 3] = f2_add(sm2[i & 3], f2_pack(p0, p1));
-        pk[i] = __uint_as_float(pack_half2(p0, p1));
+        tmem_st_p(tP + p * kPPairs, pk);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_bar(p, grp));
       }
-      tmem_st32(tP, pk);
       float sv[8];
 #pragma unroll
       for (int a = 0; a < 4; ++a) f2_unpack(sm2[a], sv[2 * a], sv[2 * a + 1]);
       const float rsum = ((sv[0] + sv[1]) + (sv[2] + sv[3])) + ((sv[4] + sv[5]) + (sv[6] + sv[7]));
-      // Rescale this half's O columns when the running max grew (rare after
-      // the first blocks): S_t,j being complete implies O_t += P_t,j-1 V_j-1
-      // is, and the next P.V waits for this warp's arrive below.
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll 1
-        for (int c = 0; c < DP / 64; ++c) {
-          float o[32];
-          tmem_ld32(tO + c * 32, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      // this warp's P is in TMEM (tcgen05.st waited): one arrive per warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[grp]);
       l = l * alpha + rsum;
       m_use = m_new;
     }

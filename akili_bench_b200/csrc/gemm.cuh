@@ -615,17 +615,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (lane == 0) ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+      // The whole warp issues, converged: each wait's outcome is made
+      // warp-uniform and one elected lane (lane 0) issues each MMA and commit.
+      ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty));
       if (!ok) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * kAccCols;
       for (int kb = 0; kb < num_kb; ++kb) {
-        if (lane == 0) ok = mbar_wait(&full[stage], phase, kSiteMmaFull);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, kSiteMmaFull));
         if (!ok) break;
         tc_fence_after();
-        if (lane == 0) {
+        {
           const uint32_t sa = smem_u32(ring + stage * kSB);
           const uint32_t sb = sa + kATileBytes;
 #pragma unroll
@@ -643,30 +643,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int op = 0; op < kOps; ++op) {
               const uint32_t d = d_tmem + op * 128;
               const uint64_t bd = bdesc(op * 16384);
-              umma_f16_ss(d, ad, bd, idesc, accum);
+              umma_f16_ss_warp(d, ad, bd, idesc, accum);
               if constexpr (kSplit) {
-                umma_f16_ss(d, ad, bdesc(kStageBytes + op * 16384), idesc, 1);
-                umma_f16_ss(d, make_sdesc(sa + kStageBytes + k * 32, 16, 1024, kSw128), bd, idesc, 1);
+                umma_f16_ss_warp(d, ad, bdesc(kStageBytes + op * 16384), idesc, 1);
+                umma_f16_ss_warp(d, make_sdesc(sa + kStageBytes + k * 32, 16, 1024, kSw128), bd, idesc, 1);
               }
             }
           }
-          umma_commit(&empty[stage]);
+          umma_commit_warp(&empty[stage]);
         }
-        __syncwarp();
         if (++stage == kSt) {
           stage = 0;
           phase ^= 1;
         }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&acc_full[acc]);
-      __syncwarp();
+      umma_commit_warp(&acc_full[acc]);
     }
     // Drain: every issued MMA has completed before TMEM is released.
-    if (lane == 0) {
-      umma_commit(drain);
-      mbar_wait(drain, 0, kSiteDrain);
-    }
+    umma_commit_warp(drain);
+    mbar_wait(drain, 0, kSiteDrain);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -896,7 +892,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     // producer).  Two N = 128 pair MMAs (64 columns per CTA) kept the tensor
     // pipe 62% busy; MMAs of 64 columns run at 48 cycles for 32 of work.
     constexpr uint32_t idesc = make_idesc_f16(2 * kBM, 256, false, !kBKMajor);
-    if (leader && lane == 0) {
+    // The whole warp issues, converged: each wait's outcome is made
+    // warp-uniform and one elected lane (lane 0) issues each MMA and commit.
+    if (leader) {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -904,12 +902,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
-        ok = mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
+        ok = __all_sync(0xffffffffu, mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty));
         if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kAccCols;
         for (int kb = 0; kb < num_kb; ++kb) {
-          ok = mbar_wait_cluster(&full[stage], phase, kSiteMmaFull);
+          ok = __all_sync(0xffffffffu, mbar_wait_cluster(&full[stage], phase, kSiteMmaFull));
           if (!ok) break;
           tc_fence_after();
           const uint32_t sa = smem_u32(ring + stage * kSB);
@@ -920,24 +918,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             const uint32_t accum = (kb | k) != 0;
             const uint64_t bd = kBKMajor ? make_sdesc(sb + k * 32, 16, 1024, kSw128)
                                          : make_sdesc(sb + k * 2048, 8192, 1024, kSw128);
-            umma_f16_ss_pair(d_tmem, ad, bd, idesc, accum);
+            umma_f16_ss_pair_warp(d_tmem, ad, bd, idesc, accum);
             if constexpr (kSplit) {  // + A_hi.B_lo + A_lo.B_hi (lo parts kPairStageBytes behind)
               constexpr uint64_t lo = kPairStageBytes >> 4;
-              umma_f16_ss_pair(d_tmem, ad, bd + lo, idesc, 1);
-              umma_f16_ss_pair(d_tmem, ad + lo, bd, idesc, 1);
+              umma_f16_ss_pair_warp(d_tmem, ad, bd + lo, idesc, 1);
+              umma_f16_ss_pair_warp(d_tmem, ad + lo, bd, idesc, 1);
             }
           }
-          umma_commit_pair(&empty[stage], 0x3);
+          umma_commit_pair_warp(&empty[stage], 0x3);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit_pair(&acc_full[acc], 0x3);
+        umma_commit_pair_warp(&acc_full[acc], 0x3);
       }
       // Drain: every issued MMA has completed before either CTA frees TMEM.
-      umma_commit_pair(drain, 0x1);
+      umma_commit_pair_warp(drain, 0x1);
       mbar_wait(drain, 0, kSiteDrain);
     }
     __syncwarp();

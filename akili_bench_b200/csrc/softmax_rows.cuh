@@ -285,7 +285,9 @@ __global__ void __launch_bounds__(kSmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA
     constexpr uint32_t idesc = make_idesc_f16(kBM, 256, false, !kBKMajor);
-    if (lane == 0) {
+    // The whole warp issues, converged: each wait's outcome is made
+    // warp-uniform and one elected lane (lane 0) issues each MMA and commit.
+    {
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -293,18 +295,18 @@ __global__ void __launch_bounds__(kSmThreads, 1)
       bool ok = true;
       const uint32_t sa0 = smem_u32(a_smem);
       for (int rb = blockIdx.x; rb < num_rb && ok; rb += gridDim.x, ++rbi) {
-        ok = mbar_wait(a_full, rbi & 1, kSiteMmaFull);
+        ok = __all_sync(0xffffffffu, mbar_wait(a_full, rbi & 1, kSiteMmaFull));
         if (!ok) break;
         tc_fence_after();
         for (int i = 0; i < 2 * T && ok; ++i, ++it) {
           const int acc = it & 1;
           const uint32_t acc_phase = (it >> 1) & 1;
-          ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty);
+          ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[acc], acc_phase ^ 1, kSiteMmaAccEmpty));
           if (!ok) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + acc * kAccCols;
           for (int kb = 0; kb < KB; ++kb) {
-            ok = mbar_wait(&full[stage], phase, kSiteMmaFull);
+            ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, kSiteMmaFull));
             if (!ok) break;
             tc_fence_after();
             const uint32_t sa = sa0 + kb * kATileBytes;
@@ -314,24 +316,25 @@ __global__ void __launch_bounds__(kSmThreads, 1)
               const uint64_t ad = make_sdesc(sa + k * 32, 16, 1024, kSw128);
               const uint32_t accum = (kb | k) != 0;
               if constexpr (kBKMajor)
-                umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
+                umma_f16_ss_warp(d_tmem, ad, make_sdesc(sb + k * 32, 16, 1024, kSw128), idesc, accum);
               else
-                umma_f16_ss(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc, accum);
+                umma_f16_ss_warp(d_tmem, ad, make_sdesc(sb + k * 2048, 8192, 1024, kSw128), idesc,
+                                 accum);
             }
-            umma_commit(&empty[stage]);
+            umma_commit_warp(&empty[stage]);
             if (++stage == S) {
               stage = 0;
               phase ^= 1;
             }
           }
           if (!ok) break;
-          umma_commit(&acc_full[acc]);
+          umma_commit_warp(&acc_full[acc]);
         }
         if (!ok) break;
-        umma_commit(a_empty);  // the A rows are free once this block's MMAs complete
+        umma_commit_warp(a_empty);  // the A rows are free once this block's MMAs complete
       }
       // Drain: every issued MMA has completed before TMEM is released.
-      umma_commit(drain);
+      umma_commit_warp(drain);
       mbar_wait(drain, 0, kSiteDrain);
     }
     __syncwarp();

@@ -6,7 +6,9 @@
 // weight matrices on the host.  Here:
 //   * a weight matrix that lives in read-only host memory (llama.cpp maps
 //     the checkpoint PROT_READ, llama2/llama.cpp:166) cannot change, so it is
-//     uploaded once and stays resident in HBM, keyed by its host address;
+//     uploaded once and stays resident in HBM, keyed by its host address
+//     and checked on every call against a fingerprint of its host bytes
+//     (a mapping can be replaced by another at the same address);
 //     any other operand is copied for each call, as the reference does;
 //   * vx_matmul with N = 1 is one matrix-vector launch
 //     (akili_llama2_matmul), other N the library's GEMM paths;
@@ -34,9 +36,26 @@ struct DevBuf {
   size_t bytes = 0;
 };
 
+// A read-only mapping cannot change while it is mapped, but it can be unmapped
+// and another mapping (another checkpoint, or writable memory) placed at the
+// same address.  A resident matrix therefore keeps kSamples 32-bit words of
+// its host bytes, at fixed offsets from the first to the last; every call
+// compares them, and a mismatch drops the entry and decides afresh.
+constexpr int kSamples = 16;
+struct Resident {
+  DevBuf buf;
+  uint32_t sample[kSamples];
+};
+
+void fingerprint(const float* host, size_t bytes, uint32_t (&out)[kSamples]) {
+  const size_t words = bytes / 4;
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(host);
+  for (int i = 0; i < kSamples; ++i) out[i] = words ? w[(words - 1) * i / (kSamples - 1)] : 0u;
+}
+
 struct State {
   bool open = false;
-  std::unordered_map<const float*, DevBuf> resident;  // read-only host matrices
+  std::unordered_map<const float*, Resident> resident;  // read-only host matrices
   std::vector<std::pair<uintptr_t, uintptr_t>> ro_ranges;  // read-only mappings seen so far
   DevBuf x, y, a;  // per-call operand, result and non-resident matrix buffers
 };
@@ -87,18 +106,29 @@ bool read_only(const void* p, size_t bytes) {
 // else copied into the per-call buffer `scratch`.
 const float* matrix_on_device(const float* host, size_t bytes, DevBuf& scratch) {
   auto it = g.resident.find(host);
-  if (it != g.resident.end() && it->second.bytes >= bytes) return static_cast<const float*>(it->second.ptr);
+  if (it != g.resident.end()) {
+    uint32_t now[kSamples];
+    fingerprint(host, bytes, now);
+    if (it->second.buf.bytes >= bytes && std::memcmp(now, it->second.sample, sizeof(now)) == 0)
+      return static_cast<const float*>(it->second.buf.ptr);
+    // another size or other bytes at this address: the mapping may have
+    // changed, so forget the entry and the read-only ranges that cover it
+    VXM_CHECK(cudaFree(it->second.buf.ptr));
+    g.resident.erase(it);
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(host);
+    std::vector<std::pair<uintptr_t, uintptr_t>> keep;
+    for (const auto& r : g.ro_ranges)
+      if (!(lo >= r.first && lo < r.second)) keep.push_back(r);
+    g.ro_ranges.swap(keep);
+  }
   if (read_only(host, bytes)) {
-    DevBuf b;
-    if (it != g.resident.end()) {
-      VXM_CHECK(cudaFree(it->second.ptr));
-      g.resident.erase(it);
-    }
-    VXM_CHECK(cudaMalloc(&b.ptr, bytes));
-    b.bytes = bytes;
-    VXM_CHECK(cudaMemcpy(b.ptr, host, bytes, cudaMemcpyHostToDevice));
-    g.resident.emplace(host, b);
-    return static_cast<const float*>(b.ptr);
+    Resident e;
+    VXM_CHECK(cudaMalloc(&e.buf.ptr, bytes));
+    e.buf.bytes = bytes;
+    VXM_CHECK(cudaMemcpy(e.buf.ptr, host, bytes, cudaMemcpyHostToDevice));
+    fingerprint(host, bytes, e.sample);
+    g.resident.emplace(host, e);
+    return static_cast<const float*>(e.buf.ptr);
   }
   grow(scratch, bytes);
   VXM_CHECK(cudaMemcpyAsync(scratch.ptr, host, bytes, cudaMemcpyHostToDevice, nullptr));
@@ -181,7 +211,7 @@ void vx_matmul(float* C, float* A, float* B, int M, int N, int K) {
 // llama2/vxmath.cpp:36-55
 void matmul_cleanup() {
   if (!g.open) return;
-  for (auto& kv : g.resident) cudaFree(kv.second.ptr);
+  for (auto& kv : g.resident) cudaFree(kv.second.buf.ptr);
   g.resident.clear();
   g.ro_ranges.clear();
   for (DevBuf* b : {&g.x, &g.y, &g.a}) {

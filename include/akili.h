@@ -324,8 +324,9 @@ int akili_kbt_gemm_layernorm_ex(const kbt_gemm_layernorm_arg_t* arg, const akili
  * > AKILI_NOALLOC_SCRATCH_BYTES, returns AKILI_E_SCRATCH_LIMIT (M = 16384 at
  * N = 4096 fits).  Each call zeroes the counters on its stream before its
  * GEMM.  The first call on a device looks up that array's device address
- * (once per device, with the device current); make that first call before
- * any stream capture.  All calls share the array: calls that overlap on the
+ * (once per device and CUDA context, with the device current; after a device
+ * reset the next call looks it up again); make that first call before any
+ * stream capture.  All calls share the array: calls that overlap on the
  * GPU (different streams, or different host threads on one device) race on
  * it and must be serialised by the caller. */
 #define AKILI_NOALLOC_SCRATCH_BYTES ((4u << 20) + (64u << 10))
