@@ -100,11 +100,11 @@ __device__ __forceinline__ float sm_exp2(int j, float x) {
 // Sweep 1 by pairs: of each kSmFmaPairs consecutive column pairs the last
 // goes to the FMA pipe as one packed cubic (exp2_fma3_pair, relative error
 // 7.5e-5, below the rounding of an fp16 output), the rest to the MUFU; 0
-// keeps all on the MUFU (then kSmFmaEvery applies).  The two sweeps'
-// exponentials keep the MUFU about 73% busy; at the 16384 x 4096 x 128
-// attention score one pair in 6 or 5 on the FMA pipe measured 301 / 300
-// TFLOP/s against 284 for none, one in 4 / 3 / 2 295 / 289 / 281.  The same
-// offload in sweep 2 (the fp16 stores) gained nothing.
+// keeps all on the MUFU (then kSmFmaEvery applies).  At the 16384 x 4096 x
+// 128 attention score, with the packed fp32x2 fold, one pair in 6 / 4 / 3
+// measured 306 / 304 / 308 TFLOP/s against 296 for none (scalar fold: 301
+// with one in 6, 284 with none).  The same offload in sweep 2 (the fp16
+// stores) gained nothing.
 #ifndef AKILI_SM_FMA_PAIRS
 #define AKILI_SM_FMA_PAIRS 6
 #endif
@@ -121,24 +121,37 @@ __device__ __forceinline__ void softmax_fold64(const float (&v)[64], int nvalid,
   float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (nvalid >= 64) {
+    if constexpr (kPairs) {
+      // Packed: per score pair one 3-input max, one fp32x2 FMA (x * c - m),
+      // two exponentials and one fp32x2 add into the row sum.
 #pragma unroll
-    for (int j = 0; j < 64; ++j) cm[j & 3] = fmaxf(cm[j & 3], v[j]);
-    const float mnew = fmaxf(m, max4(cm) * c);
-    if constexpr (kPairs && kSmFmaPairs > 0) {
+      for (int jp = 0; jp < 32; ++jp) cm[jp & 3] = fmax3(cm[jp & 3], v[2 * jp], v[2 * jp + 1]);
+      const float mnew = fmaxf(m, max4(cm) * c);
+      const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-mnew, -mnew);
+      uint64_t la2[2] = {0ull, 0ull};
 #pragma unroll
       for (int jp = 0; jp < 32; ++jp) {
-        const float x0 = fmaf(v[2 * jp], c, -mnew), x1 = fmaf(v[2 * jp + 1], c, -mnew);
-        float p0, p1;
-        if (jp % (kSmFmaPairs > 0 ? kSmFmaPairs : 1) == kSmFmaPairs - 1) {
+        float x0, x1, p0, p1;
+        f2_unpack(f2_fma(f2_pack(v[2 * jp], v[2 * jp + 1]), c2, nm2), x0, x1);
+        if (kSmFmaPairs > 0 && jp % (kSmFmaPairs > 0 ? kSmFmaPairs : 1) == kSmFmaPairs - 1) {
           exp2_fma3_pair(x0, x1, p0, p1);
         } else {
           p0 = ex2_mufu(x0);
           p1 = ex2_mufu(x1);
         }
-        la[(2 * jp) & 3] += p0;
-        la[(2 * jp + 1) & 3] += p1;
+        la2[jp & 1] = f2_add(la2[jp & 1], f2_pack(p0, p1));
       }
-    } else {
+      float s0, s1, s2, s3;
+      f2_unpack(la2[0], s0, s1);
+      f2_unpack(la2[1], s2, s3);
+      l = l * ex2_mufu(m - mnew) + ((s0 + s1) + (s2 + s3));
+      m = mnew;
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 64; ++j) cm[j & 3] = fmaxf(cm[j & 3], v[j]);
+    const float mnew = fmaxf(m, max4(cm) * c);
+    {
 #pragma unroll
       for (int j = 0; j < 64; ++j) la[j & 3] += sm_exp2(j, fmaf(v[j], c, -mnew));
     }
@@ -174,10 +187,16 @@ __device__ __forceinline__ void stage_box_exp(uint8_t* box, int lane, const floa
         q.z = ex2_h2(pack_half2(fmaf(v[j + 4], c, -mm), fmaf(v[j + 5], c, -mm)));
         q.w = ex2_h2(pack_half2(fmaf(v[j + 6], c, -mm), fmaf(v[j + 7], c, -mm)));
       } else {
-        q.x = pack_half2(ex2_mufu(fmaf(v[j + 0], c, -mm)), ex2_mufu(fmaf(v[j + 1], c, -mm)));
-        q.y = pack_half2(ex2_mufu(fmaf(v[j + 2], c, -mm)), ex2_mufu(fmaf(v[j + 3], c, -mm)));
-        q.z = pack_half2(ex2_mufu(fmaf(v[j + 4], c, -mm)), ex2_mufu(fmaf(v[j + 5], c, -mm)));
-        q.w = pack_half2(ex2_mufu(fmaf(v[j + 6], c, -mm)), ex2_mufu(fmaf(v[j + 7], c, -mm)));
+        // one fp32x2 FMA (x * c - mm) per pair, then two exponentials
+        const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-mm, -mm);
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(v[j + 2 * e], v[j + 2 * e + 1]), c2, nm2), x0, x1);
+          w[e] = pack_half2(ex2_mufu(x0), ex2_mufu(x1));
+        }
+        q = make_uint4(w[0], w[1], w[2], w[3]);
       }
     } else {
       const int j = j0 + 4 * u;
