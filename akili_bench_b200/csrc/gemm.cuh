@@ -477,6 +477,93 @@ __device__ __forceinline__ void rownorm_half(const EpiArgs& ea, const CUtensorMa
   }
 }
 
+// Row-fused epilogues with fp16 output keep their tile in registers between
+// the passes.  Pass 1 rounds y to fp16, the stored precision, as the
+// two-pass form stores it, folds the rounded values into the row statistics
+// and keeps them as fp16 pairs: a warp's 32 rows x 32 * kChunks columns in
+// 16 * kChunks registers.  The accumulator is then free before the row-block
+// wait, and pass 2 normalises from registers.
+template <Epi E, int kChunks>
+__device__ __forceinline__ RowState rowstats_keep(const EpiArgs& ea, uint32_t tbase, int n0, int c_begin,
+                                                  int c_end, uint32_t (&yh)[kChunks][16]) {
+  RowState st;
+  st.a = (E == Epi::kLnPre) ? 0.0f : -INFINITY;
+  st.b = 0.0f;
+  st.n = 0.0f;
+  float u[32];
+  const LaneVec lv0 = lane_vec(epi_vec0(E) ? ea.vec0 : nullptr, n0, c_begin, c_end, ea.N);
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = c_begin + i;
+    if (c < c_end) {
+      float v[32];
+      tmem_ld32(tbase + c * 32, v);
+      const int col0 = n0 + c * 32;
+      epi_chunk<E, __half>(ea, col0, min(32, ea.N - col0), v, u, st, lane_pick(lv0, i));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) yh[i][j] = pack_half2(v[2 * j], v[2 * j + 1]);
+    }
+  }
+  return st;
+}
+
+// Pass 2 of rowstats_keep's tile: normalise the kept fp16 y (LayerNorm:
+// (y - mean) * rstd * gamma + beta; softmax: exp2(y log2 e - max) / sum),
+// stage and TMA-store it as rownorm_half does.  gamma and beta come as
+// 16-byte loads at one address for the whole warp (four columns each).
+template <Epi E, int kChunks>
+__device__ __forceinline__ void rownorm_regs(const EpiArgs& ea, const CUtensorMap* tmC,
+                                             const uint32_t (&yh)[kChunks][16], int n0, int mrow0, int r,
+                                             int c_begin, int c_end, uint8_t* staging, uint32_t bar_id, bool issuer,
+                                             int& chunk_ctr, float s0, float s1) {
+  constexpr int kStageOut = kBM * 32 * 2;
+  constexpr float kLog2e = 1.4426950408889634f;
+#pragma unroll
+  for (int i = 0; i < kChunks; ++i) {
+    const int c = c_begin + i;
+    if (c >= c_end) break;  // uniform over the 128 threads of the half
+    const int col0 = n0 + c * 32;
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&yh[i][2 * q + e]);
+        const float2 f = __half22float2(h);
+        y[2 * e] = f.x;
+        y[2 * e + 1] = f.y;
+      }
+      if constexpr (E == Epi::kLnPre) {
+        const int col = col0 + 4 * q;
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), be = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (col < ea.N) {  // N is a multiple of 8: four columns are all in or all out
+          g = __ldg(reinterpret_cast<const float4*>(ea.ln_w + col));
+          be = __ldg(reinterpret_cast<const float4*>(ea.ln_b + col));
+        }
+        v[4 * q + 0] = ((y[0] - s0) * s1) * g.x + be.x;
+        v[4 * q + 1] = ((y[1] - s0) * s1) * g.y + be.y;
+        v[4 * q + 2] = ((y[2] - s0) * s1) * g.z + be.z;
+        v[4 * q + 3] = ((y[3] - s0) * s1) * g.w + be.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[4 * q + e] = exp2f(fmaf(y[e], kLog2e, -s0)) * s1;
+      }
+    }
+    uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
+    if (issuer) bulk_wait_read<1>();
+    named_bar_sync(bar_id, 128);
+    stage_row<__half>(stg, r, v);
+    fence_async_shared();
+    named_bar_sync(bar_id, 128);
+    if (issuer) {
+      tma_store_2d(tmC, stg, col0, mrow0);
+      bulk_commit();
+    }
+    ++chunk_ctr;
+  }
+}
+
 // Per-row partial statistics of one half tile go to slot `slot` of the
 // [stat][slot][M] workspace (two slots per BN-column tile).
 template <Epi E>
@@ -982,7 +1069,21 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
         const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
         const int c0 = grp * HC, c1 = min((grp + 1) * HC, nchunks);
-        const RowState st = rowstats_half<E>(ea, tbase, n0, c0, c1);
+        constexpr bool kKeep = sizeof(OutT) == 2;  // fp16 out: the tile stays in registers
+        uint32_t yh[kKeep ? HC : 1][16];
+        RowState st;
+        if constexpr (kKeep) {
+          st = rowstats_keep<E, HC>(ea, tbase, n0, c0, c1, yh);
+          // pass 2 reads registers: release the accumulator before the wait
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) mbar_arrive(&acc_empty[acc]);
+            else mbar_arrive_cluster(acc_empty_c + acc * 8);
+          }
+        } else {
+          st = rowstats_half<E>(ea, tbase, n0, c0, c1);
+        }
         write_stats<E>(ea, 2 * n_blk + grp, mrow0 + r, st);
         __threadfence();
         named_bar_sync(3, 256);
@@ -996,13 +1097,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         __threadfence();
         float s0, s1;
         rowstats_merge<E>(ea, mrow0 + r, s0, s1);
-        rownorm_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, c0, c1, gstaging, bar_id, gtid == 0, chunk_ctr, s0,
-                              s1);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) mbar_arrive(&acc_empty[acc]);
-          else mbar_arrive_cluster(acc_empty_c + acc * 8);
+        if constexpr (kKeep) {
+          rownorm_regs<E, HC>(ea, &tmC, yh, n0, mrow0, r, c0, c1, gstaging, bar_id, gtid == 0, chunk_ctr, s0, s1);
+        } else {
+          rownorm_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, c0, c1, gstaging, bar_id, gtid == 0, chunk_ctr, s0,
+                                s1);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) mbar_arrive(&acc_empty[acc]);
+            else mbar_arrive_cluster(acc_empty_c + acc * 8);
+          }
         }
       }
     } else {

@@ -591,6 +591,56 @@ def link_probe(torch, nbytes: int = 256 << 20, reps: int = 4) -> dict:
                    "both directions at once on two streams"}
 
 
+def cublas_same_shape(torch, d, args, ours: dict):
+    """cuBLAS (torch.matmul, fp16) on the line's own x [M, K] and w [K, N],
+    timed as the line is: the 252 MiB flush before every step, the same
+    soak and step count, CUDA events around each step, nvidia-smi clocks
+    sampled meanwhile.  It computes x.w only, with no bias or activation, so
+    it does a little less work than the fused op.  None for workloads without
+    such operands."""
+    x, w = d.get("x"), d.get("w")
+    if (x is None or w is None or x.dim() != 2 or w.dim() != 2 or x.dtype != torch.float16 or
+            w.dtype != torch.float16 or x.shape[1] != w.shape[0]):
+        return None
+    M, K = x.shape
+    N = w.shape[1]
+    out = torch.empty(M, N, device=x.device, dtype=torch.float16)
+    flush = torch.empty(2 * L2_BYTES // 4, device="cuda", dtype=torch.float32)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        torch.matmul(x, w, out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+    except Exception:
+        gpu_id = str(torch.cuda.current_device())
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(gpu_id) as clk:
+        t_end = time.perf_counter() + args.soak
+        while time.perf_counter() < t_end:
+            for _ in range(8):
+                step()
+            torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    value = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    c = clk.summary()
+    return {"value": value, "unit": "TFLOP/s", "ms_per_step": ms, "sm_mhz_smi": c["sm_mhz"],
+            "reasons": c["reasons"], "ours_over_cublas": ours["value"] / value,
+            "what": f"torch.matmul fp16 (cuBLAS) on the same x [{M}, {K}] and w [{K}, {N}], no bias or "
+                    "activation; same flush, soak and step count as the line"}
+
+
 def cpu_leg(d, threads: int, rows_per_thread: int) -> dict:
     """The reference CPU gold (oracle) on the kbt_gemm_add_relu workload:
     the single-thread figure (the reference's gold is a single-threaded loop,
@@ -927,6 +977,10 @@ def run_ours(args):
                 line["cpu_baseline"] = cpu_leg(d, host_threads(), args.cpu_rows_per_thread)
             elif world == 1 and not args.no_cpu and W[name].cpu_fn is not None:
                 line["cpu_baseline"] = W[name].cpu_fn(d)
+            if world == 1 and args.vs_cublas:
+                cb = cublas_same_shape(torch, d, args, line)
+                if cb is not None:
+                    line["cublas_same_shape"] = cb
             print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -947,6 +1001,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--op", default="kbt_gemm_add_relu")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--vs-cublas", action="store_true",
+                    help="(1 GPU) also time cuBLAS's x.w on the line's own operands, same flush and soak")
     ap.add_argument("--cpu-rows-per-thread", type=int, default=48)
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="strong: the configured global problem split across the GPUs (default); weak: every GPU "
