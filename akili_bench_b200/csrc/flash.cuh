@@ -20,9 +20,9 @@
 //                O_t in TMEM only when the running max grows by more than 2^8
 //                (the stale max cancels in O / l), then write
 //                P = exp2(scale*log2e*s - m) as packed fp16 over the first 64
-//                columns of S_t in two parts, announcing each: the P.V
-//                K-steps over the first part's keys start while the second
-//                part is computed.  S_t,j being complete implies
+//                columns of S_t in parts (four at head dim 128, two at 64),
+//                announcing each: the P.V K-steps over the first parts' keys
+//                start while the later parts are computed.  S_t,j being complete implies
 //                O_t += P_t,j-1 V_j-1 is complete, and the next P.V waits for
 //                the first part, so the rescale never races the accumulation.
 // Finally the halves add their row sums, and each divides its O columns by l,
@@ -57,22 +57,26 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #endif
 constexpr int kExpGroup = AKILI_FLASH_EXP_GROUP;
 
-// The softmax writes each block's P in kPParts parts and announces each one,
-// so the P.V MMAs over the keys of the first parts run while the later parts'
+// The softmax writes each block's P in parts and announces each one, so the
+// P.V MMAs over the keys of the first parts run while the later parts'
 // exponentials are computed.  Each half of a row holds 64 keys, four P.V
 // K-steps of 16 keys (8 packed P columns each); part p covers K-steps
-// [p * kPSteps, (p + 1) * kPSteps) of both halves.  At B8 H32 S4096 d128 two
-// parts measured +4% over one (full mask and causal); four parts, or two
-// uneven ones (1 + 3 or 3 + 1 K-steps), gained less.
+// [p * steps, (p + 1) * steps) of both halves.  At B8 H32 S4096 d128, two
+// parts measured +4% over one and four parts +1% over two; two uneven
+// parts (1 + 3 or 3 + 1 K-steps) gained less.  Head dims up to 64 keep two
+// parts (four spill there).  AKILI_FLASH_P_PARTS (1, 2 or 4) overrides both.
 #ifndef AKILI_FLASH_P_PARTS
-#define AKILI_FLASH_P_PARTS 2
+#define AKILI_FLASH_P_PARTS 0
 #endif
-constexpr int kPParts = AKILI_FLASH_P_PARTS;
-static_assert(kPParts == 1 || kPParts == 2 || kPParts == 4, "P is announced in 1, 2 or 4 parts");
-constexpr int kPSteps = 4 / kPParts;  // P.V K-steps per part and half
-constexpr int kPPairs = 8 * kPSteps;  // packed P columns (score pairs) per part and half
+__host__ __device__ constexpr int flash_p_parts(int dp) {
+  return AKILI_FLASH_P_PARTS > 0 ? AKILI_FLASH_P_PARTS : (dp >= 128 ? 4 : 2);
+}
+static_assert(flash_p_parts(64) == 1 || flash_p_parts(64) == 2 || flash_p_parts(64) == 4,
+              "P is announced in 1, 2 or 4 parts");
+static_assert(flash_p_parts(128) == 1 || flash_p_parts(128) == 2 || flash_p_parts(128) == 4,
+              "P is announced in 1, 2 or 4 parts");
 
-// Store one part's n = kPPairs packed P columns (8, 16 or 32); waits for it.
+// Store one part's n packed P columns (8, 16 or 32); waits for it.
 template <int n>
 __device__ __forceinline__ void tmem_st_p(uint32_t taddr, const uint32_t (&v)[n]) {
   if constexpr (n == 32) {
@@ -125,6 +129,9 @@ __global__ void __maxnreg__(96)
                      const FlashArgs fa) {
   using L = FlashSmem<DP, kSplit>;
   constexpr int kChunks = DP / 64;  // 64-column swizzle chunks of Q/K/V
+  constexpr int kPParts = flash_p_parts(DP);
+  constexpr int kPSteps = 4 / kPParts;  // P.V K-steps per part and half
+  constexpr int kPPairs = 8 * kPSteps;  // packed P columns (score pairs) per part and half
   constexpr int kStageOut = kFlashBM * 32 * sizeof(OutT);
   constexpr uint32_t kColO = 256;   // O_t at 256 + 128 t; S_t / P_t at 128 t
 
