@@ -9,8 +9,9 @@
 //   warp 1       TMEM owner and MMA issuer.  Per key block j and Q tile t:
 //                  O_t += P_t,j-1 . V_j-1   (A = P from TMEM, B = V, MN-major)
 //                  S_t,j  = Q_t . K_j^T     (into the columns P_t,j-1 occupied)
-//                Issued in that order on one thread, the MMAs run in order, so
-//                S may overwrite P once the P.V that reads it is ahead of it.
+//                Issued in that order by one elected lane of the converged
+//                warp, the MMAs run in order, so S may overwrite P once the
+//                P.V that reads it is ahead of it.
 //   warps 2..9   softmax of Q tile 0, warps 10..17 of Q tile 1: two threads
 //                per query row, each taking 64 of the block's 128 scores.
 //                While one tile's softmax runs, the tensor core works on the

@@ -9,8 +9,9 @@
 //               into a kStages-deep shared-memory ring (full/empty mbarriers).
 //   warp 1      allocates 512 TMEM columns (two 256-column accumulators) and
 //               issues tcgen05.mma (M=128, N=256 or 2 x N=128 for the dual
-//               GEMMs, K=16 per instruction) from one thread; tcgen05.commit
-//               frees ring slots and publishes finished accumulators.
+//               GEMMs, K=16 per instruction) from the whole warp, converged,
+//               one elected lane issuing; tcgen05.commit frees ring slots and
+//               publishes finished accumulators.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one thread per
 //               output row), apply the op, and either stage the tile through
 //               swizzled shared memory for a TMA store (which also clips the

@@ -223,30 +223,12 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem], fp16 inputs, fp32 accumulate; issued by one thread.
-__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem]: A is read from tensor memory, one row per
-// lane, two fp16 values per 32-bit column (K = 16 spans 8 columns).
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Warp-wide forms: the whole (converged) warp executes them and elect.sync
-// picks one lane, the lowest, lane 0, to issue.  The issuing loop then runs on
-// a converged warp, so its operand arithmetic stays warp-uniform.
+// MMA issue, executed by the whole (converged) warp: elect.sync picks one
+// lane, the lowest, lane 0, to issue, so that the issuing loop runs on a
+// converged warp and its operand arithmetic stays warp-uniform.  Every
+// commit comes from the same lane, so it tracks all the MMAs issued before it.
+//
+// D[tmem] (+)= A[smem] * B[smem], fp16 inputs, fp32 accumulate.
 __device__ __forceinline__ void umma_f16_ss_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                  uint32_t accumulate) {
   asm volatile(
@@ -257,6 +239,8 @@ __device__ __forceinline__ void umma_f16_ss_warp(uint32_t d_tmem, uint64_t adesc
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]: A is read from tensor memory, one row per
+// lane, two fp16 values per 32-bit column (K = 16 spans 8 columns).
 __device__ __forceinline__ void umma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                                  uint32_t accumulate) {
   asm volatile(
@@ -267,19 +251,13 @@ __device__ __forceinline__ void umma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tme
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Arrive once on `bar` when all previously issued tcgen05.mma complete.
 __device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
       : "memory");
-}
-
-// Arrive once on `bar` when all previously issued tcgen05.mma of this thread complete.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
 }
 
 // 32 lanes x 32 consecutive fp32 columns: thread t of the warp receives lane
@@ -462,16 +440,9 @@ __device__ __forceinline__ void tmem_relinquish_pair() {
 __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Warp-wide forms of the two above (see umma_f16_ss_warp).
+// The CTA-pair forms, executed by the even CTA's whole MMA warp (see
+// umma_f16_ss_warp): D (M = 256 over both CTAs' TMEM) (+)= A * B, each CTA
+// holding its half of A and of B.
 __device__ __forceinline__ void umma_f16_ss_pair_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                                       uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -482,21 +453,14 @@ __device__ __forceinline__ void umma_f16_ss_pair_warp(uint32_t d_tmem, uint64_t 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Arrive once on the barrier at this shared-memory offset in every CTA of
+// `cta_mask` when all previously issued tcgen05.mma complete.
 __device__ __forceinline__ void umma_commit_pair_warp(uint64_t* bar, uint16_t cta_mask) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
       "\n\t}" ::"r"(smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
-// Arrive once on the barrier at this shared-memory offset in every CTA of
-// `cta_mask` when all prior tcgen05.mma of this thread complete.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
       "h"(cta_mask)
       : "memory");
 }
