@@ -1236,6 +1236,16 @@ int entry_kb2(const Arg* a, const akili_ex_t* ex, akili_stream_t s) {
 // FFN hidden size, 11008 for 7B: 44 KB).
 constexpr size_t kMatvecSmemMax = 200 * 1024;
 
+// AKILI_PDL=0 launches the matrix-vector kernels without the programmatic
+// dependent launch attribute (for A/B measurements).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("AKILI_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <bool kVec, bool kSmemX>
 int launch_matvec_t(const DevInfo& di, const MatvecArgs& a, cudaStream_t st) {
   auto kern = matvec_kernel<kVec, kSmemX>;
@@ -1260,7 +1270,24 @@ int launch_matvec_t(const DevInfo& di, const MatvecArgs& a, cudaStream_t st) {
   const int warps = kMatvecThreads / 32;
   const int need = (a.rows + warps - 1) / warps;
   const int blocks = std::max(1, std::min(need, di.sms * per_sm));
-  kern<<<blocks, kMatvecThreads, smem, st>>>(a);
+  // A programmatic dependent launch: a decode step is tens of these launches
+  // back to back, and each may be dispatched while the previous one drains
+  // (the kernel waits for it before touching memory).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kMatvecThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    cudaGetLastError();
+    return AKILI_E_LAUNCH;
+  }
   return launch_status();
 }
 

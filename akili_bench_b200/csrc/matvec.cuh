@@ -46,6 +46,11 @@ struct MatvecArgs {
 template <bool kVec, bool kSmemX>
 __global__ void __launch_bounds__(kMatvecThreads) matvec_kernel(const __grid_constant__ MatvecArgs a) {
   const KClock kclk = kclock_begin();
+  // Launched as a programmatic dependent: wait for the previous kernel of the
+  // stream (its outputs may be this one's x or W) before any memory access,
+  // then let the next one launch while this grid runs.
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ float4 xs4[];
   float* xs = reinterpret_cast<float*>(xs4);
   const int K = a.K;

@@ -84,6 +84,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream serialization attribute may start before the previous kernel in
+// its stream has finished; griddep_wait() blocks until that kernel has
+// completed and its memory operations are visible, so a kernel that calls it
+// before touching memory keeps stream order.  griddep_launch_dependents()
+// lets the next such kernel launch once every CTA of this grid has called it
+// (or exited).  Without the attribute both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // -------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
