@@ -245,8 +245,14 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
     if (nvalid > 0) {
       const float mnew = fmaxf(st.a, max4(cm) * kLog2e);
       float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // fp16-output softmax: the hardware exp2 (ex2.approx, relative error
+      // near 2^-22) is far inside the output's rounding; otherwise exp2f.
+      constexpr bool kApprox = E == Epi::kSoftmaxPre && sizeof(OutT) == 2;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) la[j & 3] += (j < nvalid) ? exp2f(fmaf(v[j], kLog2e, -mnew)) : 0.0f;
+      for (int j = 0; j < 32; ++j) {
+        const float x = fmaf(v[j], kLog2e, -mnew);
+        la[j & 3] += (j < nvalid) ? (kApprox ? ex2_mufu(x) : exp2f(x)) : 0.0f;
+      }
       st.b = ((st.a == -INFINITY) ? 0.0f : st.b * exp2f(st.a - mnew)) + sum4(la);
       st.a = mnew;
     }
@@ -547,8 +553,9 @@ __device__ __forceinline__ void rownorm_regs(const EpiArgs& ea, const CUtensorMa
         v[4 * q + 2] = ((y[2] - s0) * s1) * g.z + be.z;
         v[4 * q + 3] = ((y[3] - s0) * s1) * g.w + be.w;
       } else {
+        // fp16 output: the hardware exp2 suffices (see epi_chunk)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[4 * q + e] = exp2f(fmaf(y[e], kLog2e, -s0)) * s1;
+        for (int e = 0; e < 4; ++e) v[4 * q + e] = ex2_mufu(fmaf(y[e], kLog2e, -s0)) * s1;
       }
     }
     uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
