@@ -161,7 +161,10 @@ __device__ __forceinline__ float col_of(float lane_val, int j) { return __shfl_s
 
 // One 32-column chunk of the epilogue: b0 / b1 are this lane's values of
 // vec0 / vec1 for the chunk (lane_vec), column j is col_of(b0, j).
-template <Epi E, typename OutT>
+// kFastExp: the clamp's log-sum-exp statistics take the hardware exp2
+// (ex2.approx, relative error near 2^-22); the kernels set it for fp16
+// operands, not for the fp32 (split) mode, which keeps exp2f.
+template <Epi E, typename OutT, bool kFastExp = false>
 __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvalid, float (&v)[32],
                                           const float (&u)[32], RowState& st, float b0 = 0.0f, float b1 = 0.0f) {
   (void)col0;
@@ -245,9 +248,10 @@ __device__ __forceinline__ void epi_chunk(const EpiArgs& ea, int col0, int nvali
     if (nvalid > 0) {
       const float mnew = fmaxf(st.a, max4(cm) * kLog2e);
       float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      // fp16-output softmax: the hardware exp2 (ex2.approx, relative error
-      // near 2^-22) is far inside the output's rounding; otherwise exp2f.
-      constexpr bool kApprox = E == Epi::kSoftmaxPre && sizeof(OutT) == 2;
+      // fp16-output softmax and the fp16-operand clamp: the hardware exp2
+      // (ex2.approx, relative error near 2^-22) is far inside what the
+      // outputs resolve; otherwise exp2f.
+      constexpr bool kApprox = (E == Epi::kSoftmaxPre && sizeof(OutT) == 2) || (E == Epi::kLseClamp && kFastExp);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float x = fmaf(v[j], kLog2e, -mnew);
@@ -302,7 +306,7 @@ __device__ __forceinline__ void stage_row(uint8_t* stage, int r, const float (&v
 // buffers) for TMA stores issued by `issuer`, or reduced to the row's
 // statistics, which are returned.  `bar_id` is the named barrier of these
 // 128 threads.
-template <Epi E, typename OutT>
+template <Epi E, typename OutT, bool kFastExp = false>
 __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUtensorMap* tmC, uint32_t tbase, int n0,
                                                   int mrow0, int r, int c_begin, int c_end, uint8_t* staging,
                                                   uint32_t bar_id, bool issuer, int& chunk_ctr) {
@@ -334,7 +338,8 @@ __device__ __forceinline__ RowState epilogue_half(const EpiArgs& ea, const CUten
     }
     const int col0 = n0 + c * 32;
     const int nvalid = min(32, ea.N - col0);
-    epi_chunk<E, OutT>(ea, col0, nvalid, v, u, st, lane_pick(lv0, c - c_begin), lane_pick(lv1, c - c_begin));
+    epi_chunk<E, OutT, kFastExp>(ea, col0, nvalid, v, u, st, lane_pick(lv0, c - c_begin),
+                                 lane_pick(lv1, c - c_begin));
     if constexpr (kStore) {
       uint8_t* stg = staging + (chunk_ctr & 1) * kStageOut;
       if (issuer) bulk_wait_read<1>();
@@ -783,8 +788,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       RowState st[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h)
-        st[h] = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, m_blk * kBM, r, h * HC, min((h + 1) * HC, nchunks),
-                                       staging, 1, ep_tid == 0, chunk_ctr);
+        st[h] = epilogue_half<E, OutT, !kSplit>(ea, &tmC, tbase, n0, m_blk * kBM, r, h * HC,
+                                                min((h + 1) * HC, nchunks), staging, 1, ep_tid == 0, chunk_ctr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -1134,7 +1139,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int n0 = n_blk * BN;
         const int mrow0 = m_blk * 2 * kBM + static_cast<int>(rank) * kBM;
         const int nchunks = min(BN / 32, (N - n0 + 31) / 32);
-        const RowState st = epilogue_half<E, OutT>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
+        const RowState st = epilogue_half<E, OutT, !kSplit>(ea, &tmC, tbase, n0, mrow0, r, grp * HC,
                                                    min((grp + 1) * HC, nchunks), gstaging, bar_id, gtid == 0,
                                                    chunk_ctr);
         // This warp has read its TMEM rows: release the accumulator to the even CTA's MMA.
