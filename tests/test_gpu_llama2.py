@@ -126,3 +126,57 @@ def test_reference_llama_generates_the_cpu_text_on_b200(tmp_path):
     assert cpu.startswith("the cat")
     assert run(os.path.join(REF, "b200", "llama"), 1) == cpu
     assert run(os.path.join(REF, "b200", "llama_vxmath"), 1) == cpu
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_dependent_matvec_chain_sees_each_previous_product(oracle, graph):
+    """The matrix-vector kernels launch as programmatic dependents: each may be
+    dispatched before the previous kernel of its stream ends, and must wait
+    for it before reading its input.  A chain y_{i+1} = W_i . y_i of eight
+    launches on one stream (a long one first, then short ones, so that a
+    launch that did not wait would read a stale or half-written y_i), run
+    directly and replayed from a CUDA graph; each step is checked against the
+    oracle applied to the previous step's device output."""
+    rng = np.random.default_rng(41)
+    dims = [4096, 1024, 1024, 512, 1024, 256, 1024, 512, 768]
+    ws = [(rng.standard_normal((dims[i + 1], dims[i])) * dims[i] ** -0.5).astype(np.float32)
+          for i in range(len(dims) - 1)]
+    big = (rng.standard_normal((8192, dims[0])) * dims[0] ** -0.5).astype(np.float32)
+    x = rng.standard_normal(dims[0]).astype(np.float32)
+    dw = [torch.from_numpy(w).cuda() for w in ws]
+    dbig = torch.from_numpy(big).cuda()
+    dx = torch.from_numpy(x).cuda()
+    ys = [torch.empty(d, device="cuda", dtype=torch.float32) for d in dims[1:]]
+    scratch = torch.empty(big.shape[0], device="cuda", dtype=torch.float32)
+
+    def chain(stream):
+        ops.llama2_matmul(dbig, dx, out=scratch, stream=stream)  # a long launch ahead of the chain
+        prev = dx
+        for w, y in zip(dw, ys):
+            ops.llama2_matmul(w, prev, out=y, stream=stream)
+            prev = y
+
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    if graph:
+        with torch.cuda.stream(stream):
+            chain(stream)  # warm-up outside the capture
+        torch.cuda.synchronize()
+        for y in ys:
+            y.fill_(float("nan"))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            chain(stream)
+        g.replay()
+    else:
+        with torch.cuda.stream(stream):
+            chain(stream)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    prev = x
+    for i, (w, y) in enumerate(zip(ws, ys)):
+        got = y.cpu().numpy()
+        ref = oracle.llama2_matmul(w, prev.reshape(-1, 1), w.shape[0], 1, w.shape[1])[:, 0]
+        err = np.abs(got.astype(np.float64) - ref)
+        assert (err <= bound(w, prev.reshape(-1, 1), w.shape[1])[:, 0]).all(), f"step {i}: max err {err.max():.3e}"
+        prev = got
